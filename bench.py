@@ -1,0 +1,426 @@
+"""Benchmark of the KV-cache decode path (append + GQA decode attention).
+
+Default workload ("cfg4"): per GPU, 64 independent
+sequences with context lengths U[1k, 32k], 32 layers, 32 query / 8 KV heads,
+head_dim 128, bf16 caches.  One step = for every layer, one batched decode call
+(append of each sequence's new K/V row + split-sequence attention of its new
+query over the whole cache).  The metric is decode tokens/s (one token per
+sequence per step, all layers) and achieved HBM GB/s of the attention launches.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload cfg4|cfg5|cfg2]
+
+N > 1 runs under torchrun, one rank per GPU.  cfg4 shards by sequences (each
+rank owns its own 64; weak scaling, no collective on the data path).  cfg5
+(one 131072-token sequence) shards KV-head groups and all-gathers the per-head
+outputs with NCCL after every layer (strong scaling).
+
+Inputs are synthetic (seeded normal values; the reference names no dataset)
+and larger than L2 (126 MB) between timed iterations.  `--impl reference`
+times the reference algorithm's CPU path (the engine-order restatement of
+src/tgai_engine.c:3943-4011 in oracle/, all host threads) on a bounded sample
+of the same workload.
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "tgai-go_b200"))
+
+HBM_FALLBACK_GBS = 6650.0
+METRIC = "decode attn+KV-append tokens/s & HBM GB/s vs ~8 TB/s peak at 1/2/4/8 B200"
+
+WORKLOADS = {
+    # name: sequences per rank, layers, q heads, kv heads, head_dim, length range
+    "cfg4": dict(n_seq=64, layers=32, nh=32, nkv=8, hd=128, lmin=1024, lmax=32768,
+                 desc="configs[3]: 64 seqs/GPU, L~U[1k,32k], 32 layers, 32q/8kv, hd128, bf16"),
+    "cfg5": dict(n_seq=1, layers=32, nh=32, nkv=8, hd=128, lmin=131072, lmax=131072,
+                 desc="configs[4]: 1 seq, L=131072, 32 layers, 32q/8kv, hd128, bf16"),
+    "cfg2": dict(n_seq=1, layers=24, nh=16, nkv=4, hd=128, lmin=4096, lmax=4096,
+                 desc="configs[1] at its largest context: 1 seq, L=4096, 24 layers, 16q/4kv, hd128, bf16"),
+}
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def lengths_for(wl, seed, rank):
+    rng = np.random.default_rng([seed, rank, 4])
+    return rng.integers(wl["lmin"], wl["lmax"] + 1, wl["n_seq"]).astype(np.int64)
+
+
+def attn_bytes(lens_after, nh, nkv, hd, b=2):
+    """Algorithmic bytes of one layer's decode call: K and V read once per KV
+    head over L positions, the new row's append write, q read and out write."""
+    L = np.asarray(lens_after, np.float64)
+    return float((2 * L * nkv * hd * b + 2 * nkv * hd * b + nh * hd * 4 * 2).sum())
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world and world > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    return world, rank, local
+
+
+def make_cpu_sample(wl, lens, seed, max_bytes=1.5e9):
+    """Shortest-first whole sequences of one layer as fp32 caches (the
+    reference has no bf16 cache), within max_bytes of host memory."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    nh, nkv, hd = wl["nh"], wl["nkv"], wl["hd"]
+    items, used = [], 0
+    for idx in np.argsort(lens):
+        L = int(lens[idx])
+        b = 2 * L * nkv * hd * 4
+        if items and used + b > max_bytes:
+            break
+        items.append((O.normal(2 * L * nkv * hd, seed, int(idx), 9),
+                      O.normal(nh * hd, seed, int(idx), 10), L))
+        used += b
+    return items
+
+
+def time_cpu_sample(wl, lens, items, threads, budget_s):
+    """Reference-order CPU decode (oracle/: the engine loop of
+    src/tgai_engine.c:3943-4011, one query per sequence) over the sample until
+    budget_s of CPU work; extrapolated by positions x layers to the full step.
+    Returns (tokens/s, description)."""
+    import oracle as O
+    nh, nkv, hd = wl["nh"], wl["nkv"], wl["hd"]
+    done, spent, n = 0, 0.0, 0
+    while spent < budget_s:
+        kvc, q, L = items[n % len(items)]
+        t0 = time.perf_counter()
+        O.decode_batch([kvc], [q], [L], nh, nkv, hd, threads=threads)
+        spent += time.perf_counter() - t0
+        done += L
+        n += 1
+    step_s = spent * float(np.sum(lens)) * wl["layers"] / done
+    desc = (f"{n} single-layer sequence decodes (L={items[0][2]}..{items[-1][2]}, the shortest "
+            f"{len(items)} of {len(lens)}), fp32 cache, {spent:.1f}s of CPU work, scaled by "
+            f"positions x {wl['layers']} layers to the full step")
+    return wl["n_seq"] / step_s, desc
+
+
+def run_reference(args):
+    """--impl reference: the reference algorithm's CPU path, all host threads."""
+    world, rank, _ = dist_setup(args)
+    if rank != 0:
+        return
+    wl = WORKLOADS[args.workload]
+    lens = lengths_for(wl, args.seed, 0)
+    threads = os.cpu_count() or 1
+    items = make_cpu_sample(wl, lens, args.seed)
+    budget = max(0.5, args.cpu_total_s / max(1, args.steps + args.warmup))
+    vals = []
+    for i in range(args.warmup + args.steps):
+        tok, desc = time_cpu_sample(wl, lens, items, threads, budget)
+        if i >= args.warmup:
+            vals.append(tok)
+    v = float(np.median(vals))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * wl["n_seq"] / float(np.median(vals)),
+        "higher_is_better": True, "scaling": "weak" if args.workload == "cfg4" else "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "desc": wl["desc"]},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import tgkv
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    lib = tgkv.load()
+    tgkv.check(lib.tg_cuda_kv_set_device(local), lib, "set_device")
+    tgkv.check(lib.tg_be_select(b"cuda"), lib, "tg_be_select")
+    wl = WORKLOADS[args.workload]
+    heads_sharded = args.workload != "cfg4" and world > 1
+    if heads_sharded and wl["nkv"] % world:
+        raise SystemExit(f"{wl['nkv']} KV heads do not split over {world} GPUs")
+    nkv = wl["nkv"] // world if heads_sharded else wl["nkv"]
+    nh = wl["nh"] // world if heads_sharded else wl["nh"]
+    hd, layers, n_seq = wl["hd"], wl["layers"], wl["n_seq"]
+    kvd = nkv * hd
+    lens0 = lengths_for(wl, args.seed, 0 if heads_sharded else rank)
+    e2e_steps = 0 if args.no_e2e else args.steps
+    e2e_warm = 0 if args.no_e2e else args.warmup
+    total_steps = args.warmup + args.steps + e2e_warm + e2e_steps + 1
+    stream = torch.cuda.current_stream()
+    sh = tgkv.stream_handle(stream)
+
+    # ---- caches: one per (layer, sequence), filled by the append kernel
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed * 1000 + rank)
+    caches = [[None] * n_seq for _ in range(layers)]
+    t_fill = time.time()
+    for i in range(n_seq):
+        L = int(lens0[i])
+        for l in range(layers):
+            c = lib.tg_kv_create_ex(L + total_steps, nkv, hd, tgkv.TG_KV_BF16)
+            tgkv.check(c, lib, "tg_kv_create_ex")
+            k = torch.randn(L, kvd, device="cuda", generator=gen)
+            v = torch.randn(L, kvd, device="cuda", generator=gen)
+            tgkv.check(lib.tg_kv_append_dev(c, k.data_ptr(), v.data_ptr(), L, sh), lib,
+                       "append_dev")
+            caches[l][i] = c
+    torch.cuda.synchronize()
+    t_fill = time.time() - t_fill
+    plans = []
+    for l in range(layers):
+        arr = (C.c_void_p * n_seq)(*caches[l])
+        b = lib.tg_kv_batch_create(arr, n_seq, nh)
+        tgkv.check(b, lib, "tg_kv_batch_create")
+        plans.append(b)
+    q = [torch.randn(n_seq, nh, hd, device="cuda", generator=gen) for _ in range(layers)]
+    kn = [torch.randn(n_seq, kvd, device="cuda", generator=gen) for _ in range(layers)]
+    vn = [torch.randn(n_seq, kvd, device="cuda", generator=gen) for _ in range(layers)]
+    out = [torch.empty(n_seq, nh, hd, device="cuda") for _ in range(layers)]
+    gathered = ([torch.empty(world, n_seq, nh, hd, device="cuda") for _ in range(layers)]
+                if heads_sharded else None)
+    launches = [0]
+
+    def step(events=None):
+        for l in range(layers):
+            if events is not None:
+                events[l][0].record(stream)
+            ok = lib.tg_kv_batch_decode(plans[l], q[l].data_ptr(), kn[l].data_ptr(),
+                                        vn[l].data_ptr(), out[l].data_ptr(), sh)
+            if not ok:
+                raise RuntimeError(lib.tg_kv_last_error().decode())
+            launches[0] += lib.tg_kv_batch_last_launches(plans[l])
+            if events is not None:
+                events[l][1].record(stream)
+            if heads_sharded:
+                dist.all_gather_into_tensor(gathered[l], out[l])
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+          for _ in range(layers * args.steps)]
+    lens_step = [np.array([lib.tg_kv_len(caches[0][i]) for i in range(n_seq)]) + 1]
+    launches[0] = 0
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for s_ in range(args.steps):
+        step(ev[s_ * layers:(s_ + 1) * layers])
+    t1.record(stream)
+    barrier()
+    clock = clocks.stop()
+    timed_launches = launches[0]
+    ms = t0.elapsed_time(t1) / args.steps
+    ms_max = max_over_ranks(ms)
+    call_ms = [a.elapsed_time(b) for a, b in ev]
+    algo = sum(attn_bytes(lens_step[0] + s_, nh, nkv, hd) for s_ in range(args.steps)) * layers
+    kernel_gbs = algo / (sum(call_ms) / 1000.0) / 1e9
+    per_launch_bytes = algo / (args.steps * layers)
+
+    # ---- end to end: host buffers, copies inside the timed region
+    e2e = None
+    if e2e_steps:
+        qh = [torch.randn(n_seq, nh, hd, generator=torch.Generator().manual_seed(l)).pin_memory()
+              for l in range(layers)]
+        kh = [torch.randn(n_seq, kvd).pin_memory() for _ in range(layers)]
+        vh = [torch.randn(n_seq, kvd).pin_memory() for _ in range(layers)]
+        oh = [torch.empty(n_seq, nh, hd).pin_memory() for _ in range(layers)]
+
+        def step_host():
+            for l in range(layers):
+                ok = lib.tg_kv_batch_decode_host(plans[l], qh[l].data_ptr(), kh[l].data_ptr(),
+                                                 vh[l].data_ptr(), oh[l].data_ptr(), sh)
+                if not ok:
+                    raise RuntimeError(lib.tg_kv_last_error().decode())
+                if heads_sharded:
+                    dist.all_gather_into_tensor(gathered[l], out[l])
+
+        for _ in range(e2e_warm):
+            step_host()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            step_host()
+        e1.record(stream)
+        barrier()
+        e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+        h2d = layers * (qh[0].numel() + 2 * kh[0].numel()) * 4
+        d2h = layers * oh[0].numel() * 4
+        tokens = n_seq * (world if not heads_sharded else 1)
+        e2e = {"value": tokens / (e_ms / 1000.0), "unit": "tokens/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e_ms}
+
+    err = lib.tg_cuda_kv_device_error()
+    for b in plans:
+        lib.tg_kv_batch_destroy(b)
+    for row in caches:
+        for c in row:
+            lib.tg_kv_destroy(c)
+    if err:
+        raise RuntimeError(f"kernel bounded wait expired (code {err})")
+
+    tokens = n_seq * (world if not heads_sharded else 1)
+    value = tokens / (ms_max / 1000.0)
+    peak, peak_kind = measured_peak()
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "attention_dram_ratio.json")
+    if os.path.exists(tp):
+        try:
+            traffic = per_launch_bytes * float(json.load(open(tp))[args.workload])
+        except Exception:
+            traffic = None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        items = make_cpu_sample(wl, lens0, args.seed)
+        tok, desc = time_cpu_sample(wl, lens0, items, 1, args.cpu_baseline_s)
+        cpu = {"value": tok, "unit": "tokens/s", "cores": 1, "kind": "port", "sample": desc}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+            "higher_is_better": True, "scaling": "strong" if heads_sharded else "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": args.workload, "desc": wl["desc"],
+                       "sequences_per_gpu": n_seq if not heads_sharded else n_seq,
+                       "kv_heads_per_gpu": nkv, "context_mean": float(lens0.mean()),
+                       "l2": "inputs larger than L2 (K/V read per step >> 126 MB)",
+                       "parallelism": (f"kv-head groups x{world} + NCCL all-gather"
+                                       if heads_sharded else f"sequences x{world}, no collective"),
+                       "fill_s": round(t_fill, 1)},
+            "hbm_gbs": algo / (ms * args.steps / 1000.0) / 1e9 * (1 if heads_sharded else 1),
+            "roofline": {"bound": "hbm", "achieved": kernel_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": kernel_gbs / peak, "traffic": traffic,
+                         "peak_source": peak_kind,
+                         "kernel": "tg_kv_batch_decode per layer (append + split-sequence "
+                                   "attention launches), CUDA events on the launch stream",
+                         "algorithmic_bytes_per_launch": per_launch_bytes},
+            "gpu_launches": timed_launches,
+            "clocks": clock,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
+    ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-baseline-s", type=float, default=12.0)
+    ap.add_argument("--cpu-total-s", type=float, default=120.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,109 @@
+/* tgai_cuda_bridge.h -- the thin C-ABI layer between TGAI GO's host C code and
+ * the CUDA kernels of the KV-cache path.
+ *
+ * Replaces the role of cuda/tgai_cuda_bridge.{h,c} (cuda/tgai_cuda_bridge.h:
+ * 31-60) for this path: host C code (the KV-cache API, the backend table, the
+ * GPU dispatch router) reaches CUDA only through these functions.  Plain C
+ * types only; device memory is passed as addresses, streams as void*
+ * (cudaStream_t, NULL = legacy default stream).
+ *
+ * Return convention (as the reference bridge): int 1 = done, 0 = failed with
+ * the reason in tg_cuda_kv_last_error().  No function falls back to the CPU.
+ *
+ * The whole-forward entry points of the reference bridge (tg_engine_cuda_init
+ * / forward / reset_slot / free_slot / shutdown, cuda/tgai_cuda_bridge.h:
+ * 31-53) need the model's projections and FFN and are not part of this path.
+ */
+#ifndef TGAI_CUDA_BRIDGE_H
+#define TGAI_CUDA_BRIDGE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- device and memory -------------------------------------------------- */
+int         tg_cuda_kv_init(void);              /* idempotent; 1 = a CUDA device is usable */
+/* Make `device` this thread's device for the library (one process per GPU
+ * calls this before anything else; default: the runtime's current device). */
+int         tg_cuda_kv_set_device(int device);
+void        tg_cuda_kv_shutdown(void);
+int         tg_cuda_kv_ready(void);
+const char* tg_cuda_kv_last_error(void);        /* thread-local */
+const char* tg_cuda_kv_device_name(void);
+uint64_t    tg_cuda_kv_device_mem(void);
+int         tg_cuda_kv_sm_count(void);
+
+void* tg_cuda_kv_malloc(size_t bytes);          /* zero-filled; NULL on failure */
+void  tg_cuda_kv_free(void* p);
+int   tg_cuda_kv_h2d(void* dst, const void* src, size_t bytes, void* stream);
+int   tg_cuda_kv_d2h(void* dst, const void* src, size_t bytes, void* stream);
+int   tg_cuda_kv_memset(void* dst, int value, size_t bytes, void* stream);
+/* The h2d/d2h/memset calls block when stream is NULL; otherwise they are
+ * queued on stream and tg_cuda_kv_sync(stream) waits for them. */
+int   tg_cuda_kv_sync(void* stream);
+
+/* Read and clear the device error word set by kernels whose bounded waits
+ * expired (0 = none).  Blocks on the whole device. */
+int   tg_cuda_kv_device_error(void);
+
+/* Testing hook: make the next `n` tg_cuda_kv_malloc calls fail (0 = off).
+ * Also set at start-up from TGKV_FAIL_ALLOC. */
+void  tg_cuda_kv_inject_alloc_failures(int n);
+
+/* ---- kernels ------------------------------------------------------------ */
+
+/* Cache descriptor as the kernels read it (same layout as TGKvCacheDesc). */
+typedef struct {
+    uint64_t base;
+    uint32_t max_seq;
+    uint32_t pad;
+} TGCudaCacheDesc;
+
+/* Append rows (fp32 device sources [n_rows][kv_dim]) into one cache starting at
+ * row `row0`, storing dtype (0 = fp32, 1 = bf16 round-to-nearest-even). */
+int tg_cuda_kv_append(int dtype, TGCudaCacheDesc cache, uint32_t kv_dim, uint32_t row0,
+                      const float* k, const float* v, uint32_t n_rows, void* stream);
+
+/* Append one row per item i into cache table[i] at position pos[i] (host
+ * array).  k, v: fp32 device [n_items][kv_dim]. */
+int tg_cuda_kv_append_batch(int dtype, const TGCudaCacheDesc* table_dev, uint32_t kv_dim,
+                            const uint32_t* pos, uint32_t n_items,
+                            const float* k, const float* v, void* stream);
+
+/* One attention call: item i attends positions [0, n_pos[i]) of its cache
+ * with query row i of q (fp32 [n_items][n_heads][head_dim]) into row i of out.
+ * Items use table_dev[i] when table_dev is set, else `cache`. */
+typedef struct {
+    int      dtype;
+    uint32_t n_heads, n_kv_heads, head_dim;
+    TGCudaCacheDesc        cache;
+    const TGCudaCacheDesc* table_dev;
+    const float*    q;
+    float*          out;
+    const uint32_t* n_pos;          /* host array [n_items], each >= 1 */
+    uint32_t        n_items;
+    float           scale;          /* softmax scale (1/sqrt(head_dim)) */
+    void*           scratch;        /* device, >= tg_cuda_kv_attn_scratch_bytes() */
+    uint32_t*       counters;       /* device, zeroed, >= tg_cuda_kv_attn_counters() */
+} TGCudaAttnCall;
+
+int      tg_cuda_kv_attn_supported(int dtype, uint32_t head_dim);
+uint64_t tg_cuda_kv_attn_scratch_bytes(const TGCudaAttnCall* c);
+uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c);
+/* Launches made by the last tg_cuda_kv_attention on this thread. */
+uint32_t tg_cuda_kv_attn_last_launches(void);
+int      tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream);
+
+/* RoPE + KV write, shaders/rope.comp semantics (see TGBackend.rope). */
+int tg_cuda_kv_rope_append(int dtype, const float* qkv, const float* cs, const float* sn,
+                           void* kvc, float* qout, uint32_t n_tokens, uint32_t n_heads,
+                           uint32_t n_kv_heads, uint32_t head_dim, uint32_t start_pos,
+                           uint32_t max_seq, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TGAI_CUDA_BRIDGE_H */

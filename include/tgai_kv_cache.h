@@ -1,0 +1,139 @@
+/* tgai_kv_cache.h -- per-layer KV cache on a B200, behind TGAI GO's KV-cache API.
+ *
+ * The first block keeps the reference interface of src/tgai_kv_cache.h:41-76
+ * (same names, argument meaning, return values and error behaviour) so that
+ * existing callers link unchanged.  The cache layout is the reference's
+ * (src/tgai_kv_cache.h:15-21): one device buffer [2][max_seq][kv_dim],
+ * kv_dim = n_kv_heads * head_dim, the K half first and the V half at element
+ * offset max_seq * kv_dim, positions [0, len) valid.
+ *
+ * Everything after "Additive extensions" is new API; the reference has no
+ * counterpart unless one is cited.
+ *
+ * Threading: a cache must not be used from two threads at once (as in the
+ * reference).  tg_kv_last_error() is thread-local here (the reference keeps
+ * one process-global buffer, src/tgai_kv_cache.c:22-26).
+ */
+#ifndef TGAI_KV_CACHE_H
+#define TGAI_KV_CACHE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct TGKvCache TGKvCache;
+
+/* ---- Reference interface (src/tgai_kv_cache.h:41-76) ------------------- */
+
+/* Replaces tg_kv_create (src/tgai_kv_cache.h:41, .c:28-69).  fp32 storage.
+ * Uses the selected backend (tg_be_select("cuda") first); NULL on failure with
+ * the reason in tg_kv_last_error().  The buffer is zero-filled once. */
+TGKvCache* tg_kv_create(uint32_t max_seq, uint32_t n_kv_heads, uint32_t head_dim);
+
+/* Replaces tg_kv_destroy (src/tgai_kv_cache.h:43, .c:71-76). */
+void tg_kv_destroy(TGKvCache* c);
+
+/* Replaces tg_kv_reset (src/tgai_kv_cache.h:46, .c:78-83): len = 0; memory kept. */
+void tg_kv_reset(TGKvCache* c);
+
+/* Replaces tg_kv_len / tg_kv_capacity (src/tgai_kv_cache.h:49-52). */
+uint32_t tg_kv_len(const TGKvCache* c);
+uint32_t tg_kv_capacity(const TGKvCache* c);
+
+/* Replaces tg_kv_device_handle (src/tgai_kv_cache.h:56): here the raw device
+ * address of the [2][max_seq][kv_dim] buffer (what TGBackend.attention takes
+ * as `kvc`). */
+void* tg_kv_device_handle(TGKvCache* c);
+
+/* Replaces tg_kv_host_ptr (src/tgai_kv_cache.h:60): always NULL, the cache
+ * lives in HBM and is not host-mappable. */
+float* tg_kv_host_ptr(TGKvCache* c);
+
+/* Replaces tg_kv_append (src/tgai_kv_cache.h:67-70, .c:90-110): append
+ * n_tokens rows of K and V from HOST memory ([n_tokens][kv_dim] fp32 each).
+ * Returns 1, or 0 with "capacity exceeded" when len + n_tokens > max_seq, or
+ * on NULL arguments.  n_tokens == 0 returns 1.  Blocks until the rows are in
+ * the cache; bf16 caches store round-to-nearest-even. */
+int tg_kv_append(TGKvCache* c, const float* k_src, const float* v_src,
+                 uint32_t n_tokens);
+
+/* Replaces tg_kv_advance (src/tgai_kv_cache.h:73, .c:112-116): len += n,
+ * clamped to capacity. */
+void tg_kv_advance(TGKvCache* c, uint32_t n_tokens);
+
+/* Replaces tg_kv_last_error (src/tgai_kv_cache.h:76). */
+const char* tg_kv_last_error(void);
+
+/* ---- Additive extensions ------------------------------------------------ */
+
+/* Storage element types. */
+#define TG_KV_F32  0
+#define TG_KV_BF16 1
+
+/* tg_kv_create with a storage type (TG_KV_F32 or TG_KV_BF16). */
+TGKvCache* tg_kv_create_ex(uint32_t max_seq, uint32_t n_kv_heads, uint32_t head_dim,
+                           int dtype);
+
+int      tg_kv_dtype(const TGKvCache* c);
+uint32_t tg_kv_n_kv_heads(const TGKvCache* c);
+uint32_t tg_kv_head_dim(const TGKvCache* c);
+
+/* Truncate to n positions (n <= len), the LCP prefix-reuse step of
+ * python/tgai_go/_session.py:137-163.  Same effect as tg_kv_reset followed by
+ * tg_kv_advance(n); rows [0, n) are untouched.  /clear is n = 0.
+ * Returns 0 with an error if n > len. */
+int tg_kv_truncate(TGKvCache* c, uint32_t n);
+
+/* Append n_tokens rows from DEVICE memory (fp32 [n_tokens][kv_dim] each),
+ * asynchronously on `stream` (a cudaStream_t; NULL = legacy default stream).
+ * Same capacity rule as tg_kv_append; len advances at once on the host. */
+int tg_kv_append_dev(TGKvCache* c, const float* k_dev, const float* v_dev,
+                     uint32_t n_tokens, void* stream);
+
+/* Causal attention of the last n_q cached positions' queries over the cache,
+ * asynchronously on `stream`.  q_dev, out_dev: fp32 [n_q][n_heads][head_dim]
+ * in device memory.  Query t sits at position p = len - n_q + t and sees
+ * positions [0, p]; q head h reads KV head h * n_kv_heads / n_heads
+ * (src/tgai_engine.c:3951).  Scores are scaled by 1/sqrt(head_dim).
+ * Requires n_heads % n_kv_heads == 0 and 1 <= n_q <= len. */
+int tg_kv_attention(TGKvCache* c, const float* q_dev, float* out_dev,
+                    uint32_t n_heads, uint32_t n_q, void* stream);
+
+/* Copy the whole [2][max_seq][kv_dim] buffer (raw storage bytes) to host
+ * memory `dst` of tg_kv_bytes(c) bytes.  Blocks. */
+uint64_t tg_kv_bytes(const TGKvCache* c);
+int      tg_kv_download(const TGKvCache* c, void* dst);
+
+/* ---- Batched decode over many caches (one layer of many sequences) ------- */
+
+typedef struct TGKvBatch TGKvBatch;
+
+/* A plan over n caches of equal n_kv_heads, head_dim and dtype (up to 1024
+ * per plan), for n_heads query heads.  The plan owns its split-sequence
+ * scratch and device descriptor table.  NULL on failure. */
+TGKvBatch* tg_kv_batch_create(TGKvCache* const* caches, uint32_t n, uint32_t n_heads);
+void       tg_kv_batch_destroy(TGKvBatch* b);
+
+/* One decode step for every cache i of the plan: append row i of k_new/v_new
+ * (fp32 [n][kv_dim], device) at position len_i, then attend query row i of q
+ * (fp32 [n][n_heads][head_dim], device) over positions [0, len_i] into row i
+ * of out (same shape).  Each cache's len grows by one.  Async on `stream`.
+ * Returns 0 (nothing launched) if any cache is full. */
+int tg_kv_batch_decode(TGKvBatch* b, const float* q, const float* k_new,
+                       const float* v_new, float* out, void* stream);
+
+/* The same step from HOST buffers: copies q/k_new/v_new in (pinned host memory
+ * gives async copies), runs the step and copies out back, all on `stream`.
+ * The caller synchronises `stream` before reading out_host. */
+int tg_kv_batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_host,
+                            const float* v_host, float* out_host, void* stream);
+
+/* Number of kernel launches the last tg_kv_batch_decode made (for reports). */
+uint32_t tg_kv_batch_last_launches(const TGKvBatch* b);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TGAI_KV_CACHE_H */

@@ -1,0 +1,98 @@
+"""Shared fixtures: paths, the C-ABI library, device buffers through the C-ABI.
+
+GPU tests are marked `gpu`; everything else runs on a CPU-only machine.
+"""
+import ctypes as C
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+PKG = os.path.join(ROOT, "tgai-go_b200")
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+for p in (PKG, os.path.join(ROOT, "oracle")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200)")
+
+
+@pytest.fixture(scope="session")
+def lib():
+    import tgkv
+    return tgkv.load()
+
+
+@pytest.fixture(scope="session")
+def cuda(lib):
+    """The library with the cuda backend selected (GPU tests only)."""
+    if not lib.tg_be_select(b"cuda"):
+        pytest.fail("tg_be_select('cuda') failed: " + lib.tg_cuda_kv_last_error().decode())
+    return lib
+
+
+class DevBuf:
+    """Device memory from tg_cuda_kv_malloc, filled/read through the C-ABI."""
+
+    def __init__(self, lib, nbytes):
+        self.lib = lib
+        self.nbytes = int(nbytes)
+        self.ptr = lib.tg_cuda_kv_malloc(max(self.nbytes, 16))
+        assert self.ptr, lib.tg_cuda_kv_last_error().decode()
+
+    @classmethod
+    def from_array(cls, lib, a):
+        a = np.ascontiguousarray(a)
+        b = cls(lib, a.nbytes)
+        assert lib.tg_cuda_kv_h2d(b.ptr, a.ctypes.data, a.nbytes, None)
+        return b
+
+    def get(self, dtype, shape):
+        out = np.empty(shape, dtype)
+        assert out.nbytes <= self.nbytes
+        assert self.lib.tg_cuda_kv_d2h(out.ctypes.data, self.ptr, out.nbytes, None)
+        return out
+
+    def free(self):
+        if self.ptr:
+            self.lib.tg_cuda_kv_free(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+@pytest.fixture
+def devbuf(cuda):
+    made = []
+
+    def make(a=None, nbytes=None):
+        b = DevBuf.from_array(cuda, a) if a is not None else DevBuf(cuda, nbytes)
+        made.append(b)
+        return b
+
+    yield make
+    for b in made:
+        b.free()
+
+
+def rel_head_err(got, ref):
+    """Max over elements of |got-ref| / max|ref| of that (token, head) row.
+
+    Outputs are convex combinations of V rows, so single elements can sit
+    near zero; the error is measured against the magnitude of the head's
+    output vector, the scale at which a consumer (out_proj) reads it."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    hd = ref.shape[-1]
+    g = got.reshape(-1, hd)
+    r = ref.reshape(-1, hd)
+    scale = np.maximum(np.abs(r).max(axis=1, keepdims=True), 1e-30)
+    return float((np.abs(g - r) / scale).max())

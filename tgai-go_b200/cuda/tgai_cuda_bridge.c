@@ -1,0 +1,390 @@
+/* tgai_cuda_bridge.c -- thin C layer from TGAI GO host code to CUDA for the
+ * KV-cache path.  Plain C (C11); talks to the CUDA runtime and to the kernel
+ * launchers of tgkv_kernels.cu, nothing else.
+ *
+ * Host-side planning of split-sequence attention lives here: the per-item
+ * position counts, the chunk length and the CTA prefix table are computed on
+ * the host and handed to the kernel by value (tgkv_launch.h), so a launch
+ * needs no copy of its own.
+ */
+#include "tgai_cuda_bridge.h"
+#include "tgkv_launch.h"
+
+#include <cuda_runtime_api.h>
+#include <math.h>
+#include <pthread.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+static _Thread_local char t_err[256] = "cuda bridge: no error";
+static _Thread_local uint32_t t_last_launches = 0;
+
+static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
+static int g_ready = 0;
+static int g_sm_count = 0;
+static uint64_t g_mem = 0;
+static char g_name[256] = "";
+static int32_t* g_err_word = NULL;      /* device error word for bounded waits */
+static int g_fail_allocs = 0;           /* testing hook */
+
+static void set_err(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_err, sizeof(t_err), fmt, ap);
+    va_end(ap);
+}
+
+static int cuda_ok(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return 1;
+    set_err("%s: %s", what, cudaGetErrorString(e));
+    return 0;
+}
+
+const char* tg_cuda_kv_last_error(void) { return t_err; }
+
+int tg_cuda_kv_init(void) {
+    pthread_mutex_lock(&g_mu);
+    if (g_ready) { pthread_mutex_unlock(&g_mu); return 1; }
+    const char* fa = getenv("TGKV_FAIL_ALLOC");
+    if (fa && fa[0]) g_fail_allocs = atoi(fa);
+    int n = 0, dev = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n <= 0) {
+        set_err("no CUDA device: %s", e == cudaSuccess ? "count is 0" : cudaGetErrorString(e));
+        pthread_mutex_unlock(&g_mu);
+        return 0;
+    }
+    struct cudaDeviceProp prop;
+    if (!cuda_ok(cudaGetDevice(&dev), "cudaGetDevice") ||
+        !cuda_ok(cudaGetDeviceProperties(&prop, dev), "cudaGetDeviceProperties")) {
+        pthread_mutex_unlock(&g_mu);
+        return 0;
+    }
+    if (prop.major < 10) {
+        set_err("device %s is sm_%d%d; this build targets sm_100a", prop.name, prop.major,
+                prop.minor);
+        pthread_mutex_unlock(&g_mu);
+        return 0;
+    }
+    snprintf(g_name, sizeof(g_name), "%s", prop.name);
+    g_sm_count = prop.multiProcessorCount;
+    g_mem = (uint64_t)prop.totalGlobalMem;
+    if (!cuda_ok(cudaMalloc((void**)&g_err_word, 256), "cudaMalloc(error word)") ||
+        !cuda_ok(cudaMemset(g_err_word, 0, 256), "cudaMemset(error word)")) {
+        pthread_mutex_unlock(&g_mu);
+        return 0;
+    }
+    g_ready = 1;
+    pthread_mutex_unlock(&g_mu);
+    return 1;
+}
+
+int tg_cuda_kv_set_device(int device) {
+    if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice")) return 0;
+    pthread_mutex_lock(&g_mu);
+    const int was_ready = g_ready;
+    pthread_mutex_unlock(&g_mu);
+    if (was_ready) {                 /* re-read properties for the new device */
+        tg_cuda_kv_shutdown();
+        return tg_cuda_kv_init();
+    }
+    return 1;
+}
+
+void tg_cuda_kv_shutdown(void) {
+    pthread_mutex_lock(&g_mu);
+    if (g_err_word) cudaFree(g_err_word);
+    g_err_word = NULL;
+    g_ready = 0;
+    pthread_mutex_unlock(&g_mu);
+}
+
+int tg_cuda_kv_ready(void) { return g_ready; }
+const char* tg_cuda_kv_device_name(void) { return g_name; }
+uint64_t tg_cuda_kv_device_mem(void) { return g_mem; }
+int tg_cuda_kv_sm_count(void) { return g_sm_count; }
+
+void tg_cuda_kv_inject_alloc_failures(int n) {
+    pthread_mutex_lock(&g_mu);
+    g_fail_allocs = n;
+    pthread_mutex_unlock(&g_mu);
+}
+
+void* tg_cuda_kv_malloc(size_t bytes) {
+    if (!g_ready && !tg_cuda_kv_init()) return NULL;
+    pthread_mutex_lock(&g_mu);
+    if (g_fail_allocs > 0) {
+        g_fail_allocs--;
+        pthread_mutex_unlock(&g_mu);
+        set_err("cudaMalloc(%zu): injected failure (TGKV_FAIL_ALLOC)", bytes);
+        return NULL;
+    }
+    pthread_mutex_unlock(&g_mu);
+    void* p = NULL;
+    if (!cuda_ok(cudaMalloc(&p, bytes ? bytes : 1), "cudaMalloc")) return NULL;
+    if (!cuda_ok(cudaMemset(p, 0, bytes), "cudaMemset")) {
+        cudaFree(p);
+        return NULL;
+    }
+    return p;
+}
+
+void tg_cuda_kv_free(void* p) {
+    if (p) cudaFree(p);
+}
+
+int tg_cuda_kv_h2d(void* dst, const void* src, size_t bytes, void* stream) {
+    if (!bytes) return 1;
+    if (!stream) return cuda_ok(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice), "h2d");
+    return cuda_ok(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, (cudaStream_t)stream),
+                   "h2d async");
+}
+
+int tg_cuda_kv_d2h(void* dst, const void* src, size_t bytes, void* stream) {
+    if (!bytes) return 1;
+    if (!stream) return cuda_ok(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost), "d2h");
+    return cuda_ok(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, (cudaStream_t)stream),
+                   "d2h async");
+}
+
+int tg_cuda_kv_memset(void* dst, int value, size_t bytes, void* stream) {
+    if (!bytes) return 1;
+    if (!stream) return cuda_ok(cudaMemset(dst, value, bytes), "memset");
+    return cuda_ok(cudaMemsetAsync(dst, value, bytes, (cudaStream_t)stream), "memset async");
+}
+
+int tg_cuda_kv_sync(void* stream) {
+    if (!stream) return cuda_ok(cudaDeviceSynchronize(), "device sync");
+    return cuda_ok(cudaStreamSynchronize((cudaStream_t)stream), "stream sync");
+}
+
+int tg_cuda_kv_device_error(void) {
+    if (!g_ready) return 0;
+    int32_t v = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+    if (cudaMemcpy(&v, g_err_word, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (v) cudaMemset(g_err_word, 0, 4);
+    return v;
+}
+
+/* ---- append ------------------------------------------------------------- */
+static int launch_rc(int rc, const char* what) {
+    if (rc == 0) return 1;
+    set_err("%s: %s", what, cudaGetErrorString((cudaError_t)rc));
+    return 0;
+}
+
+int tg_cuda_kv_append(int dtype, TGCudaCacheDesc cache, uint32_t kv_dim, uint32_t row0,
+                      const float* k, const float* v, uint32_t n_rows, void* stream) {
+    if (!g_ready && !tg_cuda_kv_init()) return 0;
+    if (n_rows == 0) return 1;
+    if (!k || !v || !cache.base) { set_err("append: NULL pointer"); return 0; }
+    if ((uint64_t)row0 + n_rows > cache.max_seq) { set_err("append: capacity exceeded"); return 0; }
+    if (kv_dim % 8) { set_err("append: kv_dim %u is not a multiple of 8", kv_dim); return 0; }
+    if (((uintptr_t)k | (uintptr_t)v) & 15u) {
+        set_err("append: source rows must be 16-byte aligned");
+        return 0;
+    }
+    static _Thread_local TGKvAppendParams p;   /* ~4 KB: keep off the stack */
+    memset(&p, 0, offsetof(TGKvAppendParams, pos));
+    p.caches = NULL;
+    p.cache0.base = cache.base;
+    p.cache0.max_seq = cache.max_seq;
+    p.k = k;
+    p.v = v;
+    p.cache_stride = 0;
+    p.n_items = 1;
+    p.rows_per_item = n_rows;
+    p.kv_dim = kv_dim;
+    p.pos[0] = row0;
+    return launch_rc(tgkv_launch_append(&p, dtype, stream), "append kernel");
+}
+
+int tg_cuda_kv_append_batch(int dtype, const TGCudaCacheDesc* table_dev, uint32_t kv_dim,
+                            const uint32_t* pos, uint32_t n_items,
+                            const float* k, const float* v, void* stream) {
+    if (!g_ready && !tg_cuda_kv_init()) return 0;
+    if (n_items == 0) return 1;
+    if (!table_dev || !pos || !k || !v) { set_err("append_batch: NULL pointer"); return 0; }
+    if (kv_dim % 8) { set_err("append_batch: kv_dim %u is not a multiple of 8", kv_dim); return 0; }
+    static _Thread_local TGKvAppendParams p;
+    for (uint32_t b0 = 0; b0 < n_items; b0 += TGKV_MAX_ITEMS) {
+        const uint32_t n = (n_items - b0) < TGKV_MAX_ITEMS ? (n_items - b0) : TGKV_MAX_ITEMS;
+        memset(&p, 0, offsetof(TGKvAppendParams, pos));
+        p.caches = (const TGKvCacheDesc*)(table_dev + b0);
+        p.k = k + (uint64_t)b0 * kv_dim;
+        p.v = v + (uint64_t)b0 * kv_dim;
+        p.cache_stride = 1;
+        p.n_items = n;
+        p.rows_per_item = 1;
+        p.kv_dim = kv_dim;
+        memcpy(p.pos, pos + b0, n * sizeof(uint32_t));
+        if (!launch_rc(tgkv_launch_append(&p, dtype, stream), "append_batch kernel")) return 0;
+    }
+    return 1;
+}
+
+/* ---- attention planning ------------------------------------------------- */
+int tg_cuda_kv_attn_supported(int dtype, uint32_t head_dim) {
+    return tgkv_attention_supported(dtype, head_dim);
+}
+
+typedef struct {
+    uint32_t gt, n_sub, chunk;
+    uint64_t max_ctas;        /* largest CTA count of any launch of the call */
+} AttnPlan;
+
+static uint32_t round_up(uint32_t x, uint32_t m) { return (x + m - 1) / m * m; }
+
+/* Chunk length: about eight waves of two CTAs per SM over the whole call,
+ * never below 128 positions (per-CTA overhead) -- TGKV_CHUNK overrides. */
+static uint32_t pick_chunk(uint64_t total_positions) {
+    const char* e = getenv("TGKV_CHUNK");
+    if (e && e[0]) {
+        long c = atol(e);
+        if (c >= TGKV_TILE) return round_up((uint32_t)c, TGKV_TILE);
+    }
+    const uint64_t target = (uint64_t)(g_sm_count > 0 ? g_sm_count : 148) * 2 * 8;
+    uint64_t c = (total_positions + target - 1) / target;
+    if (c < 128) c = 128;
+    if (c > (1u << 30)) c = 1u << 30;
+    return round_up((uint32_t)c, TGKV_TILE);
+}
+
+static int plan_attention(const TGCudaAttnCall* c, AttnPlan* pl) {
+    if (!c || c->n_kv_heads == 0 || c->n_heads == 0 || c->n_heads % c->n_kv_heads) {
+        set_err("attention: n_heads must be a positive multiple of n_kv_heads");
+        return 0;
+    }
+    if (!tgkv_attention_supported(c->dtype, c->head_dim)) {
+        set_err("attention: no kernel for dtype %d head_dim %u", c->dtype, c->head_dim);
+        return 0;
+    }
+    const uint32_t group = c->n_heads / c->n_kv_heads;
+    pl->gt = tgkv_attention_g_tile(c->head_dim, group);
+    pl->n_sub = group / pl->gt;
+    uint64_t total = 0;
+    for (uint32_t i = 0; i < c->n_items; i++) {
+        if (c->n_pos[i] == 0) { set_err("attention: item %u attends no position", i); return 0; }
+        total += (uint64_t)c->n_pos[i] * c->n_kv_heads * pl->n_sub;
+    }
+    pl->chunk = pick_chunk(total);
+    pl->max_ctas = 0;
+    for (uint32_t b0 = 0; b0 < c->n_items; b0 += TGKV_MAX_ITEMS) {
+        const uint32_t n = (c->n_items - b0) < TGKV_MAX_ITEMS ? (c->n_items - b0) : TGKV_MAX_ITEMS;
+        uint64_t ctas = 0;
+        for (uint32_t i = 0; i < n; i++)
+            ctas += (uint64_t)((c->n_pos[b0 + i] + pl->chunk - 1) / pl->chunk) * c->n_kv_heads *
+                    pl->n_sub;
+        if (ctas > 0x7fffffffu) { set_err("attention: too many CTAs in one launch"); return 0; }
+        if (ctas > pl->max_ctas) pl->max_ctas = ctas;
+    }
+    return 1;
+}
+
+static uint64_t part_o_bytes(const AttnPlan* pl, uint32_t head_dim) {
+    return (pl->max_ctas * pl->gt * head_dim * 4 + 255) / 256 * 256;
+}
+
+uint64_t tg_cuda_kv_attn_scratch_bytes(const TGCudaAttnCall* c) {
+    AttnPlan pl;
+    if (!plan_attention(c, &pl)) return 0;
+    return part_o_bytes(&pl, c->head_dim) + pl.max_ctas * pl.gt * 2 * 4;
+}
+
+uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c) {
+    AttnPlan pl;
+    if (!plan_attention(c, &pl)) return 0;
+    return (uint64_t)c->n_items * c->n_kv_heads * pl.n_sub;
+}
+
+uint32_t tg_cuda_kv_attn_last_launches(void) { return t_last_launches; }
+
+int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
+    t_last_launches = 0;
+    if (!g_ready && !tg_cuda_kv_init()) return 0;
+    AttnPlan pl;
+    if (!plan_attention(c, &pl)) return 0;
+    if (c->n_items == 0) return 1;
+    if (!c->q || !c->out || (!c->table_dev && !c->cache.base)) {
+        set_err("attention: NULL pointer");
+        return 0;
+    }
+    if (((uintptr_t)c->q | (uintptr_t)c->out) & 7u) {
+        set_err("attention: q/out must be 8-byte aligned");
+        return 0;
+    }
+    int multi = 0;
+    for (uint32_t i = 0; i < c->n_items && !multi; i++) multi = c->n_pos[i] > pl.chunk;
+    if (multi && (!c->scratch || !c->counters)) {
+        set_err("attention: split-sequence scratch not provided");
+        return 0;
+    }
+    static _Thread_local TGKvAttnParams p;     /* ~8 KB: keep off the stack */
+    const uint64_t po = part_o_bytes(&pl, c->head_dim);
+    for (uint32_t b0 = 0; b0 < c->n_items; b0 += TGKV_MAX_ITEMS) {
+        const uint32_t n = (c->n_items - b0) < TGKV_MAX_ITEMS ? (c->n_items - b0) : TGKV_MAX_ITEMS;
+        memset(&p, 0, offsetof(TGKvAttnParams, n_pos));
+        p.caches = (const TGKvCacheDesc*)(c->table_dev ? c->table_dev + b0 : NULL);
+        p.cache0.base = c->cache.base;
+        p.cache0.max_seq = c->cache.max_seq;
+        p.q = c->q;
+        p.out = c->out;
+        p.part_o = (float*)c->scratch;
+        p.part_ml = c->scratch ? (float*)((char*)c->scratch + po) : NULL;
+        p.counters = c->counters;
+        p.err = g_err_word;
+        p.cache_stride = c->table_dev ? 1u : 0u;
+        p.n_items = n;
+        p.n_heads = c->n_heads;
+        p.n_kv_heads = c->n_kv_heads;
+        p.n_sub = pl.n_sub;
+        p.chunk = pl.chunk;
+        p.qscale = c->scale * 1.4426950408889634f;
+        p.item_base = b0;
+        uint32_t acc = 0;
+        for (uint32_t i = 0; i < n; i++) {
+            const uint32_t np = c->n_pos[b0 + i];
+            p.n_pos[i] = np;
+            p.cta_prefix[i] = acc;
+            acc += ((np + pl.chunk - 1) / pl.chunk) * c->n_kv_heads * pl.n_sub;
+        }
+        p.cta_prefix[n] = acc;
+        if (!launch_rc(tgkv_launch_attention(&p, c->dtype, c->head_dim, pl.gt, acc, stream),
+                       "attention kernel"))
+            return 0;
+        t_last_launches++;
+    }
+    return 1;
+}
+
+/* ---- RoPE + append ------------------------------------------------------ */
+int tg_cuda_kv_rope_append(int dtype, const float* qkv, const float* cs, const float* sn,
+                           void* kvc, float* qout, uint32_t n_tokens, uint32_t n_heads,
+                           uint32_t n_kv_heads, uint32_t head_dim, uint32_t start_pos,
+                           uint32_t max_seq, void* stream) {
+    if (!g_ready && !tg_cuda_kv_init()) return 0;
+    if (n_tokens == 0) return 1;
+    if (!qkv || !cs || !sn || !kvc || !qout) { set_err("rope: NULL pointer"); return 0; }
+    if (head_dim == 0 || (head_dim & 1) || n_kv_heads == 0 || n_kv_heads > n_heads) {
+        set_err("rope: bad head geometry");
+        return 0;
+    }
+    if ((uint64_t)start_pos + n_tokens > max_seq) { set_err("rope: capacity exceeded"); return 0; }
+    TGKvRopeParams p;
+    p.qkv = qkv;
+    p.cs = cs;
+    p.sn = sn;
+    p.kvc = kvc;
+    p.qout = qout;
+    p.n_tokens = n_tokens;
+    p.n_heads = n_heads;
+    p.n_kv_heads = n_kv_heads;
+    p.head_dim = head_dim;
+    p.start_pos = start_pos;
+    p.max_seq = max_seq;
+    p.dtype = dtype;
+    return launch_rc(tgkv_launch_rope_append(&p, stream), "rope kernel");
+}

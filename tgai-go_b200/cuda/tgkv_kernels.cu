@@ -1,0 +1,643 @@
+// tgkv_kernels.cu -- sm_100a kernels for TGAI GO's KV-cache path.
+//
+//   * attention: split-sequence (flash-decoding) GQA attention over caches in
+//     the [2][max_seq][kv_dim] layout of src/tgai_kv_cache.h:15-21.  One CTA
+//     streams one chunk of positions of one KV head: a producer warp moves K
+//     and V rows into a shared-memory ring with bulk async copies
+//     (cp.async.bulk, mbarrier completion), four consumer warps compute the
+//     scores of all GT query heads of the group from the same staged rows
+//     (K/V read once per KV head), keep an online softmax in the log2 domain
+//     with warp-shuffle reductions, and accumulate P*V with packed fp32 FMAs.
+//     Chunks of one (item, KV head) merge in the last CTA to finish.
+//     Semantics follow src/tgai_engine.c:3943-4011: kvh = h*nkv/nh, scores
+//     scaled by 1/sqrt(head_dim), causal, softmax, P*V.
+//   * append: fp32 rows -> cache rows (fp32 copy or bf16 round-to-nearest-
+//     even), 16-byte vector loads and stores.
+//   * rope_append: shaders/rope.comp semantics (rotate Q and K, write K and V
+//     into the cache).
+//
+// Every wait on an mbarrier is bounded by %globaltimer; on expiry the kernel
+// records an error code in p.err and returns instead of spinning.
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include "tgkv_launch.h"
+
+namespace tgkv {
+
+constexpr int kTile = TGKV_TILE;     // positions per stage
+constexpr int kConsumerWarps = 4;    // 8 positions of a stage per warp
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s
+
+// Error codes written to p.err.
+constexpr int kErrFullTimeout = 1;
+constexpr int kErrEmptyTimeout = 2;
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for the phase with the given parity to complete; false after ~2 s.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+        for (int i = 0; i < 256; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+// Bulk async copy global -> shared, completion counted on `bar` in bytes.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    return __ffma2_rn(a, b, c);
+}
+
+__device__ __forceinline__ float2 bf16pair_to_f2(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+__device__ __forceinline__ uint16_t f32_to_bf16_rne(float f) {
+    // Same rule as the host oracle: NaN stays a quiet NaN, else round to
+    // nearest even on the upper 16 bits.
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu))
+        return static_cast<uint16_t>((u >> 16) | 0x0040u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return static_cast<uint16_t>(u >> 16);
+}
+
+}  // namespace tgkv
+
+namespace tgkv {
+
+// ------------------------------------------------------------ attention
+// Compile-time geometry of one (dtype, head_dim, heads-per-CTA) variant.
+template <int DT, int HD, int GT>
+struct AttnCfg {
+    static constexpr int ES = DT ? 2 : 4;              // bytes per element
+    static constexpr int RB = HD * ES;                 // bytes per K/V row of one head
+    static constexpr int LB = RB / 8;                  // bytes of a row per lane (8 lanes/row)
+    static constexpr int VW = LB >= 16 ? 16 : LB;      // vector width in bytes
+    static constexpr int NVEC = LB / VW;               // vectors per lane per row
+    static constexpr int EPV = VW / ES;                // elements per vector
+    static constexpr int NP = (HD / 8) / 2;            // float2 per lane per row
+    static constexpr int STAGE = 2 * kTile * RB;       // K tile + V tile
+    static constexpr int NSTAGE = (98304 / STAGE) > 8 ? 8 : (98304 / STAGE);
+    static constexpr int HSTEP = 4 / GT;               // lane stride between heads
+    static_assert(RB % 64 == 0, "row must be a multiple of 64 bytes");
+    static_assert(GT == 1 || GT == 2 || GT == 4, "GT");
+    static_assert(NSTAGE >= 2, "stages");
+    // shared memory carve-up (bytes)
+    static constexpr int OFF_BAR = NSTAGE * STAGE;
+    static constexpr int OFF_P = OFF_BAR + 2 * NSTAGE * 8;
+    static constexpr int OFF_ALPHA = OFF_P + kConsumerWarps * 32 * 4;
+    static constexpr int OFF_CO = OFF_ALPHA + kConsumerWarps * 4 * 4;
+    static constexpr int OFF_CML = OFF_CO + kConsumerWarps * GT * HD * 4;
+    static constexpr int OFF_FLAG = OFF_CML + kConsumerWarps * GT * 2 * 4;
+    static constexpr int SMEM = OFF_FLAG + 16;
+};
+
+// Unpack one lane vector (VW bytes at p) into EPV/2 float2.
+template <int DT, int VW>
+__device__ __forceinline__ void load_vec(const unsigned char* p, float2* o) {
+    if constexpr (DT == 0) {
+        static_assert(VW == 16, "f32 rows use 16-byte vectors");
+        const float4 x = *reinterpret_cast<const float4*>(p);
+        o[0] = make_float2(x.x, x.y);
+        o[1] = make_float2(x.z, x.w);
+    } else if constexpr (VW == 16) {
+        const uint4 w = *reinterpret_cast<const uint4*>(p);
+        o[0] = bf16pair_to_f2(w.x);
+        o[1] = bf16pair_to_f2(w.y);
+        o[2] = bf16pair_to_f2(w.z);
+        o[3] = bf16pair_to_f2(w.w);
+    } else {
+        const uint2 w = *reinterpret_cast<const uint2*>(p);
+        o[0] = bf16pair_to_f2(w.x);
+        o[1] = bf16pair_to_f2(w.y);
+    }
+}
+
+// A lane's slice of one row: vector v covers bytes v*8*VW + j*VW.
+template <int DT, int HD, int GT>
+__device__ __forceinline__ void load_row(const unsigned char* row, int j, float2* o) {
+    using C = AttnCfg<DT, HD, GT>;
+#pragma unroll
+    for (int v = 0; v < C::NVEC; ++v)
+        load_vec<DT, C::VW>(row + v * 8 * C::VW + j * C::VW, o + v * (C::EPV / 2));
+}
+
+// Element index of float2 slot i of lane j (first of the pair).
+template <int DT, int HD, int GT>
+__device__ __forceinline__ int elem_of(int j, int i) {
+    using C = AttnCfg<DT, HD, GT>;
+    const int v = i / (C::EPV / 2), w = i % (C::EPV / 2);
+    return (v * 8 * C::VW + j * C::VW) / C::ES + 2 * w;
+}
+
+// Reduce N per-lane values over the 8 lanes of a group (xor 4, 2, 1) so that
+// each lane ends with one complete sum: lane bit 2 picks the upper half of
+// the values first, then bit 1, then bit 0 (while values remain to split).
+template <int N>
+__device__ __forceinline__ float group_transpose_reduce(float (&v)[N], int lane) {
+    int n = N;
+#pragma unroll
+    for (int mask = 4; mask >= 1; mask >>= 1) {
+        if (n >= 2) {
+            const int half = n / 2;
+            const bool upper = (lane & mask) != 0;
+#pragma unroll
+            for (int i = 0; i < N / 2; ++i) {
+                if (i < half) {
+                    const float send = upper ? v[i] : v[i + half];
+                    const float keep = upper ? v[i + half] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+                }
+            }
+            n = half;
+        } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], mask);
+        }
+    }
+    return v[0];
+}
+
+__device__ __forceinline__ void consumer_bar() {
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+template <int DT, int HD, int GT>
+__global__ void __launch_bounds__(kThreads, 2)
+attention_kernel(const __grid_constant__ TGKvAttnParams p) {
+    using C = AttnCfg<DT, HD, GT>;
+    extern __shared__ __align__(128) unsigned char smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+    uint64_t* empty = full + C::NSTAGE;
+    float* sm_p = reinterpret_cast<float*>(smem + C::OFF_P);          // [4][32]
+    float* sm_alpha = reinterpret_cast<float*>(smem + C::OFF_ALPHA);  // [4][4]
+    float* sm_co = reinterpret_cast<float*>(smem + C::OFF_CO);        // [4][GT][HD]
+    float* sm_cml = reinterpret_cast<float*>(smem + C::OFF_CML);      // [4][GT][2]
+    int* sm_flag = reinterpret_cast<int*>(smem + C::OFF_FLAG);        // [0] abort, [1] last
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t b = blockIdx.x;
+
+    // ---- which (item, kv head, head subset, chunk) this CTA owns
+    uint32_t lo = 0, hi = p.n_items;            // largest i with cta_prefix[i] <= b
+    while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (p.cta_prefix[mid] <= b) lo = mid; else hi = mid;
+    }
+    const uint32_t item = lo;
+    const uint32_t npos = p.n_pos[item];
+    const uint32_t nch = (npos + p.chunk - 1) / p.chunk;
+    const uint32_t unit = b - p.cta_prefix[item];
+    const uint32_t chunk = unit % nch, rest = unit / nch;
+    const uint32_t kvh = rest % p.n_kv_heads, sub = rest / p.n_kv_heads;
+    const uint32_t c0 = chunk * p.chunk;
+    const uint32_t c1 = min(c0 + p.chunk, npos);
+    const int ntiles = (int)((c1 - c0 + kTile - 1) / kTile);
+    const uint32_t group = p.n_heads / p.n_kv_heads;
+    const uint32_t head0 = kvh * group + sub * GT;
+
+    const TGKvCacheDesc cd = p.caches ? p.caches[item * p.cache_stride] : p.cache0;
+    const uint64_t kv_dim = (uint64_t)p.n_kv_heads * HD;
+    const unsigned char* kbase =
+        reinterpret_cast<const unsigned char*>(cd.base) + (uint64_t)kvh * C::RB;
+    const unsigned char* vbase = kbase + (uint64_t)cd.max_seq * kv_dim * C::ES;
+    const uint64_t rstride = kv_dim * C::ES;
+
+    if (tid == 0) {
+        for (int s = 0; s < C::NSTAGE; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        sm_flag[0] = 0;
+        sm_flag[1] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ---------------- producer: bulk copies of K and V rows into the ring
+        for (int t = 0; t < ntiles; ++t) {
+            const int s = t % C::NSTAGE;
+            if (t >= C::NSTAGE) {
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait(&empty[s], ((t / C::NSTAGE) - 1) & 1);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) {
+                    if (lane == 0) { atomicExch(p.err, kErrEmptyTimeout); sm_flag[0] = 1; }
+                    break;
+                }
+            }
+            const uint32_t row0 = c0 + (uint32_t)t * kTile;
+            const int nv = (int)min((uint32_t)kTile, c1 - row0);
+            if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * nv * C::RB));
+            __syncwarp();
+            if (lane < nv) {
+                unsigned char* st = smem + s * C::STAGE;
+                const uint64_t off = (uint64_t)(row0 + lane) * rstride;
+                bulk_g2s(st + lane * C::RB, kbase + off, C::RB, &full[s]);
+                bulk_g2s(st + kTile * C::RB + lane * C::RB, vbase + off, C::RB, &full[s]);
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers
+    const int g = lane >> 3, j = lane & 7;
+    const int r_me = (lane >> 2) & 1;
+    const int h_me = (lane & 3) / C::HSTEP;
+    const bool canon = (lane & (C::HSTEP - 1)) == 0;
+
+    float2 q2[GT][C::NP];
+    {
+        const float* qrow = p.q + (uint64_t)(p.item_base + item) * p.n_heads * HD;
+#pragma unroll
+        for (int h = 0; h < GT; ++h) {
+            const float* qh = qrow + (uint64_t)(head0 + h) * HD;
+#pragma unroll
+            for (int i = 0; i < C::NP; ++i) {
+                const float2 x = *reinterpret_cast<const float2*>(qh + elem_of<DT, HD, GT>(j, i));
+                q2[h][i] = make_float2(x.x * p.qscale, x.y * p.qscale);
+            }
+        }
+    }
+    float2 o2[GT][C::NP];
+#pragma unroll
+    for (int h = 0; h < GT; ++h)
+#pragma unroll
+        for (int i = 0; i < C::NP; ++i) o2[h][i] = make_float2(0.f, 0.f);
+    float m_run = -INFINITY, l_lane = 0.f;
+    bool aborted = false;
+
+    for (int t = 0; t < ntiles; ++t) {
+        const int s = t % C::NSTAGE;
+        if (!mbar_wait(&full[s], (t / C::NSTAGE) & 1)) {
+            if (lane == 0) { atomicExch(p.err, kErrFullTimeout); sm_flag[0] = 1; }
+            aborted = true;
+            break;
+        }
+        const unsigned char* kt = smem + s * C::STAGE;
+        const unsigned char* vt = kt + kTile * C::RB;
+        const uint32_t tpos = c0 + (uint32_t)t * kTile;
+
+        // scores of rows w*8 + r*4 + g for r = 0, 1 and all GT heads
+        float sc[2 * GT];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            float2 k2[C::NP];
+            load_row<DT, HD, GT>(kt + (warp * 8 + r * 4 + g) * C::RB, j, k2);
+#pragma unroll
+            for (int h = 0; h < GT; ++h) {
+                float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int i = 0; i < C::NP; ++i) acc = ffma2(q2[h][i], k2[i], acc);
+                sc[r * GT + h] = acc.x + acc.y;
+            }
+        }
+        float sv = group_transpose_reduce<2 * GT>(sc, lane);
+        const bool valid = tpos + (uint32_t)(warp * 8 + r_me * 4 + g) < c1;
+        sv = valid ? sv : -INFINITY;
+
+        float tm = sv;
+        tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 4));
+        tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 8));
+        tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 16));
+        // Lazy rescale: the running maximum only moves when a score exceeds it
+        // by more than 2^8, so exp2(score - m_run) stays <= 256.
+        const bool need = tm > m_run + 8.f;
+        if (__any_sync(0xffffffffu, need)) {
+            const float m_new = fmaxf(m_run, tm);
+            const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(m_run - m_new);
+            m_run = m_new;
+            l_lane *= alpha;
+            if (g == 0 && r_me == 0 && canon) sm_alpha[warp * 4 + h_me] = alpha;
+            __syncwarp();
+#pragma unroll
+            for (int h = 0; h < GT; ++h) {
+                const float a = sm_alpha[warp * 4 + h];
+#pragma unroll
+                for (int i = 0; i < C::NP; ++i) {
+                    o2[h][i].x *= a;
+                    o2[h][i].y *= a;
+                }
+            }
+        }
+        const float pv = (sv == -INFINITY) ? 0.f : exp2f(sv - m_run);
+        if (canon) l_lane += pv;
+        sm_p[warp * 32 + lane] = pv;
+        __syncwarp();
+
+        const bool tail = tpos + kTile > c1;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int row = warp * 8 + r * 4 + g;
+            float2 v2[C::NP];
+            load_row<DT, HD, GT>(vt + row * C::RB, j, v2);
+            if (tail && tpos + (uint32_t)row >= c1) {
+#pragma unroll
+                for (int i = 0; i < C::NP; ++i) v2[i] = make_float2(0.f, 0.f);
+            }
+#pragma unroll
+            for (int h = 0; h < GT; ++h) {
+                const float ph = sm_p[warp * 32 + g * 8 + r * 4 + h * C::HSTEP];
+                const float2 p2 = make_float2(ph, ph);
+#pragma unroll
+                for (int i = 0; i < C::NP; ++i) o2[h][i] = ffma2(p2, v2[i], o2[h][i]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    (void)aborted;
+
+    // ---- warp totals: O over the four row groups, l over lanes of a head
+#pragma unroll
+    for (int h = 0; h < GT; ++h)
+#pragma unroll
+        for (int i = 0; i < C::NP; ++i) {
+            o2[h][i].x += __shfl_xor_sync(0xffffffffu, o2[h][i].x, 8);
+            o2[h][i].y += __shfl_xor_sync(0xffffffffu, o2[h][i].y, 8);
+            o2[h][i].x += __shfl_xor_sync(0xffffffffu, o2[h][i].x, 16);
+            o2[h][i].y += __shfl_xor_sync(0xffffffffu, o2[h][i].y, 16);
+        }
+    if (C::HSTEP >= 2) l_lane += __shfl_xor_sync(0xffffffffu, l_lane, 1);
+    if (C::HSTEP >= 4) l_lane += __shfl_xor_sync(0xffffffffu, l_lane, 2);
+    l_lane += __shfl_xor_sync(0xffffffffu, l_lane, 4);
+    l_lane += __shfl_xor_sync(0xffffffffu, l_lane, 8);
+    l_lane += __shfl_xor_sync(0xffffffffu, l_lane, 16);
+
+    if (lane < 8) {
+#pragma unroll
+        for (int h = 0; h < GT; ++h)
+#pragma unroll
+            for (int i = 0; i < C::NP; ++i) {
+                float* dst = sm_co + (warp * GT + h) * HD + elem_of<DT, HD, GT>(j, i);
+                dst[0] = o2[h][i].x;
+                dst[1] = o2[h][i].y;
+            }
+    }
+    if (g == 0 && r_me == 0 && canon) {
+        sm_cml[(warp * GT + h_me) * 2 + 0] = m_run;
+        sm_cml[(warp * GT + h_me) * 2 + 1] = l_lane;
+    }
+    consumer_bar();
+
+    // ---- merge the four warps; write the output or this chunk's partial
+    const uint64_t out_row = (uint64_t)(p.item_base + item) * p.n_heads * HD;
+    for (int idx = tid; idx < GT * HD; idx += 128) {
+        const int h = idx / HD, d = idx % HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm_cml[(w * GT + h) * 2]);
+        float O = 0.f, L = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+            const float mw = sm_cml[(w * GT + h) * 2];
+            const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+            O += sm_co[(w * GT + h) * HD + d] * f;
+            L += sm_cml[(w * GT + h) * 2 + 1] * f;
+        }
+        if (nch == 1) {
+            p.out[out_row + (uint64_t)(head0 + h) * HD + d] = (L > 0.f) ? O / L : 0.f;
+        } else {
+            p.part_o[((uint64_t)b * GT + h) * HD + d] = O;
+            if (d == 0) {
+                p.part_ml[((uint64_t)b * GT + h) * 2 + 0] = M;
+                p.part_ml[((uint64_t)b * GT + h) * 2 + 1] = L;
+            }
+        }
+    }
+    if (nch == 1) return;
+
+    // ---- split-sequence combine in the last CTA of this (item, kvh, sub)
+    __threadfence();
+    consumer_bar();
+    const uint64_t cidx =
+        ((uint64_t)(p.item_base + item) * p.n_sub + sub) * p.n_kv_heads + kvh;
+    if (tid == 0) {
+        const uint32_t prev = atomicAdd(&p.counters[cidx], 1u);
+        sm_flag[1] = (prev == nch - 1) ? 1 : 0;
+    }
+    consumer_bar();
+    if (!sm_flag[1]) return;
+    __threadfence();
+    const uint64_t slot0 = (uint64_t)p.cta_prefix[item] + (uint64_t)rest * nch;
+    for (int idx = tid; idx < GT * HD; idx += 128) {
+        const int h = idx / HD, d = idx % HD;
+        float M = -INFINITY;
+        for (uint32_t c = 0; c < nch; ++c)
+            M = fmaxf(M, __ldcg(&p.part_ml[((slot0 + c) * GT + h) * 2]));
+        float O = 0.f, L = 0.f;
+        for (uint32_t c = 0; c < nch; ++c) {
+            const float mc = __ldcg(&p.part_ml[((slot0 + c) * GT + h) * 2]);
+            const float f = (mc == -INFINITY) ? 0.f : exp2f(mc - M);
+            O += __ldcg(&p.part_o[((slot0 + c) * GT + h) * HD + d]) * f;
+            L += __ldcg(&p.part_ml[((slot0 + c) * GT + h) * 2 + 1]) * f;
+        }
+        p.out[out_row + (uint64_t)(head0 + h) * HD + d] = (L > 0.f) ? O / L : 0.f;
+    }
+    if (tid == 0) p.counters[cidx] = 0u;
+}
+
+}  // namespace tgkv
+
+namespace tgkv {
+
+// ------------------------------------------------------------ append
+// One thread moves 8 consecutive elements of one K or V row (blockIdx.y picks
+// K or V): two 16-byte loads of fp32, one or two 16-byte stores.
+template <int DT>
+__global__ void __launch_bounds__(256) append_kernel(const __grid_constant__ TGKvAppendParams p) {
+    const uint64_t vec_per_row = p.kv_dim / 8;
+    const uint64_t rows = (uint64_t)p.n_items * p.rows_per_item;
+    const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= rows * vec_per_row) return;
+    const int which = blockIdx.y;                       // 0 = K, 1 = V
+    const uint64_t row = t / vec_per_row, e = (t % vec_per_row) * 8;
+    const uint32_t item = (uint32_t)(row / p.rows_per_item);
+    const uint32_t r = (uint32_t)(row % p.rows_per_item);
+    const float* src = (which ? p.v : p.k) + row * p.kv_dim + e;
+    const float4 a = *reinterpret_cast<const float4*>(src);
+    const float4 b = *reinterpret_cast<const float4*>(src + 4);
+    const TGKvCacheDesc cd = p.caches ? p.caches[item * p.cache_stride] : p.cache0;
+    const uint64_t pos = (uint64_t)p.pos[item] + r;
+    const uint64_t elem = (uint64_t)which * cd.max_seq * p.kv_dim + pos * p.kv_dim + e;
+    if constexpr (DT == 0) {
+        float* dst = reinterpret_cast<float*>(cd.base) + elem;
+        *reinterpret_cast<float4*>(dst) = a;
+        *reinterpret_cast<float4*>(dst + 4) = b;
+    } else {
+        uint4 w;
+        w.x = (uint32_t)f32_to_bf16_rne(a.x) | ((uint32_t)f32_to_bf16_rne(a.y) << 16);
+        w.y = (uint32_t)f32_to_bf16_rne(a.z) | ((uint32_t)f32_to_bf16_rne(a.w) << 16);
+        w.z = (uint32_t)f32_to_bf16_rne(b.x) | ((uint32_t)f32_to_bf16_rne(b.y) << 16);
+        w.w = (uint32_t)f32_to_bf16_rne(b.z) | ((uint32_t)f32_to_bf16_rne(b.w) << 16);
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(cd.base) + elem) = w;
+    }
+}
+
+// ------------------------------------------------------------ rope + append
+// shaders/rope.comp semantics: thread = (token, head, pair).  Q of every head
+// is rotated into qout; heads below n_kv_heads also rotate K and copy V into
+// the cache at position start_pos + token.  The rotation is evaluated as the
+// reference engine's gcc -mfma build evaluates src/tgai_engine.c:3480-3481:
+// x0*c - x1*s == fma(x0, c, -(x1*s)), x0*s + x1*c == fma(x0, s, x1*c).
+__device__ __forceinline__ float2 rotate_pair(float x0, float x1, float c, float s) {
+    return make_float2(__fmaf_rn(x0, c, -__fmul_rn(x1, s)), __fmaf_rn(x0, s, __fmul_rn(x1, c)));
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256) rope_append_kernel(const __grid_constant__ TGKvRopeParams p) {
+    const uint32_t half = p.head_dim >> 1;
+    const uint64_t total = (uint64_t)p.n_tokens * p.n_heads * half;
+    const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= total) return;
+    const uint32_t pair = (uint32_t)(gid % half);
+    const uint32_t head = (uint32_t)((gid / half) % p.n_heads);
+    const uint32_t tok = (uint32_t)(gid / ((uint64_t)half * p.n_heads));
+    const uint64_t q_dim = (uint64_t)p.n_heads * p.head_dim;
+    const uint64_t kv_dim = (uint64_t)p.n_kv_heads * p.head_dim;
+    const uint64_t stride = q_dim + 2 * kv_dim;
+    const uint64_t pos = (uint64_t)p.start_pos + tok;
+    const float c = p.cs[pos * half + pair], s = p.sn[pos * half + pair];
+    const uint32_t i0 = pair * 2;
+    const float* row = p.qkv + tok * stride;
+    const float2 q = rotate_pair(row[head * p.head_dim + i0], row[head * p.head_dim + i0 + 1], c, s);
+    p.qout[tok * q_dim + head * p.head_dim + i0] = q.x;
+    p.qout[tok * q_dim + head * p.head_dim + i0 + 1] = q.y;
+    if (head < p.n_kv_heads) {
+        const float* kr = row + q_dim + head * p.head_dim + i0;
+        const float* vr = row + q_dim + kv_dim + head * p.head_dim + i0;
+        const float2 k = rotate_pair(kr[0], kr[1], c, s);
+        const uint64_t ko = pos * kv_dim + head * p.head_dim + i0;
+        const uint64_t vo = (uint64_t)p.max_seq * kv_dim + ko;
+        if constexpr (DT == 0) {
+            float* kv = reinterpret_cast<float*>(p.kvc);
+            kv[ko] = k.x; kv[ko + 1] = k.y;
+            kv[vo] = vr[0]; kv[vo + 1] = vr[1];
+        } else {
+            uint32_t* kv = reinterpret_cast<uint32_t*>(p.kvc);
+            kv[ko / 2] = (uint32_t)f32_to_bf16_rne(k.x) | ((uint32_t)f32_to_bf16_rne(k.y) << 16);
+            kv[vo / 2] = (uint32_t)f32_to_bf16_rne(vr[0]) | ((uint32_t)f32_to_bf16_rne(vr[1]) << 16);
+        }
+    }
+}
+
+template <int DT, int HD, int GT>
+int launch_attn(const TGKvAttnParams* p, uint32_t grid, cudaStream_t st) {
+    using C = AttnCfg<DT, HD, GT>;
+    static bool configured = false;                 // benign race: same value
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel<DT, HD, GT>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) return (int)e;
+        configured = true;
+    }
+    attention_kernel<DT, HD, GT><<<grid, kThreads, C::SMEM, st>>>(*p);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace tgkv
+
+extern "C" uint32_t tgkv_attention_g_tile(uint32_t head_dim, uint32_t group) {
+    const uint32_t cap = head_dim >= 256 ? 2u : 4u;
+    uint32_t gt = group < cap ? group : cap;
+    while (gt > 1 && group % gt) --gt;
+    return gt;
+}
+
+extern "C" int tgkv_attention_supported(int dtype, uint32_t head_dim) {
+    if (dtype == 0) return head_dim == 32 || head_dim == 64 || head_dim == 128;
+    if (dtype == 1) return head_dim == 32 || head_dim == 64 || head_dim == 128 || head_dim == 256;
+    return 0;
+}
+
+#define TGKV_ATTN_CASE(DT, HD, GT)                                             \
+    if (dtype == DT && head_dim == HD && g_tile == GT)                         \
+        return tgkv::launch_attn<DT, HD, GT>(p, grid, st);
+
+extern "C" int tgkv_launch_attention(const TGKvAttnParams* p, int dtype, uint32_t head_dim,
+                                     uint32_t g_tile, uint32_t grid, void* stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    if (grid == 0) return 0;
+    TGKV_ATTN_CASE(0, 32, 1) TGKV_ATTN_CASE(0, 32, 2) TGKV_ATTN_CASE(0, 32, 4)
+    TGKV_ATTN_CASE(0, 64, 1) TGKV_ATTN_CASE(0, 64, 2) TGKV_ATTN_CASE(0, 64, 4)
+    TGKV_ATTN_CASE(0, 128, 1) TGKV_ATTN_CASE(0, 128, 2) TGKV_ATTN_CASE(0, 128, 4)
+    TGKV_ATTN_CASE(1, 32, 1) TGKV_ATTN_CASE(1, 32, 2) TGKV_ATTN_CASE(1, 32, 4)
+    TGKV_ATTN_CASE(1, 64, 1) TGKV_ATTN_CASE(1, 64, 2) TGKV_ATTN_CASE(1, 64, 4)
+    TGKV_ATTN_CASE(1, 128, 1) TGKV_ATTN_CASE(1, 128, 2) TGKV_ATTN_CASE(1, 128, 4)
+    TGKV_ATTN_CASE(1, 256, 1) TGKV_ATTN_CASE(1, 256, 2)
+    return (int)cudaErrorInvalidValue;
+}
+
+extern "C" int tgkv_launch_append(const TGKvAppendParams* p, int dtype, void* stream) {
+    const uint64_t vecs = (uint64_t)p->n_items * p->rows_per_item * (p->kv_dim / 8);
+    if (vecs == 0) return 0;
+    if (p->kv_dim % 8) return (int)cudaErrorInvalidValue;
+    dim3 grid((unsigned)((vecs + 255) / 256), 2);
+    if (dtype == 0)
+        tgkv::append_kernel<0><<<grid, 256, 0, (cudaStream_t)stream>>>(*p);
+    else
+        tgkv::append_kernel<1><<<grid, 256, 0, (cudaStream_t)stream>>>(*p);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int tgkv_launch_rope_append(const TGKvRopeParams* p, void* stream) {
+    const uint64_t total = (uint64_t)p->n_tokens * p->n_heads * (p->head_dim / 2);
+    if (total == 0) return 0;
+    const unsigned grid = (unsigned)((total + 255) / 256);
+    if (p->dtype == 0)
+        tgkv::rope_append_kernel<0><<<grid, 256, 0, (cudaStream_t)stream>>>(*p);
+    else
+        tgkv::rope_append_kernel<1><<<grid, 256, 0, (cudaStream_t)stream>>>(*p);
+    return (int)cudaGetLastError();
+}

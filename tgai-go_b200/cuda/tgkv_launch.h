@@ -1,0 +1,95 @@
+/* tgkv_launch.h -- kernel parameter blocks shared by the C bridge
+ * (tgai_cuda_bridge.c) and the CUDA kernels (tgkv_kernels.cu).  Plain C.
+ *
+ * The bridge plans a launch on the host (lengths, split-sequence chunking,
+ * scratch slots) and fills one of these structs; the kernels receive it by
+ * value in parameter space, so a launch carries every per-item length and
+ * needs no host-to-device copy of its own.
+ */
+#ifndef TGKV_LAUNCH_H
+#define TGKV_LAUNCH_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TGKV_MAX_ITEMS 1024      /* items (query rows / caches) per launch */
+#define TGKV_TILE      32        /* positions per pipeline stage */
+
+/* One cache buffer [2][max_seq][kv_dim] in device memory. */
+typedef struct {
+    uint64_t base;               /* device address */
+    uint32_t max_seq;
+    uint32_t pad;
+} TGKvCacheDesc;
+
+/* Split-sequence decode attention.
+ * CTA b works on item i (cta_prefix[i] <= b < cta_prefix[i+1]); inside the
+ * item, unit = b - cta_prefix[i] decomposes as
+ *     chunk = unit % n_chunks(i), rest = unit / n_chunks(i),
+ *     kvh = rest % n_kv_heads, sub = rest / n_kv_heads,
+ * with n_chunks(i) = ceil(n_pos[i] / chunk).  The CTA attends query heads
+ * kvh*G + sub*GT .. +GT (G = n_heads / n_kv_heads, GT heads per CTA) of item
+ * i over positions [chunk*C, min((chunk+1)*C, n_pos[i])). */
+typedef struct {
+    const TGKvCacheDesc* caches; /* device table, or NULL: every item uses cache0 */
+    TGKvCacheDesc cache0;
+    const float* q;              /* [items][n_heads][head_dim] fp32 */
+    float*       out;            /* same shape */
+    float*       part_o;         /* [ctas][GT][head_dim]  scratch */
+    float*       part_ml;        /* [ctas][GT][2]        scratch */
+    uint32_t*    counters;       /* [items][n_kv_heads][n_sub], zero, self-resetting */
+    int32_t*     err;            /* device error word (0 = fine) */
+    uint32_t cache_stride;       /* cache index = item * cache_stride */
+    uint32_t n_items;
+    uint32_t n_heads;
+    uint32_t n_kv_heads;
+    uint32_t n_sub;              /* head subsets per KV head = G / GT */
+    uint32_t chunk;              /* positions per CTA, multiple of TGKV_TILE */
+    float    qscale;             /* softmax scale * log2(e) */
+    uint32_t item_base;          /* first item of this launch (q/out/counter offset) */
+    uint32_t n_pos[TGKV_MAX_ITEMS];
+    uint32_t cta_prefix[TGKV_MAX_ITEMS + 1];
+} TGKvAttnParams;
+
+/* Append of one fp32 row per item into cache (item * cache_stride) at
+ * position pos[i] (batched decode), or of n_rows consecutive rows into one
+ * cache starting at pos[0] (cache_stride = 0, rows_per_item = n_rows). */
+typedef struct {
+    const TGKvCacheDesc* caches; /* device table, or NULL: every item uses cache0 */
+    TGKvCacheDesc cache0;
+    const float* k;              /* [rows][kv_dim] fp32 */
+    const float* v;
+    uint32_t cache_stride;
+    uint32_t n_items;
+    uint32_t rows_per_item;
+    uint32_t kv_dim;
+    uint32_t pos[TGKV_MAX_ITEMS];
+} TGKvAppendParams;
+
+/* RoPE + KV write with shaders/rope.comp semantics (f32 tables). */
+typedef struct {
+    const float* qkv;            /* [n_tokens][q_dim + 2*kv_dim] */
+    const float* cs;             /* [max_seq][head_dim/2] */
+    const float* sn;
+    void*        kvc;            /* cache buffer */
+    float*       qout;           /* [n_tokens][q_dim] */
+    uint32_t n_tokens, n_heads, n_kv_heads, head_dim, start_pos, max_seq;
+    int      dtype;
+} TGKvRopeParams;
+
+/* Launchers (tgkv_kernels.cu).  Return 0 on success, else a cudaError_t. */
+int tgkv_launch_attention(const TGKvAttnParams* p, int dtype, uint32_t head_dim,
+                          uint32_t g_tile, uint32_t grid, void* stream);
+int tgkv_launch_append(const TGKvAppendParams* p, int dtype, void* stream);
+int tgkv_launch_rope_append(const TGKvRopeParams* p, void* stream);
+/* Heads per CTA the attention kernel supports for this head_dim (<= G). */
+uint32_t tgkv_attention_g_tile(uint32_t head_dim, uint32_t group);
+/* 1 if (dtype, head_dim) has an attention kernel. */
+int tgkv_attention_supported(int dtype, uint32_t head_dim);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,435 @@
+/* tgai_kv_cache.c -- TGAI GO's KV-cache API on a B200.
+ *
+ * Host C.  Follows the reference implementation's rules (src/tgai_kv_cache.c):
+ * argument checks and the 64 GB request cap at create (:28-44), memory from
+ * the selected backend (:33, :55, :74), len-only reset (:78-83), the capacity
+ * rule of append (:95-98) and the clamped advance (:112-116).  Device work
+ * goes through tgai_gpu_dispatch.c / tgai_cuda_bridge.c; nothing here falls
+ * back to the CPU.
+ */
+#include "tgai_kv_cache.h"
+#include "tgai_backend.h"
+#include "tgai_cuda_bridge.h"
+#include "tgai_gpu_dispatch.h"
+
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+struct TGKvCache {
+    uint32_t max_seq, n_kv_heads, head_dim, kv_dim;
+    int      dtype;
+    uint32_t esize;
+    size_t   bytes;               /* 2 * max_seq * kv_dim * esize */
+    void*    dev;                 /* device address of the buffer */
+    float*   host;                /* always NULL (not mappable) */
+    uint32_t len;
+    TGBackend* be;                /* backend that owns dev */
+    void*    scratch;             /* split-sequence partials */
+    uint64_t scratch_bytes;
+    uint32_t* counters;
+    uint64_t counter_slots;
+    float*   staging;             /* device staging of host rows (bf16 append) */
+    size_t   staging_bytes;
+    uint32_t* npos;               /* host item table for attention */
+    uint32_t npos_cap;
+};
+
+static _Thread_local char t_err[256] = "kv: no error";
+
+static void set_err(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_err, sizeof(t_err), fmt, ap);
+    va_end(ap);
+}
+
+const char* tg_kv_last_error(void) { return t_err; }
+
+TGKvCache* tg_kv_create_ex(uint32_t max_seq, uint32_t n_kv_heads, uint32_t head_dim, int dtype) {
+    if (max_seq == 0 || n_kv_heads == 0 || head_dim == 0) {
+        set_err("invalid argument (0)");
+        return NULL;
+    }
+    if (dtype != TG_KV_F32 && dtype != TG_KV_BF16) {
+        set_err("invalid dtype %d", dtype);
+        return NULL;
+    }
+    TGBackend* b = tg_be_current();
+    if (!b || !b->alloc) {
+        set_err("no backend selected (call tg_be_select first)");
+        return NULL;
+    }
+    const uint32_t es = dtype == TG_KV_BF16 ? 2u : 4u;
+    const uint64_t kv_dim = (uint64_t)n_kv_heads * head_dim;
+    const uint64_t bytes64 = 2ull * max_seq * kv_dim * es;
+    if (bytes64 > (64ull << 30) || kv_dim > 0xffffffffull) {
+        set_err("request too large");
+        return NULL;
+    }
+    TGKvCache* c = (TGKvCache*)calloc(1, sizeof(TGKvCache));
+    if (!c) { set_err("calloc failed"); return NULL; }
+    c->max_seq = max_seq;
+    c->n_kv_heads = n_kv_heads;
+    c->head_dim = head_dim;
+    c->kv_dim = (uint32_t)kv_dim;
+    c->dtype = dtype;
+    c->esize = es;
+    c->bytes = (size_t)bytes64;
+    c->be = b;
+    c->dev = b->alloc(c->bytes);              /* zero-filled by the cuda backend */
+    if (!c->dev) {
+        set_err("device allocation failed: %s", b->last_error ? b->last_error() : "?");
+        free(c);
+        return NULL;
+    }
+    c->host = (float*)(b->map ? b->map(c->dev) : NULL);
+    tg_gpu_kv_register(c->dev, dtype, max_seq);
+    return c;
+}
+
+TGKvCache* tg_kv_create(uint32_t max_seq, uint32_t n_kv_heads, uint32_t head_dim) {
+    return tg_kv_create_ex(max_seq, n_kv_heads, head_dim, TG_KV_F32);
+}
+
+void tg_kv_destroy(TGKvCache* c) {
+    if (!c) return;
+    TGBackend* b = c->be;
+    if (c->dev) tg_gpu_kv_unregister(c->dev);
+    if (b && b->free) {
+        if (c->dev) b->free(c->dev);
+        if (c->scratch) b->free(c->scratch);
+        if (c->counters) b->free(c->counters);
+        if (c->staging) b->free(c->staging);
+    }
+    free(c->npos);
+    free(c);
+}
+
+void tg_kv_reset(TGKvCache* c) {
+    if (!c) return;
+    c->len = 0;                 /* rows stay; attention reads only [0, len) */
+}
+
+uint32_t tg_kv_len(const TGKvCache* c) { return c ? c->len : 0; }
+uint32_t tg_kv_capacity(const TGKvCache* c) { return c ? c->max_seq : 0; }
+void* tg_kv_device_handle(TGKvCache* c) { return c ? c->dev : NULL; }
+float* tg_kv_host_ptr(TGKvCache* c) { return c ? c->host : NULL; }
+int tg_kv_dtype(const TGKvCache* c) { return c ? c->dtype : -1; }
+uint32_t tg_kv_n_kv_heads(const TGKvCache* c) { return c ? c->n_kv_heads : 0; }
+uint32_t tg_kv_head_dim(const TGKvCache* c) { return c ? c->head_dim : 0; }
+uint64_t tg_kv_bytes(const TGKvCache* c) { return c ? (uint64_t)c->bytes : 0; }
+
+void tg_kv_advance(TGKvCache* c, uint32_t n_tokens) {
+    if (!c) return;
+    uint64_t l = (uint64_t)c->len + n_tokens;
+    c->len = l > c->max_seq ? c->max_seq : (uint32_t)l;
+}
+
+int tg_kv_truncate(TGKvCache* c, uint32_t n) {
+    if (!c) { set_err("null cache"); return 0; }
+    if (n > c->len) { set_err("truncate to %u beyond length %u", n, c->len); return 0; }
+    c->len = n;
+    return 1;
+}
+
+static int ensure_dev(TGKvCache* c, void** p, uint64_t* have, uint64_t need) {
+    if (need <= *have) return 1;
+    if (*p) c->be->free(*p);
+    const uint64_t want = need + need / 2;
+    *p = c->be->alloc((size_t)want);
+    if (!*p) {
+        *have = 0;
+        set_err("device allocation failed: %s",
+                c->be->last_error ? c->be->last_error() : "?");
+        return 0;
+    }
+    *have = want;
+    return 1;
+}
+
+int tg_kv_append(TGKvCache* c, const float* k_src, const float* v_src, uint32_t n_tokens) {
+    if (!c || !k_src || !v_src) { set_err("null argument"); return 0; }
+    if (n_tokens == 0) return 1;
+    if ((uint64_t)c->len + n_tokens > c->max_seq) { set_err("capacity exceeded"); return 0; }
+    const size_t row = (size_t)c->kv_dim * 4;
+    if (c->host) {                                   /* mappable backends (not cuda) */
+        memcpy(c->host + (size_t)c->len * c->kv_dim, k_src, row * n_tokens);
+        memcpy(c->host + (size_t)c->max_seq * c->kv_dim + (size_t)c->len * c->kv_dim, v_src,
+               row * n_tokens);
+        c->len += n_tokens;
+        return 1;
+    }
+    /* Stage the fp32 rows in HBM, then the append kernel writes them in the
+     * cache's storage type; blocks so the caller's buffers are free again. */
+    uint64_t have = c->staging_bytes;
+    if (!ensure_dev(c, (void**)&c->staging, &have, 2ull * row * n_tokens)) return 0;
+    c->staging_bytes = (size_t)have;
+    float* ks = c->staging;
+    float* vs = (float*)((char*)c->staging + row * n_tokens);
+    if (!tg_cuda_kv_h2d(ks, k_src, row * n_tokens, NULL) ||
+        !tg_cuda_kv_h2d(vs, v_src, row * n_tokens, NULL)) {
+        set_err("%s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    if (!tg_gpu_kv_append_dev(c->dtype, c->dev, c->max_seq, c->kv_dim, c->len, ks, vs, n_tokens,
+                              NULL) ||
+        !tg_cuda_kv_sync(NULL)) {
+        set_err("%s", tg_gpu_kv_error());
+        return 0;
+    }
+    c->len += n_tokens;
+    return 1;
+}
+
+int tg_kv_append_dev(TGKvCache* c, const float* k_dev, const float* v_dev, uint32_t n_tokens,
+                     void* stream) {
+    if (!c || !k_dev || !v_dev) { set_err("null argument"); return 0; }
+    if (n_tokens == 0) return 1;
+    if ((uint64_t)c->len + n_tokens > c->max_seq) { set_err("capacity exceeded"); return 0; }
+    if (!tg_gpu_kv_append_dev(c->dtype, c->dev, c->max_seq, c->kv_dim, c->len, k_dev, v_dev,
+                              n_tokens, stream)) {
+        set_err("%s", tg_gpu_kv_error());
+        return 0;
+    }
+    c->len += n_tokens;
+    return 1;
+}
+
+int tg_kv_download(const TGKvCache* c, void* dst) {
+    if (!c || !dst) { set_err("null argument"); return 0; }
+    if (!tg_cuda_kv_d2h(dst, c->dev, c->bytes, NULL)) {
+        set_err("%s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    return 1;
+}
+
+/* Make sure the split-sequence scratch of a call fits (grows with slack). */
+static int ensure_attn_scratch(TGBackend* be, const TGCudaAttnCall* call, void** scratch,
+                               uint64_t* scratch_bytes, uint32_t** counters, uint64_t* slots) {
+    const uint64_t need = tg_cuda_kv_attn_scratch_bytes(call);
+    const uint64_t nslots = tg_cuda_kv_attn_counters(call);
+    if (need == 0 || nslots == 0) { set_err("%s", tg_cuda_kv_last_error()); return 0; }
+    if (need > *scratch_bytes) {
+        if (*scratch) be->free(*scratch);
+        const uint64_t want = need + need / 2;
+        *scratch = be->alloc((size_t)want);
+        *scratch_bytes = *scratch ? want : 0;
+        if (!*scratch) { set_err("scratch allocation failed"); return 0; }
+    }
+    if (nslots > *slots) {
+        /* counters must start at zero; the kernel returns them to zero */
+        if (*counters) be->free(*counters);
+        *counters = (uint32_t*)be->alloc((size_t)nslots * 4);
+        *slots = *counters ? nslots : 0;
+        if (!*counters) { set_err("counter allocation failed"); return 0; }
+    }
+    return 1;
+}
+
+int tg_kv_attention(TGKvCache* c, const float* q_dev, float* out_dev, uint32_t n_heads,
+                    uint32_t n_q, void* stream) {
+    if (!c || !q_dev || !out_dev) { set_err("null argument"); return 0; }
+    if (n_q == 0 || n_q > c->len) {
+        set_err("n_q %u must be in [1, len=%u]", n_q, c->len);
+        return 0;
+    }
+    if (n_heads == 0 || n_heads % c->n_kv_heads) {
+        set_err("n_heads %u is not a multiple of n_kv_heads %u", n_heads, c->n_kv_heads);
+        return 0;
+    }
+    if (n_q > c->npos_cap) {
+        uint32_t* np = (uint32_t*)realloc(c->npos, (size_t)n_q * sizeof(uint32_t));
+        if (!np) { set_err("realloc failed"); return 0; }
+        c->npos = np;
+        c->npos_cap = n_q;
+    }
+    for (uint32_t t = 0; t < n_q; t++) c->npos[t] = c->len - n_q + t + 1;
+    TGCudaAttnCall call;
+    memset(&call, 0, sizeof(call));
+    call.dtype = c->dtype;
+    call.n_heads = n_heads;
+    call.n_kv_heads = c->n_kv_heads;
+    call.head_dim = c->head_dim;
+    call.cache.base = (uint64_t)(uintptr_t)c->dev;
+    call.cache.max_seq = c->max_seq;
+    call.n_pos = c->npos;
+    call.n_items = n_q;
+    if (!ensure_attn_scratch(c->be, &call, &c->scratch, &c->scratch_bytes, &c->counters,
+                             &c->counter_slots))
+        return 0;
+    if (!tg_gpu_kv_attention(c->dtype, c->dev, c->max_seq, n_heads, c->n_kv_heads, c->head_dim,
+                             q_dev, out_dev, c->npos, n_q, 1.0f / sqrtf((float)c->head_dim),
+                             c->scratch, c->counters, stream)) {
+        set_err("%s", tg_gpu_kv_error());
+        return 0;
+    }
+    return 1;
+}
+
+/* ---- batched decode ----------------------------------------------------- */
+struct TGKvBatch {
+    uint32_t n, n_heads, n_kv_heads, head_dim, kv_dim;
+    int dtype;
+    TGBackend* be;
+    TGKvCache** caches;
+    TGCudaCacheDesc* table_dev;
+    uint32_t* pos;                    /* host: append position per cache */
+    uint32_t* npos;                   /* host: attended positions per cache */
+    void* scratch;
+    uint64_t scratch_bytes;
+    uint32_t* counters;
+    uint64_t counter_slots;
+    float* io;                        /* device staging for the host-buffer variant */
+    uint64_t io_bytes;
+    uint32_t last_launches;
+};
+
+TGKvBatch* tg_kv_batch_create(TGKvCache* const* caches, uint32_t n, uint32_t n_heads) {
+    if (!caches || n == 0 || n > 1024) { set_err("batch: need 1..1024 caches"); return NULL; }
+    const TGKvCache* c0 = caches[0];
+    if (!c0) { set_err("batch: null cache"); return NULL; }
+    for (uint32_t i = 1; i < n; i++) {
+        const TGKvCache* c = caches[i];
+        if (!c || c->n_kv_heads != c0->n_kv_heads || c->head_dim != c0->head_dim ||
+            c->dtype != c0->dtype) {
+            set_err("batch: cache %u differs in geometry or dtype", i);
+            return NULL;
+        }
+    }
+    if (n_heads == 0 || n_heads % c0->n_kv_heads) {
+        set_err("batch: n_heads %u is not a multiple of n_kv_heads %u", n_heads, c0->n_kv_heads);
+        return NULL;
+    }
+    TGKvBatch* b = (TGKvBatch*)calloc(1, sizeof(TGKvBatch));
+    if (!b) { set_err("calloc failed"); return NULL; }
+    b->n = n;
+    b->n_heads = n_heads;
+    b->n_kv_heads = c0->n_kv_heads;
+    b->head_dim = c0->head_dim;
+    b->kv_dim = c0->kv_dim;
+    b->dtype = c0->dtype;
+    b->be = c0->be;
+    b->caches = (TGKvCache**)malloc(n * sizeof(TGKvCache*));
+    b->pos = (uint32_t*)malloc(n * sizeof(uint32_t));
+    b->npos = (uint32_t*)malloc(n * sizeof(uint32_t));
+    TGCudaCacheDesc* table = (TGCudaCacheDesc*)calloc(n, sizeof(TGCudaCacheDesc));
+    if (!b->caches || !b->pos || !b->npos || !table) {
+        free(table);
+        tg_kv_batch_destroy(b);
+        set_err("malloc failed");
+        return NULL;
+    }
+    for (uint32_t i = 0; i < n; i++) {
+        b->caches[i] = caches[i];
+        table[i].base = (uint64_t)(uintptr_t)caches[i]->dev;
+        table[i].max_seq = caches[i]->max_seq;
+    }
+    b->table_dev = (TGCudaCacheDesc*)b->be->alloc(n * sizeof(TGCudaCacheDesc));
+    if (!b->table_dev || !tg_cuda_kv_h2d(b->table_dev, table, n * sizeof(TGCudaCacheDesc), NULL)) {
+        free(table);
+        tg_kv_batch_destroy(b);
+        set_err("batch: descriptor table upload failed");
+        return NULL;
+    }
+    free(table);
+    return b;
+}
+
+void tg_kv_batch_destroy(TGKvBatch* b) {
+    if (!b) return;
+    if (b->be && b->be->free) {
+        if (b->table_dev) b->be->free(b->table_dev);
+        if (b->scratch) b->be->free(b->scratch);
+        if (b->counters) b->be->free(b->counters);
+        if (b->io) b->be->free(b->io);
+    }
+    free(b->caches);
+    free(b->pos);
+    free(b->npos);
+    free(b);
+}
+
+uint32_t tg_kv_batch_last_launches(const TGKvBatch* b) { return b ? b->last_launches : 0; }
+
+int tg_kv_batch_decode(TGKvBatch* b, const float* q, const float* k_new, const float* v_new,
+                       float* out, void* stream) {
+    if (!b || !q || !k_new || !v_new || !out) { set_err("null argument"); return 0; }
+    b->last_launches = 0;
+    for (uint32_t i = 0; i < b->n; i++) {
+        const TGKvCache* c = b->caches[i];
+        if (c->len >= c->max_seq) { set_err("batch: cache %u is full", i); return 0; }
+        b->pos[i] = c->len;
+        b->npos[i] = c->len + 1;
+    }
+    TGCudaAttnCall call;
+    memset(&call, 0, sizeof(call));
+    call.dtype = b->dtype;
+    call.n_heads = b->n_heads;
+    call.n_kv_heads = b->n_kv_heads;
+    call.head_dim = b->head_dim;
+    call.table_dev = b->table_dev;
+    call.q = q;
+    call.out = out;
+    call.n_pos = b->npos;
+    call.n_items = b->n;
+    call.scale = 1.0f / sqrtf((float)b->head_dim);
+    if (!ensure_attn_scratch(b->be, &call, &b->scratch, &b->scratch_bytes, &b->counters,
+                             &b->counter_slots))
+        return 0;
+    call.scratch = b->scratch;
+    call.counters = b->counters;
+    if (tg_be_current() != &tg_backend_cuda) {
+        set_err("KV-cache path needs the cuda backend; no fallback");
+        return 0;
+    }
+    if (!tg_cuda_kv_append_batch(b->dtype, b->table_dev, b->kv_dim, b->pos, b->n, k_new, v_new,
+                                 stream)) {
+        set_err("%s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    b->last_launches += (b->n + 1023) / 1024;
+    if (!tg_cuda_kv_attention(&call, stream)) {
+        set_err("%s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    b->last_launches += tg_cuda_kv_attn_last_launches();
+    for (uint32_t i = 0; i < b->n; i++) b->caches[i]->len++;
+    return 1;
+}
+
+int tg_kv_batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_host,
+                            const float* v_host, float* out_host, void* stream) {
+    if (!b || !q_host || !k_host || !v_host || !out_host) { set_err("null argument"); return 0; }
+    const uint64_t qb = (uint64_t)b->n * b->n_heads * b->head_dim * 4;
+    const uint64_t kb = (uint64_t)b->n * b->kv_dim * 4;
+    const uint64_t need = 2 * qb + 2 * kb + 64;
+    if (need > b->io_bytes) {
+        if (b->io) b->be->free(b->io);
+        b->io = (float*)b->be->alloc((size_t)need);
+        b->io_bytes = b->io ? need : 0;
+        if (!b->io) { set_err("batch: staging allocation failed"); return 0; }
+    }
+    float* q = b->io;
+    float* o = (float*)((char*)q + qb);
+    float* k = (float*)((char*)o + qb);
+    float* v = (float*)((char*)k + kb);
+    /* the queued copies need a real stream so they stay ordered with the
+     * kernels; NULL means the legacy default stream for both */
+    void* st = stream;
+    int ok;
+    if (st) {
+        ok = tg_cuda_kv_h2d(q, q_host, qb, st) && tg_cuda_kv_h2d(k, k_host, kb, st) &&
+             tg_cuda_kv_h2d(v, v_host, kb, st);
+    } else {
+        ok = tg_cuda_kv_h2d(q, q_host, qb, NULL) && tg_cuda_kv_h2d(k, k_host, kb, NULL) &&
+             tg_cuda_kv_h2d(v, v_host, kb, NULL);
+    }
+    if (!ok) { set_err("%s", tg_cuda_kv_last_error()); return 0; }
+    if (!tg_kv_batch_decode(b, q, k, v, o, st)) return 0;
+    if (!tg_cuda_kv_d2h(out_host, o, qb, st)) { set_err("%s", tg_cuda_kv_last_error()); return 0; }
+    return 1;
+}
