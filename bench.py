@@ -212,7 +212,11 @@ def run_ours(args):
     lib = tgkv.load()
     tgkv.check(lib.tg_cuda_kv_set_device(local), lib, "set_device")
     tgkv.check(lib.tg_be_select(b"cuda"), lib, "tg_be_select")
-    wl = WORKLOADS[args.workload]
+    wl = dict(WORKLOADS[args.workload])
+    if args.seqs:
+        wl["n_seq"] = args.seqs
+    if args.layers:
+        wl["layers"] = args.layers
     heads_sharded = args.workload != "cfg4" and world > 1
     if heads_sharded and wl["nkv"] % world:
         raise SystemExit(f"{wl['nkv']} KV heads do not split over {world} GPUs")
@@ -377,6 +381,7 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong" if heads_sharded else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": args.workload, "desc": wl["desc"],
+                       "layers": layers,
                        "sequences_per_gpu": n_seq if not heads_sharded else n_seq,
                        "kv_heads_per_gpu": nkv, "context_mean": float(lens0.mean()),
                        "l2": "inputs larger than L2 (K/V read per step >> 126 MB)",
@@ -409,6 +414,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
     ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--seqs", type=int, default=0,
+                    help="sequences per GPU (default: the workload's); for small profiling cases")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="layers (default: the workload's); for small profiling cases")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-baseline-s", type=float, default=12.0)

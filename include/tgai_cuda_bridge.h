@@ -60,7 +60,16 @@ typedef struct {
     uint64_t base;
     uint32_t max_seq;
     uint32_t pad;
+    uint64_t tmap;               /* from tg_cuda_kv_tmap_create / _write */
 } TGCudaCacheDesc;
+
+/* TMA tensor map of a cache buffer for the attention kernel, in device memory
+ * (128 bytes).  create: allocates it (free with tg_cuda_kv_free); write:
+ * encodes into existing device memory.  Blocks. */
+void* tg_cuda_kv_tmap_create(int dtype, uint64_t base, uint32_t max_seq, uint32_t n_kv_heads,
+                             uint32_t head_dim);
+int   tg_cuda_kv_tmap_write(int dtype, uint64_t base, uint32_t max_seq, uint32_t n_kv_heads,
+                            uint32_t head_dim, void* tmap_dev);
 
 /* Append rows (fp32 device sources [n_rows][kv_dim]) into one cache starting at
  * row `row0`, storing dtype (0 = fp32, 1 = bf16 round-to-nearest-even). */

@@ -30,15 +30,20 @@ void tg_gpu_kv_stats(uint64_t* calls, uint64_t* ok, uint64_t* fallbacks);
 
 /* Registry of live caches by device address, so that TGBackend.attention
  * given only `kvc` knows the storage type (a bf16 cache reads as bf16). */
-void tg_gpu_kv_register(const void* base, int dtype, uint32_t max_seq);
+void tg_gpu_kv_register(const void* base, int dtype, uint32_t max_seq, uint32_t n_kv_heads,
+                        uint32_t head_dim, const void* tmap);
 void tg_gpu_kv_unregister(const void* base);
 int  tg_gpu_kv_lookup_dtype(const void* base);   /* -1 if not a registered cache */
+/* Tensor map of a registered cache with exactly this geometry, else NULL. */
+const void* tg_gpu_kv_lookup_tmap(const void* base, uint32_t max_seq, uint32_t n_kv_heads,
+                                  uint32_t head_dim);
 
 /* Routed operations (1 = done, 0 = failed; reason in tg_kv_last_error()). */
 int tg_gpu_kv_append_dev(int dtype, void* base, uint32_t max_seq, uint32_t kv_dim,
                          uint32_t row0, const float* k, const float* v, uint32_t n,
                          void* stream);
-int tg_gpu_kv_attention(int dtype, void* base, uint32_t max_seq, uint32_t n_heads,
+int tg_gpu_kv_attention(int dtype, void* base, uint32_t max_seq, const void* tmap,
+                        uint32_t n_heads,
                         uint32_t n_kv_heads, uint32_t head_dim, const float* q, float* out,
                         const uint32_t* n_pos, uint32_t n_items, float scale,
                         void* scratch, uint32_t* counters, void* stream);

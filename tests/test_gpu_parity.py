@@ -331,7 +331,13 @@ def test_cfg5_long_context_131072(cuda, devbuf):
     got = attend(lib, devbuf, c, q[-1:], nh, 1)
     kvc = host_cache(lib, c, 1, L, nkv * hd)
     eng = O.attention_engine(q[-1:], kvc, nh, nkv, hd, 1, L - 1, L, L)
-    assert rel_head_err(got, eng) < 1e-5
+    assert rel_head_err(got, eng) < TOL_BF16
+    # At 131072 positions the engine order's sequential float sums carry
+    # ~1e-5 of rounding themselves; the double-accumulation oracle is the
+    # sharper reference and the split-sequence kernel stays within 1e-5 of it.
+    f64 = O.attention_f64(q[-1:], kvc, nh, nkv, hd, 1, L - 1, L, L)
+    assert rel_head_err(got, f64) < 1e-5
+    assert rel_head_err(eng, f64) < 1e-4
     lib.tg_kv_destroy(c)
 
 

@@ -10,6 +10,7 @@
 #include "tgai_cuda_bridge.h"
 #include "tgkv_launch.h"
 
+#include <cuda.h>                 /* CUtensorMap types; the encoder comes from the runtime */
 #include <cuda_runtime_api.h>
 #include <math.h>
 #include <pthread.h>
@@ -79,6 +80,69 @@ int tg_cuda_kv_init(void) {
     g_ready = 1;
     pthread_mutex_unlock(&g_mu);
     return 1;
+}
+
+/* ---- TMA tensor maps -------------------------------------------------------
+ * cuTensorMapEncodeTiled is reached through cudaGetDriverEntryPoint, so the
+ * library needs no link against libcuda. */
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn g_encode = NULL;
+
+static int encode_tmap(int dtype, uint64_t base, uint32_t max_seq, uint32_t n_kv_heads,
+                       uint32_t head_dim, CUtensorMap* out) {
+    if (!g_encode) {
+        enum cudaDriverEntryPointQueryResult q;
+        void* fn = NULL;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+                cudaSuccess || !fn) {
+            set_err("cuTensorMapEncodeTiled unavailable");
+            return 0;
+        }
+        g_encode = (EncodeTiledFn)fn;
+    }
+    const uint64_t es = dtype == 1 ? 2 : 4;
+    const uint64_t kv_dim = (uint64_t)n_kv_heads * head_dim;
+    if ((base & 15u) || (kv_dim * es) % 16 || (head_dim * es) % 16 || head_dim > 256) {
+        set_err("tensor map: cache layout not TMA-compatible (head_dim %u)", head_dim);
+        return 0;
+    }
+    cuuint64_t dims[3] = {kv_dim, max_seq, 2};
+    cuuint64_t strides[2] = {kv_dim * es, (uint64_t)max_seq * kv_dim * es};
+    cuuint32_t box[3] = {head_dim, TGKV_TILE, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(out, dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                          3, (void*)(uintptr_t)base, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_err("cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return 0;
+    }
+    return 1;
+}
+
+int tg_cuda_kv_tmap_write(int dtype, uint64_t base, uint32_t max_seq, uint32_t n_kv_heads,
+                          uint32_t head_dim, void* tmap_dev) {
+    if (!g_ready && !tg_cuda_kv_init()) return 0;
+    if (!tmap_dev || ((uintptr_t)tmap_dev & 63u)) { set_err("tensor map: bad destination"); return 0; }
+    CUtensorMap m;
+    if (!encode_tmap(dtype, base, max_seq, n_kv_heads, head_dim, &m)) return 0;
+    return cuda_ok(cudaMemcpy(tmap_dev, &m, sizeof(m), cudaMemcpyHostToDevice), "tensor map h2d");
+}
+
+void* tg_cuda_kv_tmap_create(int dtype, uint64_t base, uint32_t max_seq, uint32_t n_kv_heads,
+                             uint32_t head_dim) {
+    void* d = tg_cuda_kv_malloc(sizeof(CUtensorMap));
+    if (!d) return NULL;
+    if (!tg_cuda_kv_tmap_write(dtype, base, max_seq, n_kv_heads, head_dim, d)) {
+        tg_cuda_kv_free(d);
+        return NULL;
+    }
+    return d;
 }
 
 int tg_cuda_kv_set_device(int device) {
@@ -308,7 +372,7 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
     AttnPlan pl;
     if (!plan_attention(c, &pl)) return 0;
     if (c->n_items == 0) return 1;
-    if (!c->q || !c->out || (!c->table_dev && !c->cache.base)) {
+    if (!c->q || !c->out || (!c->table_dev && (!c->cache.base || !c->cache.tmap))) {
         set_err("attention: NULL pointer");
         return 0;
     }
@@ -330,6 +394,7 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         p.caches = (const TGKvCacheDesc*)(c->table_dev ? c->table_dev + b0 : NULL);
         p.cache0.base = c->cache.base;
         p.cache0.max_seq = c->cache.max_seq;
+        p.cache0.tmap = c->cache.tmap;
         p.q = c->q;
         p.out = c->out;
         p.part_o = (float*)c->scratch;

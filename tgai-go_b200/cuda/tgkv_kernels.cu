@@ -84,14 +84,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
-// Bulk async copy global -> shared, completion counted on `bar` in bytes.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
-                                         uint64_t* bar) {
+// Tiled TMA load of one box of a 3-D tensor map into shared memory.
+__device__ __forceinline__ void tma_load_3d(void* dst, uint64_t tmap, int x, int y, int z,
+                                            uint64_t* bar) {
     asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-            "r"(smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
         : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(uint64_t tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
@@ -247,11 +251,6 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
     const uint32_t head0 = kvh * group + sub * GT;
 
     const TGKvCacheDesc cd = p.caches ? p.caches[item * p.cache_stride] : p.cache0;
-    const uint64_t kv_dim = (uint64_t)p.n_kv_heads * HD;
-    const unsigned char* kbase =
-        reinterpret_cast<const unsigned char*>(cd.base) + (uint64_t)kvh * C::RB;
-    const unsigned char* vbase = kbase + (uint64_t)cd.max_seq * kv_dim * C::ES;
-    const uint64_t rstride = kv_dim * C::ES;
 
     if (tid == 0) {
         for (int s = 0; s < C::NSTAGE; ++s) {
@@ -265,27 +264,23 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
     __syncthreads();
 
     if (warp == kConsumerWarps) {
-        // ---------------- producer: bulk copies of K and V rows into the ring
-        for (int t = 0; t < ntiles; ++t) {
-            const int s = t % C::NSTAGE;
-            if (t >= C::NSTAGE) {
-                bool ok = true;
-                if (lane == 0) ok = mbar_wait(&empty[s], ((t / C::NSTAGE) - 1) & 1);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok) {
-                    if (lane == 0) { atomicExch(p.err, kErrEmptyTimeout); sm_flag[0] = 1; }
+        // ---------------- producer: one tiled TMA box of K and one of V per
+        // stage (kTile rows of this KV head; rows past max_seq arrive as 0)
+        if (lane == 0) {
+            prefetch_tmap(cd.tmap);
+            const int x = (int)(kvh * HD);
+            for (int t = 0; t < ntiles; ++t) {
+                const int s = t % C::NSTAGE;
+                if (t >= C::NSTAGE && !mbar_wait(&empty[s], ((t / C::NSTAGE) - 1) & 1)) {
+                    atomicExch(p.err, kErrEmptyTimeout);
+                    sm_flag[0] = 1;
                     break;
                 }
-            }
-            const uint32_t row0 = c0 + (uint32_t)t * kTile;
-            const int nv = (int)min((uint32_t)kTile, c1 - row0);
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * nv * C::RB));
-            __syncwarp();
-            if (lane < nv) {
+                const int row0 = (int)(c0 + (uint32_t)t * kTile);
                 unsigned char* st = smem + s * C::STAGE;
-                const uint64_t off = (uint64_t)(row0 + lane) * rstride;
-                bulk_g2s(st + lane * C::RB, kbase + off, C::RB, &full[s]);
-                bulk_g2s(st + kTile * C::RB + lane * C::RB, vbase + off, C::RB, &full[s]);
+                mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * kTile * C::RB));
+                tma_load_3d(st, cd.tmap, x, row0, 0, &full[s]);
+                tma_load_3d(st + kTile * C::RB, cd.tmap, x, row0, 1, &full[s]);
             }
         }
         return;
@@ -589,10 +584,12 @@ int launch_attn(const TGKvAttnParams* p, uint32_t grid, cudaStream_t st) {
 }  // namespace tgkv
 
 extern "C" uint32_t tgkv_attention_g_tile(uint32_t head_dim, uint32_t group) {
+    // Largest of 4, 2, 1 that divides the group and fits the register budget
+    // (query and output slices of GT heads per lane).
     const uint32_t cap = head_dim >= 256 ? 2u : 4u;
-    uint32_t gt = group < cap ? group : cap;
-    while (gt > 1 && group % gt) --gt;
-    return gt;
+    for (uint32_t gt = cap; gt > 1; gt >>= 1)
+        if (group % gt == 0) return gt;
+    return 1u;
 }
 
 extern "C" int tgkv_attention_supported(int dtype, uint32_t head_dim) {

@@ -17,11 +17,14 @@ extern "C" {
 #define TGKV_MAX_ITEMS 1024      /* items (query rows / caches) per launch */
 #define TGKV_TILE      32        /* positions per pipeline stage */
 
-/* One cache buffer [2][max_seq][kv_dim] in device memory. */
+/* One cache buffer [2][max_seq][kv_dim] in device memory, with the device
+ * address of its TMA tensor map: a 3-D map over (kv_dim, max_seq, 2) whose box
+ * is (head_dim, TGKV_TILE, 1) -- one KV head's rows of one tile of K or V. */
 typedef struct {
     uint64_t base;               /* device address */
     uint32_t max_seq;
     uint32_t pad;
+    uint64_t tmap;               /* device address of a 64-byte aligned CUtensorMap */
 } TGKvCacheDesc;
 
 /* Split-sequence decode attention.

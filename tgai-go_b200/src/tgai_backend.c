@@ -65,6 +65,7 @@ static void* g_scratch = NULL;
 static uint64_t g_scratch_bytes = 0;
 static uint32_t* g_counters = NULL;
 static uint64_t g_counter_slots = 0;
+static void* g_tmap = NULL;            /* tensor map for caller-owned cache buffers */
 
 static int cu_attention(void* q, void* kvc, void* out, uint32_t nh, uint32_t nkvh, uint32_t hd,
                         uint32_t n_kv, uint32_t pos, uint32_t max_seq) {
@@ -77,6 +78,17 @@ static int cu_attention(void* q, void* kvc, void* out, uint32_t nh, uint32_t nkv
     int dtype = tg_gpu_kv_lookup_dtype(kvc);
     if (dtype < 0) dtype = 0;
     pthread_mutex_lock(&g_attn_mu);
+    const void* tmap = tg_gpu_kv_lookup_tmap(kvc, max_seq, nkvh, hd);
+    if (!tmap) {                     /* a buffer this library did not create */
+        if (!g_tmap) g_tmap = tg_cuda_kv_malloc(128);
+        if (!g_tmap || !tg_cuda_kv_tmap_write(dtype, (uint64_t)(uintptr_t)kvc, max_seq, nkvh, hd,
+                                              g_tmap)) {
+            snprintf(g_cuda_err, sizeof(g_cuda_err), "%s", tg_cuda_kv_last_error());
+            pthread_mutex_unlock(&g_attn_mu);
+            return 0;
+        }
+        tmap = g_tmap;
+    }
     TGCudaAttnCall c;
     memset(&c, 0, sizeof(c));
     c.dtype = dtype;
@@ -85,6 +97,7 @@ static int cu_attention(void* q, void* kvc, void* out, uint32_t nh, uint32_t nkv
     c.head_dim = hd;
     c.cache.base = (uint64_t)(uintptr_t)kvc;
     c.cache.max_seq = max_seq;
+    c.cache.tmap = (uint64_t)(uintptr_t)tmap;
     c.q = (const float*)q;
     c.out = (float*)out;
     c.n_pos = &n;
@@ -106,7 +119,8 @@ static int cu_attention(void* q, void* kvc, void* out, uint32_t nh, uint32_t nkv
         ok = g_counters != NULL;
     }
     if (ok)
-        ok = tg_gpu_kv_attention(dtype, kvc, max_seq, nh, nkvh, hd, c.q, c.out, &n, 1, c.scale,
+        ok = tg_gpu_kv_attention(dtype, kvc, max_seq, tmap, nh, nkvh, hd, c.q, c.out, &n, 1,
+                                 c.scale,
                                  g_scratch, g_counters, NULL) &&
              tg_cuda_kv_sync(NULL);
     if (!ok) snprintf(g_cuda_err, sizeof(g_cuda_err), "%s", tg_gpu_kv_error());

@@ -62,11 +62,17 @@ void tg_gpu_kv_stats(uint64_t* calls, uint64_t* ok, uint64_t* fallbacks) {
 }
 
 /* ---- cache registry (small open list; caches are few and long-lived) ---- */
-typedef struct { const void* base; int dtype; uint32_t max_seq; } RegEntry;
+typedef struct {
+    const void* base;
+    int dtype;
+    uint32_t max_seq, n_kv_heads, head_dim;
+    const void* tmap;
+} RegEntry;
 static RegEntry* g_reg = NULL;
 static size_t g_reg_n = 0, g_reg_cap = 0;
 
-void tg_gpu_kv_register(const void* base, int dtype, uint32_t max_seq) {
+void tg_gpu_kv_register(const void* base, int dtype, uint32_t max_seq, uint32_t n_kv_heads,
+                        uint32_t head_dim, const void* tmap) {
     pthread_mutex_lock(&g_mu);
     if (g_reg_n == g_reg_cap) {
         size_t nc = g_reg_cap ? g_reg_cap * 2 : 64;
@@ -78,6 +84,9 @@ void tg_gpu_kv_register(const void* base, int dtype, uint32_t max_seq) {
     g_reg[g_reg_n].base = base;
     g_reg[g_reg_n].dtype = dtype;
     g_reg[g_reg_n].max_seq = max_seq;
+    g_reg[g_reg_n].n_kv_heads = n_kv_heads;
+    g_reg[g_reg_n].head_dim = head_dim;
+    g_reg[g_reg_n].tmap = tmap;
     g_reg_n++;
     pthread_mutex_unlock(&g_mu);
 }
@@ -96,6 +105,20 @@ int tg_gpu_kv_lookup_dtype(const void* base) {
         if (g_reg[i].base == base) { d = g_reg[i].dtype; break; }
     pthread_mutex_unlock(&g_mu);
     return d;
+}
+
+const void* tg_gpu_kv_lookup_tmap(const void* base, uint32_t max_seq, uint32_t n_kv_heads,
+                                  uint32_t head_dim) {
+    const void* t = NULL;
+    pthread_mutex_lock(&g_mu);
+    for (size_t i = 0; i < g_reg_n; i++)
+        if (g_reg[i].base == base && g_reg[i].max_seq == max_seq &&
+            g_reg[i].n_kv_heads == n_kv_heads && g_reg[i].head_dim == head_dim) {
+            t = g_reg[i].tmap;
+            break;
+        }
+    pthread_mutex_unlock(&g_mu);
+    return t;
 }
 
 /* ---- routing ------------------------------------------------------------ */
@@ -126,11 +149,12 @@ int tg_gpu_kv_append_dev(int dtype, void* base, uint32_t max_seq, uint32_t kv_di
                          uint32_t row0, const float* k, const float* v, uint32_t n,
                          void* stream) {
     if (!route_begin()) return 0;
-    TGCudaCacheDesc d = {(uint64_t)(uintptr_t)base, max_seq, 0};
+    TGCudaCacheDesc d = {(uint64_t)(uintptr_t)base, max_seq, 0, 0};
     return route_end(tg_cuda_kv_append(dtype, d, kv_dim, row0, k, v, n, stream));
 }
 
-int tg_gpu_kv_attention(int dtype, void* base, uint32_t max_seq, uint32_t n_heads,
+int tg_gpu_kv_attention(int dtype, void* base, uint32_t max_seq, const void* tmap,
+                        uint32_t n_heads,
                         uint32_t n_kv_heads, uint32_t head_dim, const float* q, float* out,
                         const uint32_t* n_pos, uint32_t n_items, float scale,
                         void* scratch, uint32_t* counters, void* stream) {
@@ -143,6 +167,7 @@ int tg_gpu_kv_attention(int dtype, void* base, uint32_t max_seq, uint32_t n_head
     c.head_dim = head_dim;
     c.cache.base = (uint64_t)(uintptr_t)base;
     c.cache.max_seq = max_seq;
+    c.cache.tmap = (uint64_t)(uintptr_t)tmap;
     c.q = q;
     c.out = out;
     c.n_pos = n_pos;

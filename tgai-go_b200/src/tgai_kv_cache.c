@@ -33,6 +33,7 @@ struct TGKvCache {
     uint64_t counter_slots;
     float*   staging;             /* device staging of host rows (bf16 append) */
     size_t   staging_bytes;
+    void*    tmap;                /* TMA tensor map of dev (NULL: no attention kernel) */
     uint32_t* npos;               /* host item table for attention */
     uint32_t npos_cap;
 };
@@ -86,7 +87,17 @@ TGKvCache* tg_kv_create_ex(uint32_t max_seq, uint32_t n_kv_heads, uint32_t head_
         return NULL;
     }
     c->host = (float*)(b->map ? b->map(c->dev) : NULL);
-    tg_gpu_kv_register(c->dev, dtype, max_seq);
+    if (tg_cuda_kv_attn_supported(dtype, head_dim)) {
+        c->tmap = tg_cuda_kv_tmap_create(dtype, (uint64_t)(uintptr_t)c->dev, max_seq, n_kv_heads,
+                                         head_dim);
+        if (!c->tmap) {
+            set_err("tensor map: %s", tg_cuda_kv_last_error());
+            b->free(c->dev);
+            free(c);
+            return NULL;
+        }
+    }
+    tg_gpu_kv_register(c->dev, dtype, max_seq, n_kv_heads, head_dim, c->tmap);
     return c;
 }
 
@@ -104,6 +115,7 @@ void tg_kv_destroy(TGKvCache* c) {
         if (c->counters) b->free(c->counters);
         if (c->staging) b->free(c->staging);
     }
+    if (c->tmap) tg_cuda_kv_free(c->tmap);
     free(c->npos);
     free(c);
 }
@@ -256,12 +268,18 @@ int tg_kv_attention(TGKvCache* c, const float* q_dev, float* out_dev, uint32_t n
     call.head_dim = c->head_dim;
     call.cache.base = (uint64_t)(uintptr_t)c->dev;
     call.cache.max_seq = c->max_seq;
+    call.cache.tmap = (uint64_t)(uintptr_t)c->tmap;
     call.n_pos = c->npos;
     call.n_items = n_q;
     if (!ensure_attn_scratch(c->be, &call, &c->scratch, &c->scratch_bytes, &c->counters,
                              &c->counter_slots))
         return 0;
-    if (!tg_gpu_kv_attention(c->dtype, c->dev, c->max_seq, n_heads, c->n_kv_heads, c->head_dim,
+    if (!c->tmap) {
+        set_err("attention: no kernel for dtype %d head_dim %u", c->dtype, c->head_dim);
+        return 0;
+    }
+    if (!tg_gpu_kv_attention(c->dtype, c->dev, c->max_seq, c->tmap, n_heads, c->n_kv_heads,
+                             c->head_dim,
                              q_dev, out_dev, c->npos, n_q, 1.0f / sqrtf((float)c->head_dim),
                              c->scratch, c->counters, stream)) {
         set_err("%s", tg_gpu_kv_error());
@@ -304,6 +322,12 @@ TGKvBatch* tg_kv_batch_create(TGKvCache* const* caches, uint32_t n, uint32_t n_h
         set_err("batch: n_heads %u is not a multiple of n_kv_heads %u", n_heads, c0->n_kv_heads);
         return NULL;
     }
+    for (uint32_t i = 0; i < n; i++)
+        if (!caches[i]->tmap) {
+            set_err("batch: no attention kernel for dtype %d head_dim %u", c0->dtype,
+                    c0->head_dim);
+            return NULL;
+        }
     TGKvBatch* b = (TGKvBatch*)calloc(1, sizeof(TGKvBatch));
     if (!b) { set_err("calloc failed"); return NULL; }
     b->n = n;
@@ -327,6 +351,7 @@ TGKvBatch* tg_kv_batch_create(TGKvCache* const* caches, uint32_t n, uint32_t n_h
         b->caches[i] = caches[i];
         table[i].base = (uint64_t)(uintptr_t)caches[i]->dev;
         table[i].max_seq = caches[i]->max_seq;
+        table[i].tmap = (uint64_t)(uintptr_t)caches[i]->tmap;
     }
     b->table_dev = (TGCudaCacheDesc*)b->be->alloc(n * sizeof(TGCudaCacheDesc));
     if (!b->table_dev || !tg_cuda_kv_h2d(b->table_dev, table, n * sizeof(TGCudaCacheDesc), NULL)) {

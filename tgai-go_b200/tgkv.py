@@ -28,7 +28,7 @@ class TGBackendInfo(C.Structure):
 
 
 class TGCudaCacheDesc(C.Structure):
-    _fields_ = [("base", u64), ("max_seq", u32), ("pad", u32)]
+    _fields_ = [("base", u64), ("max_seq", u32), ("pad", u32), ("tmap", u64)]
 
 
 # struct TGBackend of include/tgai_backend.h (src/tgai_backend.h:55-94 order)
@@ -98,12 +98,13 @@ PROTOS = {
     "tg_gpu_backend_device": (cp, []),
     "tg_gpu_backend_shutdown": (None, []),
     "tg_gpu_kv_stats": (None, [C.POINTER(u64), C.POINTER(u64), C.POINTER(u64)]),
-    "tg_gpu_kv_register": (None, [vp, i32, u32]),
+    "tg_gpu_kv_register": (None, [vp, i32, u32, u32, u32, vp]),
+    "tg_gpu_kv_lookup_tmap": (vp, [vp, u32, u32, u32]),
     "tg_gpu_kv_unregister": (None, [vp]),
     "tg_gpu_kv_lookup_dtype": (i32, [vp]),
     "tg_gpu_kv_append_dev": (i32, [i32, vp, u32, u32, u32, vp, vp, u32, vp]),
-    "tg_gpu_kv_attention": (i32, [i32, vp, u32, u32, u32, u32, vp, vp, PU32, u32, fp, vp,
-                                  vp, vp]),
+    "tg_gpu_kv_attention": (i32, [i32, vp, u32, vp, u32, u32, u32, vp, vp, PU32, u32, fp,
+                                  vp, vp, vp]),
     "tg_gpu_kv_error": (cp, []),
     # tgai_cuda_bridge.h
     "tg_cuda_kv_init": (i32, []),
@@ -122,6 +123,8 @@ PROTOS = {
     "tg_cuda_kv_sync": (i32, [vp]),
     "tg_cuda_kv_device_error": (i32, []),
     "tg_cuda_kv_inject_alloc_failures": (None, [i32]),
+    "tg_cuda_kv_tmap_create": (vp, [i32, u64, u32, u32, u32]),
+    "tg_cuda_kv_tmap_write": (i32, [i32, u64, u32, u32, u32, vp]),
     "tg_cuda_kv_append": (i32, [i32, TGCudaCacheDesc, u32, u32, vp, vp, u32, vp]),
     "tg_cuda_kv_append_batch": (i32, [i32, vp, u32, PU32, u32, vp, vp, vp]),
     "tg_cuda_kv_attn_supported": (i32, [i32, u32]),
