@@ -106,6 +106,27 @@ int tg_kv_attention(TGKvCache* c, const float* q_dev, float* out_dev,
 uint64_t tg_kv_bytes(const TGKvCache* c);
 int      tg_kv_download(const TGKvCache* c, void* dst);
 
+/* Attention without any allocation.  No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory at this point: code running
+ * inside a host allocator hook or under a fixed device-memory budget, or an
+ * engine that owns every buffer itself and hands this library only raw
+ * addresses.  Same semantics as tg_kv_attention over a caller-owned cache
+ * buffer `kvc` ([2][max_seq][n_kv_heads*head_dim], dtype TG_KV_F32/BF16) whose
+ * first kv_len rows are valid: the last n_q positions' queries (q, out: fp32
+ * [n_q][n_heads][head_dim], device) attend causally; async on `stream`.
+ *
+ * Scratch comes from a static 8 MiB device array inside the library, which
+ * every GPU that loads the library keeps until exit; calls that need more are
+ * rejected (return 0, reason in tg_kv_last_error()), as are n_q > 1024.  The
+ * function calls no cudaMalloc/cudaFree.  The first call on each device does a
+ * one-time set-up (the array's device address) and should come before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU
+ * (other streams, other threads) race; order them on one stream. */
+int tg_kv_attention_static(const void* kvc, int dtype, uint32_t max_seq, uint32_t n_kv_heads,
+                           uint32_t head_dim, uint32_t kv_len, const float* q, float* out,
+                           uint32_t n_heads, uint32_t n_q, void* stream);
+
 /* ---- Batched decode over many caches (one layer of many sequences) ------- */
 
 typedef struct TGKvBatch TGKvBatch;

@@ -19,9 +19,16 @@
 // Every wait on an mbarrier is bounded by %globaltimer; on expiry the kernel
 // records an error code in p.err and returns instead of spinning.
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <math.h>
+#include <stdarg.h>
 #include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <mutex>
 #include "tgkv_launch.h"
 
 namespace tgkv {
@@ -637,4 +644,189 @@ extern "C" int tgkv_launch_rope_append(const TGKvRopeParams* p, void* stream) {
     else
         tgkv::rope_append_kernel<1><<<grid, 256, 0, (cudaStream_t)stream>>>(*p);
     return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------ no-allocation
+// tg_kv_attention_static: the split-sequence attention for callers that may
+// not allocate device memory -- code running where cudaMalloc is off limits
+// (inside a host allocator hook, a real-time decode thread with a fixed memory
+// budget, or an engine that hands this library only its own buffers).  Its
+// scratch (the CTA partials, the arrival counters, the cache's TMA tensor map
+// and an error word) lives in the file-scope device array below: 8 MiB that
+// every GPU which loads this library holds until the process exits.
+extern "C" void tgkv_set_last_error(const char* msg);   // tgai_kv_cache.c
+
+namespace tgkv {
+namespace staticmem {
+
+constexpr size_t kBytes = 8u << 20;
+constexpr size_t kOffTmap = 0;        // 128-byte CUtensorMap
+constexpr size_t kOffErr = 128;       // bounded-wait error word
+constexpr size_t kOffCounters = 256;  // arrival counters, then partials
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_scratch[kBytes];
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+std::mutex g_mu;
+unsigned char* g_addr[kMaxDevices];   // device address of g_scratch, per device
+int g_sms[kMaxDevices];
+EncodeTiledFn g_encode = nullptr;
+
+int fail(const char* fmt, ...) {
+    char msg[256];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(msg, sizeof(msg), fmt, ap);
+    va_end(ap);
+    tgkv_set_last_error(msg);
+    return 0;
+}
+
+// Per-device set-up on the first call made with that device current: the
+// array's device address (host code only sees a stand-in symbol) and the SM
+// count used by the split planner.
+bool setup(int dev) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_addr[dev]) return true;
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_scratch);
+    if (e != cudaSuccess || !ptr) {
+        fail("tg_kv_attention_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+        return false;
+    }
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) {
+        fail("tg_kv_attention_static: SM count query failed: %s", cudaGetErrorString(e));
+        return false;
+    }
+    if (!g_encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+                cudaSuccess || !fn) {
+            fail("tg_kv_attention_static: cuTensorMapEncodeTiled unavailable");
+            return false;
+        }
+        g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+    g_sms[dev] = sms;
+    g_addr[dev] = static_cast<unsigned char*>(ptr);
+    return true;
+}
+
+}  // namespace staticmem
+}  // namespace tgkv
+
+extern "C" __attribute__((visibility("default"))) int tg_kv_attention_static(
+    const void* kvc, int dtype, uint32_t max_seq, uint32_t n_kv_heads, uint32_t head_dim,
+    uint32_t kv_len, const float* q, float* out, uint32_t n_heads, uint32_t n_q, void* stream) {
+    using namespace tgkv::staticmem;
+    if (!kvc || !q || !out) return fail("tg_kv_attention_static: null pointer");
+    if (!tgkv_attention_supported(dtype, head_dim))
+        return fail("tg_kv_attention_static: no kernel for dtype %d head_dim %u", dtype, head_dim);
+    if (n_kv_heads == 0 || n_heads == 0 || n_heads % n_kv_heads)
+        return fail("tg_kv_attention_static: n_heads %u is not a multiple of n_kv_heads %u",
+                    n_heads, n_kv_heads);
+    if (kv_len > max_seq || n_q == 0 || n_q > kv_len)
+        return fail("tg_kv_attention_static: need 1 <= n_q (%u) <= kv_len (%u) <= max_seq (%u)",
+                    n_q, kv_len, max_seq);
+    if (n_q > TGKV_MAX_ITEMS)
+        return fail("tg_kv_attention_static: n_q %u above the limit of %u query rows", n_q,
+                    (unsigned)TGKV_MAX_ITEMS);
+    const uint64_t es = dtype == 1 ? 2 : 4;
+    const uint64_t kv_dim = (uint64_t)n_kv_heads * head_dim;
+    if (((uintptr_t)kvc & 15u) || (((uintptr_t)q | (uintptr_t)out) & 7u))
+        return fail("tg_kv_attention_static: kvc must be 16-byte and q/out 8-byte aligned");
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+        return fail("tg_kv_attention_static: no usable current device");
+    if (!setup(dev)) return 0;
+
+    // Split plan: the rule tg_cuda_kv_attention uses (about eight waves of two
+    // CTAs per SM, chunks of at least 128 positions, TGKV_CHUNK overrides).
+    const uint32_t group = n_heads / n_kv_heads;
+    const uint32_t gt = tgkv_attention_g_tile(head_dim, group);
+    const uint32_t n_sub = group / gt;
+    uint64_t total = 0;
+    for (uint32_t t = 0; t < n_q; ++t) total += (uint64_t)(kv_len - n_q + t + 1) * n_kv_heads * n_sub;
+    uint32_t chunk;
+    const char* ce = getenv("TGKV_CHUNK");
+    if (ce && ce[0] && atol(ce) >= TGKV_TILE) {
+        chunk = (uint32_t)((atol(ce) + TGKV_TILE - 1) / TGKV_TILE * TGKV_TILE);
+    } else {
+        const uint64_t target = (uint64_t)g_sms[dev] * 2 * 8;
+        uint64_t c = (total + target - 1) / target;
+        if (c < 128) c = 128;
+        if (c > (1u << 30)) c = 1u << 30;
+        chunk = (uint32_t)((c + TGKV_TILE - 1) / TGKV_TILE * TGKV_TILE);
+    }
+    TGKvAttnParams p;                     // ~8 KB on the stack: no heap, no device memory
+    memset(&p, 0, offsetof(TGKvAttnParams, n_pos));
+    uint64_t ctas = 0;
+    for (uint32_t t = 0; t < n_q; ++t) {
+        const uint32_t np = kv_len - n_q + t + 1;
+        p.n_pos[t] = np;
+        p.cta_prefix[t] = (uint32_t)ctas;
+        ctas += (uint64_t)((np + chunk - 1) / chunk) * n_kv_heads * n_sub;
+    }
+    p.cta_prefix[n_q] = (uint32_t)ctas;
+    const uint64_t counters = ((uint64_t)n_q * n_kv_heads * n_sub * 4 + 255) / 256 * 256;
+    const uint64_t part_o = (ctas * gt * head_dim * 4 + 255) / 256 * 256;
+    const uint64_t need = kOffCounters + counters + part_o + ctas * gt * 2 * 4;
+    if (need > kBytes)
+        return fail("tg_kv_attention_static: needs %llu bytes of scratch, above the static "
+                    "limit of %llu bytes (8 MiB); use tg_kv_attention or fewer query rows",
+                    (unsigned long long)need, (unsigned long long)kBytes);
+
+    // The cache's tensor map goes into the static array on the stream, ahead
+    // of the kernel; the counters and the error word are cleared the same way
+    // (the previous call's contents are still there).
+    CUtensorMap tm;
+    cuuint64_t dims[3] = {kv_dim, max_seq, 2};
+    cuuint64_t strides[2] = {kv_dim * es, (uint64_t)max_seq * kv_dim * es};
+    cuuint32_t box[3] = {head_dim, TGKV_TILE, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(&tm, dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                          3, const_cast<void*>(kvc), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail("tg_kv_attention_static: cuTensorMapEncodeTiled failed (%d)", (int)r);
+    unsigned char* base = g_addr[dev];
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e = cudaMemcpyAsync(base + kOffTmap, &tm, sizeof(tm), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(base + kOffErr, 0, kOffCounters - kOffErr + counters, st);
+    if (e != cudaSuccess)
+        return fail("tg_kv_attention_static: staging failed: %s", cudaGetErrorString(e));
+
+    p.caches = nullptr;
+    p.cache0.base = (uint64_t)(uintptr_t)kvc;
+    p.cache0.max_seq = max_seq;
+    p.cache0.tmap = (uint64_t)(uintptr_t)(base + kOffTmap);
+    p.q = q;
+    p.out = out;
+    p.counters = reinterpret_cast<uint32_t*>(base + kOffCounters);
+    p.part_o = reinterpret_cast<float*>(base + kOffCounters + counters);
+    p.part_ml = reinterpret_cast<float*>(base + kOffCounters + counters + part_o);
+    p.err = reinterpret_cast<int32_t*>(base + kOffErr);
+    p.cache_stride = 0;
+    p.n_items = n_q;
+    p.n_heads = n_heads;
+    p.n_kv_heads = n_kv_heads;
+    p.n_sub = n_sub;
+    p.chunk = chunk;
+    p.qscale = (1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
+    p.item_base = 0;
+    const int rc = tgkv_launch_attention(&p, dtype, head_dim, gt, (uint32_t)ctas, stream);
+    if (rc != 0)
+        return fail("tg_kv_attention_static: launch failed: %s",
+                    cudaGetErrorString((cudaError_t)rc));
+    return 1;
 }

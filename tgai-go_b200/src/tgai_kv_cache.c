@@ -49,6 +49,12 @@ static void set_err(const char* fmt, ...) {
 
 const char* tg_kv_last_error(void) { return t_err; }
 
+/* Lets the allocation-free attention entry point in tgkv_kernels.cu report
+ * through tg_kv_last_error(); not exported. */
+__attribute__((visibility("hidden"))) void tgkv_set_last_error(const char* msg) {
+    set_err("%s", msg ? msg : "unknown");
+}
+
 TGKvCache* tg_kv_create_ex(uint32_t max_seq, uint32_t n_kv_heads, uint32_t head_dim, int dtype) {
     if (max_seq == 0 || n_kv_heads == 0 || head_dim == 0) {
         set_err("invalid argument (0)");
