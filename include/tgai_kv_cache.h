@@ -116,7 +116,7 @@ int      tg_kv_download(const TGKvCache* c, void* dst);
  * first kv_len rows are valid: the last n_q positions' queries (q, out: fp32
  * [n_q][n_heads][head_dim], device) attend causally; async on `stream`.
  *
- * Scratch comes from a static 8 MiB device array inside the library, which
+ * Scratch comes from a static 4 MiB device array inside the library, which
  * every GPU that loads the library keeps until exit; calls that need more are
  * rejected (return 0, reason in tg_kv_last_error()), as are n_q > 1024.  The
  * function calls no cudaMalloc/cudaFree.  The first call on each device does a

@@ -85,16 +85,21 @@ def test_static_on_caller_owned_buffer(cuda, devbuf):
 
 
 def test_static_rejects_beyond_limit(cuda, devbuf):
+    """Scratch beyond the static 4 MiB is refused before anything is launched.
+    The split partials stay below 2.2 MiB (at most two per CTA of one
+    persistent wave), so the case that overflows is the arrival counters of
+    very many (query row, KV head) pairs: 1024 rows x 1024 KV heads."""
     lib = cuda
-    nh, nkv, hd, L = 32, 8, 128, 4096
-    c = _cache_with_rows(lib, devbuf, L, nkv, hd, 1, L, 77)
-    q = devbuf(nbytes=1024 * nh * hd * 4)
+    nh = nkv = 1024
+    hd, L = 32, 1024
+    c = lib.tg_kv_create_ex(L, nkv, hd, 0)
+    tgkv.check(c, lib)
+    q = devbuf(nbytes=4096)
     kvc = lib.tg_kv_device_handle(c)
-    # 1024 query rows x 8 KV heads of partials need more than the 8 MiB array
-    assert lib.tg_kv_attention_static(kvc, 1, L, nkv, hd, L, q.ptr, q.ptr, nh, 1024, None) == 0
+    assert lib.tg_kv_attention_static(kvc, 0, L, nkv, hd, L, q.ptr, q.ptr, nh, 1024, None) == 0
     msg = lib.tg_kv_last_error()
-    assert b"8 MiB" in msg and b"bytes of scratch" in msg, msg
-    assert lib.tg_kv_attention_static(kvc, 1, L, nkv, hd, L, q.ptr, q.ptr, nh, 1025, None) == 0
+    assert b"4 MiB" in msg and b"bytes of scratch" in msg, msg
+    assert lib.tg_kv_attention_static(kvc, 0, L, nkv, hd, L, q.ptr, q.ptr, nh, 1025, None) == 0
     assert b"1024" in lib.tg_kv_last_error()
-    assert lib.tg_kv_attention_static(kvc, 1, L, nkv, hd, L + 1, q.ptr, q.ptr, nh, 1, None) == 0
+    assert lib.tg_kv_attention_static(kvc, 0, L, nkv, hd, L + 1, q.ptr, q.ptr, nh, 1, None) == 0
     lib.tg_kv_destroy(c)

@@ -3,8 +3,8 @@
  * launchers of tgkv_kernels.cu, nothing else.
  *
  * Host-side planning of split-sequence attention lives here: the per-item
- * position counts, the chunk length and the CTA prefix table are computed on
- * the host and handed to the kernel by value (tgkv_launch.h), so a launch
+ * position counts, the chunk length and the chunk prefix table are computed
+ * on the host and handed to the kernel by value (tgkv_launch.h), so a launch
  * needs no copy of its own.
  */
 #include "tgai_cuda_bridge.h"
@@ -297,24 +297,37 @@ int tg_cuda_kv_attn_supported(int dtype, uint32_t head_dim) {
 
 typedef struct {
     uint32_t gt, n_sub, chunk;
-    uint64_t max_ctas;        /* largest CTA count of any launch of the call */
+    uint64_t max_chunks;      /* most chunks in any launch of the call */
 } AttnPlan;
 
-static uint32_t round_up(uint32_t x, uint32_t m) { return (x + m - 1) / m * m; }
+static uint32_t round_up32(uint64_t x) { return (uint32_t)((x + TGKV_TILE - 1) / TGKV_TILE * TGKV_TILE); }
 
-/* Chunk length: about eight waves of two CTAs per SM over the whole call,
- * never below 128 positions (per-CTA overhead) -- TGKV_CHUNK overrides. */
-static uint32_t pick_chunk(uint64_t total_positions) {
+/* Chunk length (one CTA per chunk; the hardware block scheduler balances
+ * uneven CTAs): about eight waves of two CTAs per SM over the whole call, but
+ * at least 48 tiles (1536 positions) per CTA as long as that still fills one
+ * wave -- short chunks pay the per-CTA start-up and more partials to merge --
+ * and never below 128 positions.  A multiple of the TMA tile.  TGKV_CHUNK
+ * overrides (tests use it to force split boundaries), TGKV_WAVES changes the
+ * wave target. */
+__attribute__((visibility("hidden"))) uint32_t tgkv_pick_chunk(uint64_t total_positions,
+                                                             uint32_t sm_count) {
     const char* e = getenv("TGKV_CHUNK");
-    if (e && e[0]) {
-        long c = atol(e);
-        if (c >= TGKV_TILE) return round_up((uint32_t)c, TGKV_TILE);
+    if (e && e[0] && atol(e) >= 1) return round_up32((uint64_t)atol(e));
+    const char* w = getenv("TGKV_WAVES");
+    const uint64_t waves = (w && w[0] && atol(w) >= 1) ? (uint64_t)atol(w) : 8;
+    const uint64_t slots = (uint64_t)(sm_count ? sm_count : 148) * 2;
+    uint64_t c = (total_positions + slots * waves - 1) / (slots * waves);
+    if (c < 1536) {
+        const uint64_t one_wave = (total_positions + slots - 1) / slots;
+        c = one_wave < 1536 ? one_wave : 1536;
     }
-    const uint64_t target = (uint64_t)(g_sm_count > 0 ? g_sm_count : 148) * 2 * 8;
-    uint64_t c = (total_positions + target - 1) / target;
     if (c < 128) c = 128;
     if (c > (1u << 30)) c = 1u << 30;
-    return round_up((uint32_t)c, TGKV_TILE);
+    return round_up32(c);
+}
+
+static uint32_t pick_chunk(uint64_t total_positions) {
+    return tgkv_pick_chunk(total_positions, (uint32_t)g_sm_count);
 }
 
 static int plan_attention(const TGCudaAttnCall* c, AttnPlan* pl) {
@@ -335,29 +348,30 @@ static int plan_attention(const TGCudaAttnCall* c, AttnPlan* pl) {
         total += (uint64_t)c->n_pos[i] * c->n_kv_heads * pl->n_sub;
     }
     pl->chunk = pick_chunk(total);
-    pl->max_ctas = 0;
+    pl->max_chunks = 0;
     for (uint32_t b0 = 0; b0 < c->n_items; b0 += TGKV_MAX_ITEMS) {
         const uint32_t n = (c->n_items - b0) < TGKV_MAX_ITEMS ? (c->n_items - b0) : TGKV_MAX_ITEMS;
-        uint64_t ctas = 0;
+        uint64_t chunks = 0;
         for (uint32_t i = 0; i < n; i++)
-            ctas += (uint64_t)((c->n_pos[b0 + i] + pl->chunk - 1) / pl->chunk) * c->n_kv_heads *
-                    pl->n_sub;
-        if (ctas > 0x7fffffffu) { set_err("attention: too many CTAs in one launch"); return 0; }
-        if (ctas > pl->max_ctas) pl->max_ctas = ctas;
+            chunks += (uint64_t)((c->n_pos[b0 + i] + pl->chunk - 1) / pl->chunk) * c->n_kv_heads *
+                      pl->n_sub;
+        if (chunks > 0x7fffffffu) { set_err("attention: too many chunks in one launch"); return 0; }
+        if (chunks > pl->max_chunks) pl->max_chunks = chunks;
     }
     return 1;
 }
 
 static uint64_t part_o_bytes(const AttnPlan* pl, uint32_t head_dim) {
-    return (pl->max_ctas * pl->gt * head_dim * 4 + 255) / 256 * 256;
+    return (pl->max_chunks * pl->gt * head_dim * 4 + 255) / 256 * 256;
 }
 
 uint64_t tg_cuda_kv_attn_scratch_bytes(const TGCudaAttnCall* c) {
     AttnPlan pl;
     if (!plan_attention(c, &pl)) return 0;
-    return part_o_bytes(&pl, c->head_dim) + pl.max_ctas * pl.gt * 2 * 4;
+    return part_o_bytes(&pl, c->head_dim) + pl.max_chunks * pl.gt * 2 * 4;
 }
 
+/* One arrival counter per segment. */
 uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c) {
     AttnPlan pl;
     if (!plan_attention(c, &pl)) return 0;
@@ -380,9 +394,7 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         set_err("attention: q/out must be 8-byte aligned");
         return 0;
     }
-    int multi = 0;
-    for (uint32_t i = 0; i < c->n_items && !multi; i++) multi = c->n_pos[i] > pl.chunk;
-    if (multi && (!c->scratch || !c->counters)) {
+    if (!c->scratch || !c->counters) {
         set_err("attention: split-sequence scratch not provided");
         return 0;
     }
@@ -398,7 +410,7 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         p.q = c->q;
         p.out = c->out;
         p.part_o = (float*)c->scratch;
-        p.part_ml = c->scratch ? (float*)((char*)c->scratch + po) : NULL;
+        p.part_ml = (float*)((char*)c->scratch + po);
         p.counters = c->counters;
         p.err = g_err_word;
         p.cache_stride = c->table_dev ? 1u : 0u;
@@ -413,10 +425,10 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         for (uint32_t i = 0; i < n; i++) {
             const uint32_t np = c->n_pos[b0 + i];
             p.n_pos[i] = np;
-            p.cta_prefix[i] = acc;
+            p.chunk_prefix[i] = acc;
             acc += ((np + pl.chunk - 1) / pl.chunk) * c->n_kv_heads * pl.n_sub;
         }
-        p.cta_prefix[n] = acc;
+        p.chunk_prefix[n] = acc;
         if (!launch_rc(tgkv_launch_attention(&p, c->dtype, c->head_dim, pl.gt, acc, stream),
                        "attention kernel"))
             return 0;

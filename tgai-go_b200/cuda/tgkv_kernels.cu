@@ -1,14 +1,15 @@
 // tgkv_kernels.cu -- sm_100a kernels for TGAI GO's KV-cache path.
 //
 //   * attention: split-sequence (flash-decoding) GQA attention over caches in
-//     the [2][max_seq][kv_dim] layout of src/tgai_kv_cache.h:15-21.  One CTA
-//     streams one chunk of positions of one KV head: a producer warp moves K
-//     and V rows into a shared-memory ring with bulk async copies
-//     (cp.async.bulk, mbarrier completion), four consumer warps compute the
-//     scores of all GT query heads of the group from the same staged rows
+//     the [2][max_seq][kv_dim] layout of src/tgai_kv_cache.h:15-21.  Each
+//     (query row, KV head) segment is cut into fixed-size chunks, one CTA per
+//     chunk (about eight waves).  A producer warp moves 32-row
+//     boxes of K and V of one KV head into a shared-memory ring with tiled TMA
+//     (cp.async.bulk.tensor, mbarrier completion); four consumer warps compute
+//     the scores of all GT query heads of the group from the same staged rows
 //     (K/V read once per KV head), keep an online softmax in the log2 domain
 //     with warp-shuffle reductions, and accumulate P*V with packed fp32 FMAs.
-//     Chunks of one (item, KV head) merge in the last CTA to finish.
+//     The chunks of one segment merge in the last CTA to finish one.
 //     Semantics follow src/tgai_engine.c:3943-4011: kvh = h*nkv/nh, scores
 //     scaled by 1/sqrt(head_dim), causal, softmax, P*V.
 //   * append: fp32 rows -> cache rows (fp32 copy or bf16 round-to-nearest-
@@ -37,6 +38,8 @@ constexpr int kTile = TGKV_TILE;     // positions per stage
 constexpr int kConsumerWarps = 4;    // 8 positions of a stage per warp
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s
+constexpr int kFacBlock = 256;       // partials merged per block in the combine
+
 
 // Error codes written to p.err.
 constexpr int kErrFullTimeout = 1;
@@ -150,7 +153,9 @@ struct AttnCfg {
     static constexpr int OFF_ALPHA = OFF_P + kConsumerWarps * 32 * 4;
     static constexpr int OFF_CO = OFF_ALPHA + kConsumerWarps * 4 * 4;
     static constexpr int OFF_CML = OFF_CO + kConsumerWarps * GT * HD * 4;
-    static constexpr int OFF_FLAG = OFF_CML + kConsumerWarps * GT * 2 * 4;
+    static constexpr int OFF_FAC = OFF_CML + kConsumerWarps * GT * 2 * 4;   // [GT][kFacBlock]
+    static constexpr int OFF_RED = OFF_FAC + GT * kFacBlock * 4;               // [4][GT][2]
+    static constexpr int OFF_FLAG = OFF_RED + kConsumerWarps * GT * 2 * 4;
     static constexpr int SMEM = OFF_FLAG + 16;
 };
 
@@ -223,6 +228,128 @@ __device__ __forceinline__ void consumer_bar() {
     asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
+// A chunk of a segment (see TGKvAttnParams), decoded from its number.
+struct Chunk {
+    uint32_t item, seg, kvh, sub;
+    uint32_t pos0, pos1;         // positions [pos0, pos1) of the segment
+    uint32_t nch;                // chunks of this segment
+    uint32_t first;              // number of the segment's first chunk
+};
+
+__device__ __forceinline__ Chunk decode_chunk(const TGKvAttnParams& p, uint32_t u) {
+    uint32_t lo = 0, hi = p.n_items;            // largest i with chunk_prefix[i] <= u
+    while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (p.chunk_prefix[mid] <= u) lo = mid; else hi = mid;
+    }
+    Chunk c;
+    c.item = lo;
+    const uint32_t np = p.n_pos[lo];
+    c.nch = (np + p.chunk - 1) / p.chunk;
+    const uint32_t rem = u - p.chunk_prefix[lo];
+    c.seg = rem / c.nch;
+    const uint32_t ci = rem % c.nch;
+    c.first = u - ci;
+    c.kvh = c.seg % p.n_kv_heads;
+    c.sub = c.seg / p.n_kv_heads;
+    c.pos0 = ci * p.chunk;
+    c.pos1 = min(c.pos0 + p.chunk, np);
+    return c;
+}
+
+// Merge the nparts partials of one segment (slots first .. first+nparts-1;
+// this CTA finished last): per-head maxima, then blocks of per-partial
+// factors in shared memory and coalesced weighted sums.  Kept out of line so
+// the streaming loop keeps its registers.
+template <int GT, int HD>
+__device__ __noinline__ void combine_segment(const TGKvAttnParams& p, uint32_t first,
+                                             uint32_t nparts, uint64_t row, uint32_t head0,
+                                             float* sm_fac, float* sm_red, int tid, int lane,
+                                             int warp) {
+    float mloc[GT];
+#pragma unroll
+    for (int h = 0; h < GT; ++h) mloc[h] = -INFINITY;
+    for (uint32_t c = tid; c < nparts; c += 128) {
+#pragma unroll
+        for (int h = 0; h < GT; ++h)
+            mloc[h] = fmaxf(mloc[h], __ldcg(&p.part_ml[((uint64_t)(first + c) * GT + h) * 2]));
+    }
+#pragma unroll
+    for (int h = 0; h < GT; ++h) {
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1)
+            mloc[h] = fmaxf(mloc[h], __shfl_xor_sync(0xffffffffu, mloc[h], o));
+        if (lane == 0) sm_red[(warp * GT + h) * 2] = mloc[h];
+    }
+    consumer_bar();
+    float M[GT];
+#pragma unroll
+    for (int h = 0; h < GT; ++h) {
+        M[h] = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) M[h] = fmaxf(M[h], sm_red[(w * GT + h) * 2]);
+    }
+    constexpr int kOut = (GT * HD + 127) / 128;    // outputs per thread
+    float acc[kOut];
+#pragma unroll
+    for (int k = 0; k < kOut; ++k) acc[k] = 0.f;
+    float lsum[GT];
+#pragma unroll
+    for (int h = 0; h < GT; ++h) lsum[h] = 0.f;
+    for (uint32_t c0 = 0; c0 < nparts; c0 += kFacBlock) {
+        const uint32_t nb = min((uint32_t)kFacBlock, nparts - c0);
+        consumer_bar();                           // the previous block's factors are used
+        for (uint32_t c = tid; c < nb; c += 128) {
+            const uint64_t sl = first + c0 + c;
+#pragma unroll
+            for (int h = 0; h < GT; ++h) {
+                const float mc = __ldcg(&p.part_ml[(sl * GT + h) * 2]);
+                const float f = (mc == -INFINITY) ? 0.f : exp2f(mc - M[h]);
+                sm_fac[h * kFacBlock + c] = f;
+                lsum[h] += __ldcg(&p.part_ml[(sl * GT + h) * 2 + 1]) * f;
+            }
+        }
+        consumer_bar();
+#pragma unroll
+        for (int k = 0; k < kOut; ++k) {
+            const int idx = tid + k * 128;
+            if (idx < GT * HD) {
+                const int h = idx / HD, d = idx % HD;
+                const float* po = p.part_o + ((uint64_t)(first + c0) * GT + h) * HD + d;
+                const float* fc = sm_fac + h * kFacBlock;
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                uint32_t c = 0;
+                for (; c + 4 <= nb; c += 4) {
+                    a0 += __ldcg(po + (uint64_t)(c + 0) * GT * HD) * fc[c + 0];
+                    a1 += __ldcg(po + (uint64_t)(c + 1) * GT * HD) * fc[c + 1];
+                    a2 += __ldcg(po + (uint64_t)(c + 2) * GT * HD) * fc[c + 2];
+                    a3 += __ldcg(po + (uint64_t)(c + 3) * GT * HD) * fc[c + 3];
+                }
+                for (; c < nb; ++c) a0 += __ldcg(po + (uint64_t)c * GT * HD) * fc[c];
+                acc[k] += (a0 + a1) + (a2 + a3);
+            }
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < GT; ++h) {
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) lsum[h] += __shfl_xor_sync(0xffffffffu, lsum[h], o);
+        if (lane == 0) sm_red[(warp * GT + h) * 2 + 1] = lsum[h];
+    }
+    consumer_bar();
+#pragma unroll
+    for (int k = 0; k < kOut; ++k) {
+        const int idx = tid + k * 128;
+        if (idx < GT * HD) {
+            const int h = idx / HD, d = idx % HD;
+            float L = 0.f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) L += sm_red[(w * GT + h) * 2 + 1];
+            p.out[row + (uint64_t)(head0 + h) * HD + d] = (L > 0.f) ? acc[k] / L : 0.f;
+        }
+    }
+}
+
 template <int DT, int HD, int GT>
 __global__ void __launch_bounds__(kThreads, 2)
 attention_kernel(const __grid_constant__ TGKvAttnParams p) {
@@ -234,30 +361,14 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
     float* sm_alpha = reinterpret_cast<float*>(smem + C::OFF_ALPHA);  // [4][4]
     float* sm_co = reinterpret_cast<float*>(smem + C::OFF_CO);        // [4][GT][HD]
     float* sm_cml = reinterpret_cast<float*>(smem + C::OFF_CML);      // [4][GT][2]
+    float* sm_fac = reinterpret_cast<float*>(smem + C::OFF_FAC);      // [GT][kFacBlock]
+    float* sm_red = reinterpret_cast<float*>(smem + C::OFF_RED);      // [4][GT][2]
     int* sm_flag = reinterpret_cast<int*>(smem + C::OFF_FLAG);        // [0] abort, [1] last
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t b = blockIdx.x;
-
-    // ---- which (item, kv head, head subset, chunk) this CTA owns
-    uint32_t lo = 0, hi = p.n_items;            // largest i with cta_prefix[i] <= b
-    while (hi - lo > 1) {
-        const uint32_t mid = (lo + hi) >> 1;
-        if (p.cta_prefix[mid] <= b) lo = mid; else hi = mid;
-    }
-    const uint32_t item = lo;
-    const uint32_t npos = p.n_pos[item];
-    const uint32_t nch = (npos + p.chunk - 1) / p.chunk;
-    const uint32_t unit = b - p.cta_prefix[item];
-    const uint32_t chunk = unit % nch, rest = unit / nch;
-    const uint32_t kvh = rest % p.n_kv_heads, sub = rest / p.n_kv_heads;
-    const uint32_t c0 = chunk * p.chunk;
-    const uint32_t c1 = min(c0 + p.chunk, npos);
-    const int ntiles = (int)((c1 - c0 + kTile - 1) / kTile);
-    const uint32_t group = p.n_heads / p.n_kv_heads;
-    const uint32_t head0 = kvh * group + sub * GT;
-
-    const TGKvCacheDesc cd = p.caches ? p.caches[item * p.cache_stride] : p.cache0;
+    const uint32_t u = blockIdx.x;                // this CTA's chunk
+    const Chunk ck = decode_chunk(p, u);
+    const int ntiles = (int)((ck.pos1 - ck.pos0 + kTile - 1) / kTile);
 
     if (tid == 0) {
         for (int s = 0; s < C::NSTAGE; ++s) {
@@ -272,10 +383,11 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
 
     if (warp == kConsumerWarps) {
         // ---------------- producer: one tiled TMA box of K and one of V per
-        // stage (kTile rows of this KV head; rows past max_seq arrive as 0)
+        // stage (32 rows of this KV head; rows past max_seq arrive as 0)
         if (lane == 0) {
+            const TGKvCacheDesc cd = p.caches ? p.caches[ck.item * p.cache_stride] : p.cache0;
             prefetch_tmap(cd.tmap);
-            const int x = (int)(kvh * HD);
+            const int x = (int)(ck.kvh * HD);
             for (int t = 0; t < ntiles; ++t) {
                 const int s = t % C::NSTAGE;
                 if (t >= C::NSTAGE && !mbar_wait(&empty[s], ((t / C::NSTAGE) - 1) & 1)) {
@@ -283,7 +395,7 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
                     sm_flag[0] = 1;
                     break;
                 }
-                const int row0 = (int)(c0 + (uint32_t)t * kTile);
+                const int row0 = (int)(ck.pos0 + (uint32_t)t * kTile);
                 unsigned char* st = smem + s * C::STAGE;
                 mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * kTile * C::RB));
                 tma_load_3d(st, cd.tmap, x, row0, 0, &full[s]);
@@ -298,18 +410,18 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
     const int r_me = (lane >> 2) & 1;
     const int h_me = (lane & 3) / C::HSTEP;
     const bool canon = (lane & (C::HSTEP - 1)) == 0;
+    const uint32_t group = p.n_heads / p.n_kv_heads;
+    const uint32_t head0 = ck.kvh * group + ck.sub * GT;
+    const uint64_t row = (uint64_t)(p.item_base + ck.item) * p.n_heads * HD;
 
     float2 q2[GT][C::NP];
-    {
-        const float* qrow = p.q + (uint64_t)(p.item_base + item) * p.n_heads * HD;
 #pragma unroll
-        for (int h = 0; h < GT; ++h) {
-            const float* qh = qrow + (uint64_t)(head0 + h) * HD;
+    for (int h = 0; h < GT; ++h) {
+        const float* qh = p.q + row + (uint64_t)(head0 + h) * HD;
 #pragma unroll
-            for (int i = 0; i < C::NP; ++i) {
-                const float2 x = *reinterpret_cast<const float2*>(qh + elem_of<DT, HD, GT>(j, i));
-                q2[h][i] = make_float2(x.x * p.qscale, x.y * p.qscale);
-            }
+        for (int i = 0; i < C::NP; ++i) {
+            const float2 x = *reinterpret_cast<const float2*>(qh + elem_of<DT, HD, GT>(j, i));
+            q2[h][i] = make_float2(x.x * p.qscale, x.y * p.qscale);
         }
     }
     float2 o2[GT][C::NP];
@@ -318,18 +430,16 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
 #pragma unroll
         for (int i = 0; i < C::NP; ++i) o2[h][i] = make_float2(0.f, 0.f);
     float m_run = -INFINITY, l_lane = 0.f;
-    bool aborted = false;
 
     for (int t = 0; t < ntiles; ++t) {
         const int s = t % C::NSTAGE;
         if (!mbar_wait(&full[s], (t / C::NSTAGE) & 1)) {
             if (lane == 0) { atomicExch(p.err, kErrFullTimeout); sm_flag[0] = 1; }
-            aborted = true;
             break;
         }
         const unsigned char* kt = smem + s * C::STAGE;
         const unsigned char* vt = kt + kTile * C::RB;
-        const uint32_t tpos = c0 + (uint32_t)t * kTile;
+        const uint32_t tpos = ck.pos0 + (uint32_t)t * kTile;
 
         // scores of rows w*8 + r*4 + g for r = 0, 1 and all GT heads
         float sc[2 * GT];
@@ -346,15 +456,15 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
             }
         }
         float sv = group_transpose_reduce<2 * GT>(sc, lane);
-        const bool valid = tpos + (uint32_t)(warp * 8 + r_me * 4 + g) < c1;
+        const bool valid = tpos + (uint32_t)(warp * 8 + r_me * 4 + g) < ck.pos1;
         sv = valid ? sv : -INFINITY;
 
         float tm = sv;
         tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 4));
         tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 8));
         tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 16));
-        // Lazy rescale: the running maximum only moves when a score exceeds it
-        // by more than 2^8, so exp2(score - m_run) stays <= 256.
+        // Lazy rescale: the running maximum only moves when a score exceeds
+        // it by more than 2^8, so exp2(score - m_run) stays <= 256.
         const bool need = tm > m_run + 8.f;
         if (__any_sync(0xffffffffu, need)) {
             const float m_new = fmaxf(m_run, tm);
@@ -378,13 +488,13 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
         sm_p[warp * 32 + lane] = pv;
         __syncwarp();
 
-        const bool tail = tpos + kTile > c1;
+        const bool tail = tpos + kTile > ck.pos1;
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-            const int row = warp * 8 + r * 4 + g;
+            const int rw = warp * 8 + r * 4 + g;
             float2 v2[C::NP];
-            load_row<DT, HD, GT>(vt + row * C::RB, j, v2);
-            if (tail && tpos + (uint32_t)row >= c1) {
+            load_row<DT, HD, GT>(vt + rw * C::RB, j, v2);
+            if (tail && tpos + (uint32_t)rw >= ck.pos1) {
 #pragma unroll
                 for (int i = 0; i < C::NP; ++i) v2[i] = make_float2(0.f, 0.f);
             }
@@ -399,7 +509,6 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
-    (void)aborted;
 
     // ---- warp totals: O over the four row groups, l over lanes of a head
 #pragma unroll
@@ -434,7 +543,7 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
     consumer_bar();
 
     // ---- merge the four warps; write the output or this chunk's partial
-    const uint64_t out_row = (uint64_t)(p.item_base + item) * p.n_heads * HD;
+    const bool whole = ck.nch == 1;
     for (int idx = tid; idx < GT * HD; idx += 128) {
         const int h = idx / HD, d = idx % HD;
         float M = -INFINITY;
@@ -448,45 +557,30 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
             O += sm_co[(w * GT + h) * HD + d] * f;
             L += sm_cml[(w * GT + h) * 2 + 1] * f;
         }
-        if (nch == 1) {
-            p.out[out_row + (uint64_t)(head0 + h) * HD + d] = (L > 0.f) ? O / L : 0.f;
+        if (whole) {
+            p.out[row + (uint64_t)(head0 + h) * HD + d] = (L > 0.f) ? O / L : 0.f;
         } else {
-            p.part_o[((uint64_t)b * GT + h) * HD + d] = O;
+            p.part_o[((uint64_t)u * GT + h) * HD + d] = O;
             if (d == 0) {
-                p.part_ml[((uint64_t)b * GT + h) * 2 + 0] = M;
-                p.part_ml[((uint64_t)b * GT + h) * 2 + 1] = L;
+                p.part_ml[((uint64_t)u * GT + h) * 2 + 0] = M;
+                p.part_ml[((uint64_t)u * GT + h) * 2 + 1] = L;
             }
         }
     }
-    if (nch == 1) return;
+    if (whole) return;
 
-    // ---- split-sequence combine in the last CTA of this (item, kvh, sub)
+    // ---- the last chunk of the segment to finish merges them all
     __threadfence();
     consumer_bar();
-    const uint64_t cidx =
-        ((uint64_t)(p.item_base + item) * p.n_sub + sub) * p.n_kv_heads + kvh;
+    const uint64_t cidx = (uint64_t)(p.item_base + ck.item) * (p.n_sub * p.n_kv_heads) + ck.seg;
     if (tid == 0) {
         const uint32_t prev = atomicAdd(&p.counters[cidx], 1u);
-        sm_flag[1] = (prev == nch - 1) ? 1 : 0;
+        sm_flag[1] = (prev == ck.nch - 1) ? 1 : 0;
     }
     consumer_bar();
     if (!sm_flag[1]) return;
     __threadfence();
-    const uint64_t slot0 = (uint64_t)p.cta_prefix[item] + (uint64_t)rest * nch;
-    for (int idx = tid; idx < GT * HD; idx += 128) {
-        const int h = idx / HD, d = idx % HD;
-        float M = -INFINITY;
-        for (uint32_t c = 0; c < nch; ++c)
-            M = fmaxf(M, __ldcg(&p.part_ml[((slot0 + c) * GT + h) * 2]));
-        float O = 0.f, L = 0.f;
-        for (uint32_t c = 0; c < nch; ++c) {
-            const float mc = __ldcg(&p.part_ml[((slot0 + c) * GT + h) * 2]);
-            const float f = (mc == -INFINITY) ? 0.f : exp2f(mc - M);
-            O += __ldcg(&p.part_o[((slot0 + c) * GT + h) * HD + d]) * f;
-            L += __ldcg(&p.part_ml[((slot0 + c) * GT + h) * 2 + 1]) * f;
-        }
-        p.out[out_row + (uint64_t)(head0 + h) * HD + d] = (L > 0.f) ? O / L : 0.f;
-    }
+    combine_segment<GT, HD>(p, ck.first, ck.nch, row, head0, sm_fac, sm_red, tid, lane, warp);
     if (tid == 0) p.counters[cidx] = 0u;
 }
 
@@ -652,14 +746,14 @@ extern "C" int tgkv_launch_rope_append(const TGKvRopeParams* p, void* stream) {
 // (inside a host allocator hook, a real-time decode thread with a fixed memory
 // budget, or an engine that hands this library only its own buffers).  Its
 // scratch (the CTA partials, the arrival counters, the cache's TMA tensor map
-// and an error word) lives in the file-scope device array below: 8 MiB that
+// and an error word) lives in the file-scope device array below: 4 MiB that
 // every GPU which loads this library holds until the process exits.
 extern "C" void tgkv_set_last_error(const char* msg);   // tgai_kv_cache.c
 
 namespace tgkv {
 namespace staticmem {
 
-constexpr size_t kBytes = 8u << 20;
+constexpr size_t kBytes = 4u << 20;
 constexpr size_t kOffTmap = 0;        // 128-byte CUtensorMap
 constexpr size_t kOffErr = 128;       // bounded-wait error word
 constexpr size_t kOffCounters = 256;  // arrival counters, then partials
@@ -748,41 +842,32 @@ extern "C" __attribute__((visibility("default"))) int tg_kv_attention_static(
         return fail("tg_kv_attention_static: no usable current device");
     if (!setup(dev)) return 0;
 
-    // Split plan: the rule tg_cuda_kv_attention uses (about eight waves of two
-    // CTAs per SM, chunks of at least 128 positions, TGKV_CHUNK overrides).
+    // Split plan: the rule tg_cuda_kv_attention uses (tgkv_pick_chunk).
     const uint32_t group = n_heads / n_kv_heads;
     const uint32_t gt = tgkv_attention_g_tile(head_dim, group);
     const uint32_t n_sub = group / gt;
     uint64_t total = 0;
     for (uint32_t t = 0; t < n_q; ++t) total += (uint64_t)(kv_len - n_q + t + 1) * n_kv_heads * n_sub;
-    uint32_t chunk;
-    const char* ce = getenv("TGKV_CHUNK");
-    if (ce && ce[0] && atol(ce) >= TGKV_TILE) {
-        chunk = (uint32_t)((atol(ce) + TGKV_TILE - 1) / TGKV_TILE * TGKV_TILE);
-    } else {
-        const uint64_t target = (uint64_t)g_sms[dev] * 2 * 8;
-        uint64_t c = (total + target - 1) / target;
-        if (c < 128) c = 128;
-        if (c > (1u << 30)) c = 1u << 30;
-        chunk = (uint32_t)((c + TGKV_TILE - 1) / TGKV_TILE * TGKV_TILE);
-    }
+    const uint64_t chunk = tgkv_pick_chunk(total, (uint32_t)g_sms[dev]);
     TGKvAttnParams p;                     // ~8 KB on the stack: no heap, no device memory
     memset(&p, 0, offsetof(TGKvAttnParams, n_pos));
-    uint64_t ctas = 0;
+    uint64_t n_chunks = 0;
     for (uint32_t t = 0; t < n_q; ++t) {
         const uint32_t np = kv_len - n_q + t + 1;
         p.n_pos[t] = np;
-        p.cta_prefix[t] = (uint32_t)ctas;
-        ctas += (uint64_t)((np + chunk - 1) / chunk) * n_kv_heads * n_sub;
+        p.chunk_prefix[t] = (uint32_t)n_chunks;
+        n_chunks += (uint64_t)((np + chunk - 1) / chunk) * n_kv_heads * n_sub;
     }
-    p.cta_prefix[n_q] = (uint32_t)ctas;
+    if (n_chunks > 0x7fffffffu) return fail("tg_kv_attention_static: too many chunks");
+    p.chunk_prefix[n_q] = (uint32_t)n_chunks;
     const uint64_t counters = ((uint64_t)n_q * n_kv_heads * n_sub * 4 + 255) / 256 * 256;
-    const uint64_t part_o = (ctas * gt * head_dim * 4 + 255) / 256 * 256;
-    const uint64_t need = kOffCounters + counters + part_o + ctas * gt * 2 * 4;
+    const uint64_t part_o = (n_chunks * gt * head_dim * 4 + 255) / 256 * 256;
+    const uint64_t need = kOffCounters + counters + part_o + n_chunks * gt * 2 * 4;
     if (need > kBytes)
         return fail("tg_kv_attention_static: needs %llu bytes of scratch, above the static "
-                    "limit of %llu bytes (8 MiB); use tg_kv_attention or fewer query rows",
+                    "limit of %llu bytes (4 MiB); use tg_kv_attention or fewer query rows",
                     (unsigned long long)need, (unsigned long long)kBytes);
+    const uint32_t grid = (uint32_t)n_chunks;
 
     // The cache's tensor map goes into the static array on the stream, ahead
     // of the kernel; the counters and the error word are cleared the same way
@@ -821,10 +906,10 @@ extern "C" __attribute__((visibility("default"))) int tg_kv_attention_static(
     p.n_heads = n_heads;
     p.n_kv_heads = n_kv_heads;
     p.n_sub = n_sub;
-    p.chunk = chunk;
+    p.chunk = (uint32_t)chunk;
     p.qscale = (1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
     p.item_base = 0;
-    const int rc = tgkv_launch_attention(&p, dtype, head_dim, gt, (uint32_t)ctas, stream);
+    const int rc = tgkv_launch_attention(&p, dtype, head_dim, gt, grid, stream);
     if (rc != 0)
         return fail("tg_kv_attention_static: launch failed: %s",
                     cudaGetErrorString((cudaError_t)rc));

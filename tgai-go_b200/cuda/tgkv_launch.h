@@ -28,32 +28,36 @@ typedef struct {
 } TGKvCacheDesc;
 
 /* Split-sequence decode attention.
- * CTA b works on item i (cta_prefix[i] <= b < cta_prefix[i+1]); inside the
- * item, unit = b - cta_prefix[i] decomposes as
- *     chunk = unit % n_chunks(i), rest = unit / n_chunks(i),
- *     kvh = rest % n_kv_heads, sub = rest / n_kv_heads,
- * with n_chunks(i) = ceil(n_pos[i] / chunk).  The CTA attends query heads
- * kvh*G + sub*GT .. +GT (G = n_heads / n_kv_heads, GT heads per CTA) of item
- * i over positions [chunk*C, min((chunk+1)*C, n_pos[i])). */
+ * For each item i (a query row) and each (head subset sub, KV head kvh) of it
+ * there is one segment: the n_pos[i] positions that row attends.  Every
+ * segment is cut into chunks of `chunk` positions (a multiple of the TMA tile,
+ * the last chunk shorter); chunks are numbered item-major, then
+ * seg = sub*n_kv_heads + kvh, then chunk index, so chunk_prefix[i] is item i's
+ * first chunk and a segment's chunks are consecutive.  CTA b streams chunk b
+ * (one CTA per chunk, about eight waves, balanced by the hardware block
+ * scheduler).  A one-chunk segment is finished by the CTA that streams it;
+ * otherwise each chunk leaves a partial in slot <chunk number> and the last
+ * chunk to finish merges the segment.  GT query heads (kvh*G + sub*GT ..)
+ * share each staged K/V row. */
 typedef struct {
     const TGKvCacheDesc* caches; /* device table, or NULL: every item uses cache0 */
     TGKvCacheDesc cache0;
     const float* q;              /* [items][n_heads][head_dim] fp32 */
     float*       out;            /* same shape */
-    float*       part_o;         /* [ctas][GT][head_dim]  scratch */
-    float*       part_ml;        /* [ctas][GT][2]        scratch */
-    uint32_t*    counters;       /* [items][n_kv_heads][n_sub], zero, self-resetting */
+    float*       part_o;         /* [n_chunks][GT][head_dim]  scratch */
+    float*       part_ml;        /* [n_chunks][GT][2]         scratch */
+    uint32_t*    counters;       /* [items][n_sub*n_kv_heads], zero, self-resetting */
     int32_t*     err;            /* device error word (0 = fine) */
     uint32_t cache_stride;       /* cache index = item * cache_stride */
     uint32_t n_items;
     uint32_t n_heads;
     uint32_t n_kv_heads;
     uint32_t n_sub;              /* head subsets per KV head = G / GT */
-    uint32_t chunk;              /* positions per CTA, multiple of TGKV_TILE */
+    uint32_t chunk;              /* positions per chunk, multiple of TGKV_TILE */
     float    qscale;             /* softmax scale * log2(e) */
     uint32_t item_base;          /* first item of this launch (q/out/counter offset) */
     uint32_t n_pos[TGKV_MAX_ITEMS];
-    uint32_t cta_prefix[TGKV_MAX_ITEMS + 1];
+    uint32_t chunk_prefix[TGKV_MAX_ITEMS + 1];
 } TGKvAttnParams;
 
 /* Append of one fp32 row per item into cache (item * cache_stride) at
@@ -87,6 +91,8 @@ int tgkv_launch_attention(const TGKvAttnParams* p, int dtype, uint32_t head_dim,
                           uint32_t g_tile, uint32_t grid, void* stream);
 int tgkv_launch_append(const TGKvAppendParams* p, int dtype, void* stream);
 int tgkv_launch_rope_append(const TGKvRopeParams* p, void* stream);
+/* Chunk length the planner uses for a launch of total_positions (bridge). */
+uint32_t tgkv_pick_chunk(uint64_t total_positions, uint32_t sm_count);
 /* Heads per CTA the attention kernel supports for this head_dim (<= G). */
 uint32_t tgkv_attention_g_tile(uint32_t head_dim, uint32_t group);
 /* 1 if (dtype, head_dim) has an attention kernel. */
