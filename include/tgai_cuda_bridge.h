@@ -92,6 +92,8 @@ typedef struct {
     const TGCudaCacheDesc* table_dev;
     const float*    q;
     float*          out;
+    const float*    k_new;          /* optional fp32 [n_items][kv_dim]: written as row */
+    const float*    v_new;          /*   n_pos[i]-1 of item i's cache before attending */
     const uint32_t* n_pos;          /* host array [n_items], each >= 1 */
     uint32_t        n_items;
     float           scale;          /* softmax scale (1/sqrt(head_dim)) */

@@ -140,7 +140,8 @@ void       tg_kv_batch_destroy(TGKvBatch* b);
 /* One decode step for every cache i of the plan: append row i of k_new/v_new
  * (fp32 [n][kv_dim], device) at position len_i, then attend query row i of q
  * (fp32 [n][n_heads][head_dim], device) over positions [0, len_i] into row i
- * of out (same shape).  Each cache's len grows by one.  Async on `stream`.
+ * of out (same shape).  Each cache's len grows by one.  Async on `stream`;
+ * one kernel launch per 1024 caches (the append is fused into the attention).
  * Returns 0 (nothing launched) if any cache is full. */
 int tg_kv_batch_decode(TGKvBatch* b, const float* q, const float* k_new,
                        const float* v_new, float* out, void* stream);

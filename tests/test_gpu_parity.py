@@ -291,6 +291,48 @@ def test_cfg4_batched_decode_ragged(cuda, devbuf):
         lib.tg_kv_destroy(c)
 
 
+@pytest.mark.parametrize("dtype,nh,nkv,hd", [(0, 16, 2, 64), (1, 16, 2, 64), (1, 8, 8, 32)])
+def test_batched_decode_fused_append_geometries(cuda, devbuf, dtype, nh, nkv, hd):
+    """The decode append runs inside the attention launch: with group 8 two head
+    subsets write the same new row; fp32 and bf16; several consecutive steps
+    (back-to-back launches on one stream)."""
+    lib = cuda
+    kvd = nkv * hd
+    lens = [1, 40, 300, 2000]
+    caches = []
+    for i, L in enumerate(lens):
+        _, k, v = synth_qkv(900 + i, L, nh, nkv, hd)
+        caches.append(make_cache(lib, devbuf, L + 8, nkv, hd, dtype, k, v))
+    b = lib.tg_kv_batch_create((C.c_void_p * len(caches))(*caches), len(caches), nh)
+    tgkv.check(b, lib)
+    steps = 5
+    q = O.normal(steps * len(lens) * nh * hd, 31, 5).reshape(steps, len(lens), nh, hd)
+    kn = O.normal(steps * len(lens) * kvd, 32, 6).reshape(steps, len(lens), kvd)
+    vn = O.normal(steps * len(lens) * kvd, 33, 7).reshape(steps, len(lens), kvd)
+    qd, kd, vd = devbuf(q), devbuf(kn), devbuf(vn)
+    od = devbuf(nbytes=q.nbytes)
+    qrow, krow = len(lens) * nh * hd * 4, len(lens) * kvd * 4
+    for st in range(steps):
+        tgkv.check(lib.tg_kv_batch_decode(b, qd.ptr + st * qrow, kd.ptr + st * krow,
+                                          vd.ptr + st * krow, od.ptr + st * qrow, None), lib)
+        assert lib.tg_kv_batch_last_launches(b) == 1
+    assert lib.tg_cuda_kv_sync(None)
+    out = od.get(np.float32, q.shape)
+    for i, c in enumerate(caches):
+        ms = lens[i] + 8
+        rows = cache_rows(lib, c, dtype, ms, kvd)
+        kvc = rows if dtype == 0 else O.bf16_to_f32(rows)
+        for st in range(steps):
+            L = lens[i] + st + 1
+            want_k = kn[st, i] if dtype == 0 else O.bf16_to_f32(O.f32_to_bf16(kn[st, i]))
+            assert np.array_equal(kvc[0, L - 1], want_k), (i, st)
+            eng = O.attention_engine(q[st, i], kvc, nh, nkv, hd, 1, L - 1, L, ms)
+            assert rel_head_err(out[st, i], eng[0]) < 1e-5, (i, st)
+    lib.tg_kv_batch_destroy(b)
+    for c in caches:
+        lib.tg_kv_destroy(c)
+
+
 def test_batch_decode_host_buffers(cuda, devbuf):
     """tg_kv_batch_decode_host: the same step from host buffers."""
     lib = cuda

@@ -394,6 +394,10 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         set_err("attention: q/out must be 8-byte aligned");
         return 0;
     }
+    if (!c->k_new != !c->v_new) {
+        set_err("attention: k_new and v_new go together");
+        return 0;
+    }
     if (!c->scratch || !c->counters) {
         set_err("attention: split-sequence scratch not provided");
         return 0;
@@ -409,6 +413,8 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         p.cache0.tmap = c->cache.tmap;
         p.q = c->q;
         p.out = c->out;
+        p.k_new = c->k_new ? c->k_new + (uint64_t)b0 * c->n_kv_heads * c->head_dim : NULL;
+        p.v_new = c->v_new ? c->v_new + (uint64_t)b0 * c->n_kv_heads * c->head_dim : NULL;
         p.part_o = (float*)c->scratch;
         p.part_ml = (float*)((char*)c->scratch + po);
         p.counters = c->counters;

@@ -380,12 +380,39 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
+    // Programmatic dependent launch: everything above overlaps the previous
+    // kernel on the stream; nothing below reads global memory before it is done.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (warp == kConsumerWarps) {
+        const TGKvCacheDesc cd = p.caches ? p.caches[ck.item * p.cache_stride] : p.cache0;
+        if (p.k_new && ck.pos1 == p.n_pos[ck.item]) {
+            // ---------------- fused append: the chunk that ends at the newest
+            // position first stores this KV head's slice of the new K and V
+            // row (fp32 -> cache type), then makes the stores visible to the
+            // TMA reads below.  Every head subset's CTA writes the same bytes.
+            const uint64_t kv_dim = (uint64_t)p.n_kv_heads * HD;
+            const uint64_t src = (uint64_t)(p.item_base + ck.item) * kv_dim + ck.kvh * HD;
+            const uint64_t dst = (uint64_t)(ck.pos1 - 1) * kv_dim + ck.kvh * HD;
+            const uint64_t vofs = (uint64_t)cd.max_seq * kv_dim;
+            for (int e = lane; e < HD; e += 32) {
+                const float kx = p.k_new[src + e], vx = p.v_new[src + e];
+                if constexpr (DT == 0) {
+                    float* c = reinterpret_cast<float*>(cd.base);
+                    c[dst + e] = kx;
+                    c[vofs + dst + e] = vx;
+                } else {
+                    uint16_t* c = reinterpret_cast<uint16_t*>(cd.base);
+                    c[dst + e] = f32_to_bf16_rne(kx);
+                    c[vofs + dst + e] = f32_to_bf16_rne(vx);
+                }
+            }
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            __syncwarp();
+        }
         // ---------------- producer: one tiled TMA box of K and one of V per
         // stage (32 rows of this KV head; rows past max_seq arrive as 0)
         if (lane == 0) {
-            const TGKvCacheDesc cd = p.caches ? p.caches[ck.item * p.cache_stride] : p.cache0;
             prefetch_tmap(cd.tmap);
             const int x = (int)(ck.kvh * HD);
             for (int t = 0; t < ntiles; ++t) {
@@ -509,6 +536,8 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
+    // the streaming is over: the next kernel on the stream may start launching
+    if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     // ---- warp totals: O over the four row groups, l over lanes of a head
 #pragma unroll
@@ -668,6 +697,9 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const __grid_constant_
     }
 }
 
+// Launched with programmatic stream serialization (PDL) unless TGKV_PDL=0:
+// the kernel waits (griddepcontrol.wait) before its first global access, so
+// overlapping its launch with the previous kernel is safe.
 template <int DT, int HD, int GT>
 int launch_attn(const TGKvAttnParams* p, uint32_t grid, cudaStream_t st) {
     using C = AttnCfg<DT, HD, GT>;
@@ -678,8 +710,21 @@ int launch_attn(const TGKvAttnParams* p, uint32_t grid, cudaStream_t st) {
         if (e != cudaSuccess) return (int)e;
         configured = true;
     }
-    attention_kernel<DT, HD, GT><<<grid, kThreads, C::SMEM, st>>>(*p);
-    return (int)cudaGetLastError();
+    static const bool pdl = [] {
+        const char* e = getenv("TGKV_PDL");
+        return !(e && e[0] == '0');
+    }();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return (int)cudaLaunchKernelEx(&cfg, attention_kernel<DT, HD, GT>, *p);
 }
 
 }  // namespace tgkv

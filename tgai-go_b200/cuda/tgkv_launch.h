@@ -44,6 +44,8 @@ typedef struct {
     TGKvCacheDesc cache0;
     const float* q;              /* [items][n_heads][head_dim] fp32 */
     float*       out;            /* same shape */
+    const float* k_new;          /* NULL, or [items][kv_dim] fp32: row n_pos[i]-1 of item i's */
+    const float* v_new;          /*   cache is written first (decode append fused in) */
     float*       part_o;         /* [n_chunks][GT][head_dim]  scratch */
     float*       part_ml;        /* [n_chunks][GT][2]         scratch */
     uint32_t*    counters;       /* [items][n_sub*n_kv_heads], zero, self-resetting */

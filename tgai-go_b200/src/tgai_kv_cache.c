@@ -301,7 +301,6 @@ struct TGKvBatch {
     TGBackend* be;
     TGKvCache** caches;
     TGCudaCacheDesc* table_dev;
-    uint32_t* pos;                    /* host: append position per cache */
     uint32_t* npos;                   /* host: attended positions per cache */
     void* scratch;
     uint64_t scratch_bytes;
@@ -344,10 +343,9 @@ TGKvBatch* tg_kv_batch_create(TGKvCache* const* caches, uint32_t n, uint32_t n_h
     b->dtype = c0->dtype;
     b->be = c0->be;
     b->caches = (TGKvCache**)malloc(n * sizeof(TGKvCache*));
-    b->pos = (uint32_t*)malloc(n * sizeof(uint32_t));
     b->npos = (uint32_t*)malloc(n * sizeof(uint32_t));
     TGCudaCacheDesc* table = (TGCudaCacheDesc*)calloc(n, sizeof(TGCudaCacheDesc));
-    if (!b->caches || !b->pos || !b->npos || !table) {
+    if (!b->caches || !b->npos || !table) {
         free(table);
         tg_kv_batch_destroy(b);
         set_err("malloc failed");
@@ -379,7 +377,6 @@ void tg_kv_batch_destroy(TGKvBatch* b) {
         if (b->io) b->be->free(b->io);
     }
     free(b->caches);
-    free(b->pos);
     free(b->npos);
     free(b);
 }
@@ -393,7 +390,6 @@ int tg_kv_batch_decode(TGKvBatch* b, const float* q, const float* k_new, const f
     for (uint32_t i = 0; i < b->n; i++) {
         const TGKvCache* c = b->caches[i];
         if (c->len >= c->max_seq) { set_err("batch: cache %u is full", i); return 0; }
-        b->pos[i] = c->len;
         b->npos[i] = c->len + 1;
     }
     TGCudaAttnCall call;
@@ -413,16 +409,12 @@ int tg_kv_batch_decode(TGKvBatch* b, const float* q, const float* k_new, const f
         return 0;
     call.scratch = b->scratch;
     call.counters = b->counters;
+    call.k_new = k_new;               /* the append runs inside the attention launch */
+    call.v_new = v_new;
     if (tg_be_current() != &tg_backend_cuda) {
         set_err("KV-cache path needs the cuda backend; no fallback");
         return 0;
     }
-    if (!tg_cuda_kv_append_batch(b->dtype, b->table_dev, b->kv_dim, b->pos, b->n, k_new, v_new,
-                                 stream)) {
-        set_err("%s", tg_cuda_kv_last_error());
-        return 0;
-    }
-    b->last_launches += (b->n + 1023) / 1024;
     if (!tg_cuda_kv_attention(&call, stream)) {
         set_err("%s", tg_cuda_kv_last_error());
         return 0;
