@@ -217,14 +217,23 @@ def run_ours(args):
         wl["n_seq"] = args.seqs
     if args.layers:
         wl["layers"] = args.layers
+    import shard
     heads_sharded = args.workload != "cfg4" and world > 1
-    if heads_sharded and wl["nkv"] % world:
-        raise SystemExit(f"{wl['nkv']} KV heads do not split over {world} GPUs")
-    nkv = wl["nkv"] // world if heads_sharded else wl["nkv"]
-    nh = wl["nh"] // world if heads_sharded else wl["nh"]
-    hd, layers, n_seq = wl["hd"], wl["layers"], wl["n_seq"]
+    if heads_sharded:
+        kv0, kv1, q0, q1 = shard.kv_head_shard(wl["nh"], wl["nkv"], world, rank)
+        nkv, nh = kv1 - kv0, q1 - q0
+    else:
+        nkv, nh = wl["nkv"], wl["nh"]
+    hd, layers = wl["hd"], wl["layers"]
+    if args.shard_seqs and not heads_sharded:
+        # strong scaling: the workload's sequences split over ranks by LPT
+        all_lens = lengths_for(wl, args.seed, 0)
+        mine = shard.lpt_partition(all_lens, world)[rank]
+        lens0 = all_lens[mine]
+    else:
+        lens0 = lengths_for(wl, args.seed, 0 if heads_sharded else rank)
+    n_seq = len(lens0)
     kvd = nkv * hd
-    lens0 = lengths_for(wl, args.seed, 0 if heads_sharded else rank)
     e2e_steps = 0 if args.no_e2e else args.steps
     e2e_warm = 0 if args.no_e2e else args.warmup
     total_steps = args.warmup + args.steps + e2e_warm + e2e_steps + 1
@@ -282,11 +291,7 @@ def run_ours(args):
         torch.cuda.synchronize()
 
     def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return shard.max_over_ranks(x, world, device="cuda")
 
     for _ in range(args.warmup):
         step()
@@ -345,7 +350,7 @@ def run_ours(args):
         e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
         h2d = layers * (qh[0].numel() + 2 * kh[0].numel()) * 4
         d2h = layers * oh[0].numel() * 4
-        tokens = n_seq * (world if not heads_sharded else 1)
+        tokens = wl["n_seq"] if (heads_sharded or args.shard_seqs) else n_seq * world
         e2e = {"value": tokens / (e_ms / 1000.0), "unit": "tokens/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e_ms}
 
@@ -358,7 +363,9 @@ def run_ours(args):
     if err:
         raise RuntimeError(f"kernel bounded wait expired (code {err})")
 
-    tokens = n_seq * (world if not heads_sharded else 1)
+    # tokens per step over all ranks: the whole sequence set once (sharded
+    # heads or LPT-split sequences), else every rank's own sequences
+    tokens = wl["n_seq"] if (heads_sharded or args.shard_seqs) else n_seq * world
     value = tokens / (ms_max / 1000.0)
     peak, peak_kind = measured_peak()
     traffic = None
@@ -378,17 +385,19 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
-            "higher_is_better": True, "scaling": "strong" if heads_sharded else "weak",
+            "higher_is_better": True,
+            "scaling": "strong" if (heads_sharded or args.shard_seqs) else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": args.workload, "desc": wl["desc"],
                        "layers": layers,
-                       "sequences_per_gpu": n_seq if not heads_sharded else n_seq,
+                       "sequences_per_gpu": n_seq,
                        "kv_heads_per_gpu": nkv, "context_mean": float(lens0.mean()),
                        "l2": "inputs larger than L2 (K/V read per step >> 126 MB)",
                        "parallelism": (f"kv-head groups x{world} + NCCL all-gather"
-                                       if heads_sharded else f"sequences x{world}, no collective"),
+                                       if heads_sharded else
+                                       f"sequences x{world} ({'LPT split' if args.shard_seqs else 'own set per GPU'}), no collective"),
                        "fill_s": round(t_fill, 1)},
-            "hbm_gbs": algo / (ms * args.steps / 1000.0) / 1e9 * (1 if heads_sharded else 1),
+            "hbm_gbs": algo / (ms * args.steps / 1000.0) / 1e9,
             "roofline": {"bound": "hbm", "achieved": kernel_gbs, "peak": peak, "unit": "GB/s",
                          "frac": kernel_gbs / peak, "traffic": traffic,
                          "peak_source": peak_kind,
@@ -418,6 +427,9 @@ def main():
                     help="sequences per GPU (default: the workload's); for small profiling cases")
     ap.add_argument("--layers", type=int, default=0,
                     help="layers (default: the workload's); for small profiling cases")
+    ap.add_argument("--shard-seqs", action="store_true",
+                    help="cfg4: split the workload's sequences over ranks (LPT, strong scaling) "
+                         "instead of a full set per GPU (weak scaling)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-baseline-s", type=float, default=12.0)
