@@ -101,10 +101,27 @@ int tg_kv_append_dev(TGKvCache* c, const float* k_dev, const float* v_dev,
 int tg_kv_attention(TGKvCache* c, const float* q_dev, float* out_dev,
                     uint32_t n_heads, uint32_t n_q, void* stream);
 
+/* Score scale used by tg_kv_attention and the batch calls of this cache:
+ * (1/sqrt(head_dim)) * mscale, with mscale the engine's YaRN temperature
+ * (src/tgai_engine.c:3947; tg_kv_rope_tables reports it).  Default 1. */
+void tg_kv_set_attn_mscale(TGKvCache* c, float mscale);
+
 /* Copy the whole [2][max_seq][kv_dim] buffer (raw storage bytes) to host
  * memory `dst` of tg_kv_bytes(c) bytes.  Blocks. */
 uint64_t tg_kv_bytes(const TGKvCache* c);
 int      tg_kv_download(const TGKvCache* c, void* dst);
+
+/* RoPE tables for TGBackend.rope: cos/sin of positions pos0 .. pos0+n_pos-1,
+ * host arrays [n_pos][head_dim/2], from the engine's formula
+ * (src/tgai_engine.c:3404-3460): freq_i = 1/theta^(i/head_dim), and when
+ * extend_ctx > max_seq_len the NTK-by-parts interpolation between the
+ * extrapolated and interpolated frequencies.  *mscale_out (optional) gets the
+ * YaRN attention temperature the engine multiplies into 1/sqrt(head_dim)
+ * (1 without extension).  Rotating with these tables gives the engine's
+ * bits.  Returns 0 on bad arguments. */
+int tg_kv_rope_tables(float theta, uint32_t head_dim, uint32_t pos0, uint32_t n_pos,
+                      uint32_t extend_ctx, uint32_t max_seq_len, float* cos_out,
+                      float* sin_out, float* mscale_out);
 
 /* Attention without any allocation.  No counterpart in the reference.
  *

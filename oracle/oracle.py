@@ -29,6 +29,7 @@ def load():
     lib.orc_dot.argtypes = [_P, _P, C.c_int]
     lib.orc_softmax.argtypes = [_P, C.c_int]
     lib.orc_rope.argtypes = [_P, _P] + [C.c_int] * 5 + [C.c_float]
+    lib.orc_rope_tables.argtypes = [_P] + [C.c_int] * 4 + [_P, _P]
     lib.orc_f32_to_bf16.restype = C.c_uint16
     lib.orc_f32_to_bf16.argtypes = [C.c_float]
     lib.orc_kv_append.restype = C.c_int
@@ -37,6 +38,7 @@ def load():
     lib.orc_kv_decode.argtypes = [C.c_void_p, C.c_int, C.c_uint32, C.c_uint32, _P]
     for n in ("orc_attention_engine", "orc_attention_f64", "orc_attention_weights_last"):
         getattr(lib, n).argtypes = [_P, _P, _P] + [C.c_int] * 7
+    lib.orc_attention_engine_scaled.argtypes = [_P, _P, _P] + [C.c_int] * 7 + [C.c_float]
     lib.orc_decode_batch.argtypes = [C.POINTER(_P), C.POINTER(_P), C.POINTER(_P),
                                      C.POINTER(C.c_int), C.POINTER(C.c_int)] + [C.c_int] * 5
     lib.orc_normal.restype = C.c_float
@@ -91,14 +93,25 @@ def rope(q, k, n_heads, n_kv_heads, d_k, pos0, theta=10000.0):
     return q, k
 
 
-def attention_engine(q, kvc, n_heads, n_kv_heads, head_dim, n_q, pos0, kv_len, max_seq):
+def rope_tables(x, n_heads, d_k, pos0, cs, sn):
+    """Rotate a copy of x [seq][nh][dk] with tables cs/sn [pos][dk/2]."""
+    x = np.ascontiguousarray(x, np.float32).copy()
+    seq = x.size // (n_heads * d_k)
+    load().orc_rope_tables(_f(x), seq, n_heads, d_k, pos0,
+                           _f(np.ascontiguousarray(cs, np.float32)),
+                           _f(np.ascontiguousarray(sn, np.float32)))
+    return x
+
+
+def attention_engine(q, kvc, n_heads, n_kv_heads, head_dim, n_q, pos0, kv_len, max_seq,
+                     mscale=1.0):
     """Engine-order attention (src/tgai_engine.c:3943-4011) over an fp32
-    [2][max_seq][kv_dim] cache.  q: [n_q][nh][hd]."""
+    [2][max_seq][kv_dim] cache.  q: [n_q][nh][hd]; mscale: YaRN temperature."""
     q = np.ascontiguousarray(q, np.float32)
     kvc = np.ascontiguousarray(kvc, np.float32)
     out = np.zeros(n_q * n_heads * head_dim, np.float32)
-    load().orc_attention_engine(_f(q), _f(kvc), _f(out), n_heads, n_kv_heads, head_dim, n_q,
-                                pos0, kv_len, max_seq)
+    load().orc_attention_engine_scaled(_f(q), _f(kvc), _f(out), n_heads, n_kv_heads, head_dim,
+                                       n_q, pos0, kv_len, max_seq, mscale)
     return out.reshape(n_q, n_heads, head_dim)
 
 

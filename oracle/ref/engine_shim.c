@@ -24,6 +24,15 @@ void tgref_rope(float* q, float* k, int seq, int nh, int nkv, int dk, int pos0,
     rope(q, k, seq, nh, nkv, dk, pos0, theta, 0, 0, NULL);
 }
 
+/* rope with NTK-by-parts / YaRN context extension (extend_ctx > max_seq_len);
+ * returns the attention temperature mscale it reports. */
+float tgref_rope_ext(float* q, float* k, int seq, int nh, int nkv, int dk, int pos0,
+                     float theta, int extend_ctx, int max_seq_len) {
+    float ms = 0.0f;
+    rope(q, k, seq, nh, nkv, dk, pos0, theta, extend_ctx, max_seq_len, &ms);
+    return ms;
+}
+
 /* After tg_forward: the last layer's post-RoPE queries [seq][nh][dk]. */
 const float* tgref_work_q(TGModel* m) { return m->work_q; }
 

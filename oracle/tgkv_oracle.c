@@ -90,6 +90,22 @@ static void rope_rows(float* x, int seq, int nh, int d_k, int pos0, float theta)
     }
 }
 
+void orc_rope_tables(float* x, int seq, int nh, int d_k, int pos0, const float* cs,
+                     const float* sn) {
+    const int half = d_k / 2;
+    for (int t = 0; t < seq; t++)
+        for (int h = 0; h < nh; h++) {
+            float* xh = x + ((size_t)t * nh + h) * d_k;
+            for (int i = 0; i < d_k; i += 2) {
+                const float c = cs[(size_t)(pos0 + t) * half + i / 2];
+                const float s = sn[(size_t)(pos0 + t) * half + i / 2];
+                const float x0 = xh[i], x1 = xh[i + 1];
+                xh[i]     = fmaf(x0, c, -(x1 * s));
+                xh[i + 1] = fmaf(x0, s, x1 * c);
+            }
+        }
+}
+
 void orc_rope(float* q, float* k, int seq, int n_heads, int n_kv_heads, int d_k,
               int pos0, float theta) {
     if (q) rope_rows(q, seq, n_heads, d_k, pos0, theta);
@@ -166,11 +182,11 @@ ORC_HOT static void engine_head(const float* qh, const float* kvc, float* oh, fl
     }
 }
 
-void orc_attention_engine(const float* q, const float* kvc, float* out,
-                          int n_heads, int n_kv_heads, int head_dim,
-                          int n_q, int pos0, int kv_len, int max_seq) {
+void orc_attention_engine_scaled(const float* q, const float* kvc, float* out,
+                                 int n_heads, int n_kv_heads, int head_dim,
+                                 int n_q, int pos0, int kv_len, int max_seq, float mscale) {
     int kv_dim = n_kv_heads * head_dim;
-    float inv_sqrt = 1.0f / sqrtf((float)head_dim);
+    float inv_sqrt = (1.0f / sqrtf((float)head_dim)) * mscale;
     float* sc = (float*)malloc(sizeof(float) * (kv_len > 0 ? kv_len : 1));
     for (int t = 0; t < n_q; t++)
         for (int h = 0; h < n_heads; h++) {
@@ -180,6 +196,13 @@ void orc_attention_engine(const float* q, const float* kvc, float* out,
                         head_dim, kv_dim, pos0 + t, kv_len, max_seq, inv_sqrt);
         }
     free(sc);
+}
+
+void orc_attention_engine(const float* q, const float* kvc, float* out,
+                          int n_heads, int n_kv_heads, int head_dim,
+                          int n_q, int pos0, int kv_len, int max_seq) {
+    orc_attention_engine_scaled(q, kvc, out, n_heads, n_kv_heads, head_dim, n_q, pos0, kv_len,
+                                max_seq, 1.0f);
 }
 
 void orc_attention_weights_last(const float* q, const float* kvc, float* w,

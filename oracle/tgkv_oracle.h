@@ -37,6 +37,11 @@ void orc_softmax(float* x, int n);
 void orc_rope(float* q, float* k, int seq, int n_heads, int n_kv_heads, int d_k,
               int pos0, float theta);
 
+/* The same rotation with caller-given tables cs/sn [positions][d_k/2]
+ * (absolute position pos0 + t), e.g. tables with context extension. */
+void orc_rope_tables(float* x, int seq, int nh, int d_k, int pos0, const float* cs,
+                     const float* sn);
+
 /* fp32 -> bf16 bits, round to nearest even (NaN kept quiet). */
 uint16_t orc_f32_to_bf16(float f);
 float    orc_bf16_to_f32(uint16_t h);
@@ -60,6 +65,12 @@ void orc_kv_decode(const void* cache, int dtype, uint32_t max_seq, uint32_t kv_d
 void orc_attention_engine(const float* q, const float* kvc, float* out,
                           int n_heads, int n_kv_heads, int head_dim,
                           int n_q, int pos0, int kv_len, int max_seq);
+
+/* orc_attention_engine with the engine's YaRN temperature: scores scaled by
+ * (1/sqrtf(d_k)) * mscale (src/tgai_engine.c:3947). */
+void orc_attention_engine_scaled(const float* q, const float* kvc, float* out,
+                                 int n_heads, int n_kv_heads, int head_dim,
+                                 int n_q, int pos0, int kv_len, int max_seq, float mscale);
 
 /* Same inputs, double accumulation, following the reference tests'
  * cpu_attention (tests/test_kv_cache_gpu.c:21-54) extended to n_q tokens:

@@ -77,6 +77,23 @@ def engine_pins(eng):
         out[f"rope{ci}_q"], out[f"rope{ci}_k"] = q, k
         out[f"rope{ci}_qout"], out[f"rope{ci}_kout"] = q2, k2
     out["rope_cases"] = np.int32(len(cases))
+    # context extension (NTK-by-parts + YaRN mscale), tgai_engine.c:3404-3460
+    eng.tgref_rope_ext.restype = C.c_float
+    eng.tgref_rope_ext.argtypes = [P, P] + [C.c_int] * 5 + [C.c_float, C.c_int, C.c_int]
+    ext = [(4, 8, 2, 128, 16000, 10000.0, 32768, 8192), (3, 4, 4, 64, 5000, 500000.0, 16384, 4096),
+           (2, 6, 6, 32, 100, 10000.0, 1024, 128)]
+    for ci, (seq, nh, nkv, dk, pos, theta, ectx, msl) in enumerate(ext):
+        q = rng.standard_normal(seq * nh * dk).astype(np.float32)
+        k = rng.standard_normal(seq * nkv * dk).astype(np.float32)
+        q2, k2 = q.copy(), k.copy()
+        ms = eng.tgref_rope_ext(fptr(q2), fptr(k2), seq, nh, nkv, dk, pos, C.c_float(theta),
+                                ectx, msl)
+        out[f"ropex{ci}_shape"] = np.array([seq, nh, nkv, dk, pos, ectx, msl], np.int32)
+        out[f"ropex{ci}_theta"] = np.float32(theta)
+        out[f"ropex{ci}_q"], out[f"ropex{ci}_k"] = q, k
+        out[f"ropex{ci}_qout"], out[f"ropex{ci}_kout"] = q2, k2
+        out[f"ropex{ci}_mscale"] = np.float32(ms)
+    out["ropex_cases"] = np.int32(len(ext))
     np.savez_compressed(os.path.join(HERE, "engine_pins.npz"), **out)
 
 

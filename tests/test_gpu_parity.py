@@ -519,6 +519,56 @@ def test_rope_append_matches_engine_rope(cuda, devbuf, dtype):
     lib.tg_kv_destroy(c)
 
 
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_rope_append_with_context_extension(cuda, devbuf, dtype):
+    """TGBackend.rope with tg_kv_rope_tables' NTK-by-parts tables writes the
+    engine's extended-context K (golden vectors from the compiled engine) into
+    the cache, and attention with the engine's YaRN temperature
+    (tg_kv_set_attn_mscale) matches the oracle at that scale."""
+    lib = cuda
+    z = golden("engine_pins.npz")
+    seq, nh, nkv, dk, pos, ectx, msl = (int(v) for v in z["ropex0_shape"])
+    n = pos + seq
+    cs = np.zeros((n, dk // 2), np.float32)
+    sn = np.zeros_like(cs)
+    ms = C.c_float()
+    assert lib.tg_kv_rope_tables(float(z["ropex0_theta"]), dk, 0, n, ectx, msl,
+                                 cs.ctypes.data_as(tgkv.PF), sn.ctypes.data_as(tgkv.PF),
+                                 C.byref(ms))
+    kvd = nkv * dk
+    rng = np.random.default_rng(99)
+    v = rng.standard_normal((seq, kvd)).astype(np.float32)
+    qkv = np.concatenate([z["ropex0_q"].reshape(seq, nh * dk), z["ropex0_k"].reshape(seq, kvd), v],
+                         axis=1)
+    # fill positions [0, pos) so attention has a context, then rope-append seq rows
+    k_ctx = O.normal(pos * kvd, 4, 1).reshape(pos, kvd)
+    v_ctx = O.normal(pos * kvd, 4, 2).reshape(pos, kvd)
+    c = make_cache(lib, devbuf, n, nkv, dk, dtype, k_ctx, v_ctx)
+    qd, csd, snd = devbuf(np.ascontiguousarray(qkv)), devbuf(cs), devbuf(sn)
+    qo = devbuf(nbytes=seq * nh * dk * 4)
+    be = tgkv.current_backend(lib)
+    assert be.rope(qd.ptr, csd.ptr, snd.ptr, lib.tg_kv_device_handle(c), qo.ptr, seq, nh, nkv, dk,
+                   pos, n)
+    lib.tg_kv_advance(c, seq)
+    rows = cache_rows(lib, c, dtype, n, kvd)
+    kref = z["ropex0_kout"].reshape(seq, kvd)
+    if dtype == 0:
+        assert np.array_equal(rows[0, pos:n].view(np.uint32), kref.view(np.uint32))
+    else:
+        assert np.array_equal(rows[0, pos:n], O.f32_to_bf16(kref))
+    q_rot = qo.get(np.float32, (seq, nh, dk))
+    assert np.array_equal(q_rot.reshape(-1).view(np.uint32),
+                          z["ropex0_qout"].reshape(-1).view(np.uint32))
+    lib.tg_kv_set_attn_mscale(c, ms.value)
+    got = attend(lib, devbuf, c, q_rot, nh, seq)
+    kvc = host_cache(lib, c, dtype, n, kvd)
+    eng = O.attention_engine(q_rot, kvc, nh, nkv, dk, seq, pos, n, n, mscale=ms.value)
+    assert rel_head_err(got, eng) < 1e-5
+    plain = O.attention_engine(q_rot, kvc, nh, nkv, dk, seq, pos, n, n)
+    assert rel_head_err(got, plain) > 1e-3          # the temperature did change the result
+    lib.tg_kv_destroy(c)
+
+
 def test_error_paths(cuda, devbuf):
     lib = cuda
     c = make_cache(lib, devbuf, 8, 2, 64, 0, np.zeros((4, 128), np.float32),

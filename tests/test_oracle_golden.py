@@ -145,3 +145,37 @@ def test_decode_batch_equals_engine_loop(seed):
     for kvc, q, L, o in zip(kvcs, qs, lens, outs):
         ref = O.attention_engine(q, kvc, nh, nkv, hd, 1, L - 1, L, 80).ravel()
         assert np.array_equal(bits(o), bits(ref))
+
+
+def test_rope_tables_with_context_extension_match_engine(lib):
+    """tg_kv_rope_tables (host code of the product, no GPU needed) builds the
+    tables the engine's rope() evaluates inline -- NTK-by-parts frequencies and
+    the YaRN temperature included (src/tgai_engine.c:3404-3460); rotating with
+    them reproduces the engine's bits."""
+    import ctypes as C
+    import tgkv
+    z = load("engine_pins.npz")
+    for ci in range(int(z["ropex_cases"])):
+        seq, nh, nkv, dk, pos, ectx, msl = (int(v) for v in z[f"ropex{ci}_shape"])
+        n = pos + seq
+        cs = np.zeros((n, dk // 2), np.float32)
+        sn = np.zeros_like(cs)
+        ms = C.c_float()
+        assert lib.tg_kv_rope_tables(float(z[f"ropex{ci}_theta"]), dk, 0, n, ectx, msl,
+                                     cs.ctypes.data_as(tgkv.PF), sn.ctypes.data_as(tgkv.PF),
+                                     C.byref(ms))
+        q = O.rope_tables(z[f"ropex{ci}_q"], nh, dk, pos, cs, sn)
+        k = O.rope_tables(z[f"ropex{ci}_k"], nkv, dk, pos, cs, sn)
+        assert np.array_equal(bits(q), bits(z[f"ropex{ci}_qout"])), ci
+        assert np.array_equal(bits(k), bits(z[f"ropex{ci}_kout"])), ci
+        assert np.float32(ms.value) == z[f"ropex{ci}_mscale"]
+    # without extension the tables reproduce the plain rope() pins as well
+    for ci in range(int(z["rope_cases"])):
+        seq, nh, nkv, dk, pos = (int(v) for v in z[f"rope{ci}_shape"])
+        n = pos + seq
+        cs = np.zeros((n, dk // 2), np.float32)
+        sn = np.zeros_like(cs)
+        assert lib.tg_kv_rope_tables(10000.0, dk, 0, n, 0, 0, cs.ctypes.data_as(tgkv.PF),
+                                     sn.ctypes.data_as(tgkv.PF), None)
+        q = O.rope_tables(z[f"rope{ci}_q"], nh, dk, pos, cs, sn)
+        assert np.array_equal(bits(q), bits(z[f"rope{ci}_qout"])), ci

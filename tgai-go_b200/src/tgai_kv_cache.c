@@ -36,6 +36,7 @@ struct TGKvCache {
     void*    tmap;                /* TMA tensor map of dev (NULL: no attention kernel) */
     uint32_t* npos;               /* host item table for attention */
     uint32_t npos_cap;
+    float    mscale;              /* YaRN temperature on the 1/sqrt(head_dim) scale */
 };
 
 static _Thread_local char t_err[256] = "kv: no error";
@@ -86,6 +87,7 @@ TGKvCache* tg_kv_create_ex(uint32_t max_seq, uint32_t n_kv_heads, uint32_t head_
     c->esize = es;
     c->bytes = (size_t)bytes64;
     c->be = b;
+    c->mscale = 1.0f;
     c->dev = b->alloc(c->bytes);              /* zero-filled by the cuda backend */
     if (!c->dev) {
         set_err("device allocation failed: %s", b->last_error ? b->last_error() : "?");
@@ -139,6 +141,15 @@ int tg_kv_dtype(const TGKvCache* c) { return c ? c->dtype : -1; }
 uint32_t tg_kv_n_kv_heads(const TGKvCache* c) { return c ? c->n_kv_heads : 0; }
 uint32_t tg_kv_head_dim(const TGKvCache* c) { return c ? c->head_dim : 0; }
 uint64_t tg_kv_bytes(const TGKvCache* c) { return c ? (uint64_t)c->bytes : 0; }
+
+void tg_kv_set_attn_mscale(TGKvCache* c, float mscale) {
+    if (c) c->mscale = mscale;
+}
+
+/* (1/sqrt(head_dim)) * mscale, as src/tgai_engine.c:3947 forms it */
+static float score_scale(const TGKvCache* c) {
+    return (1.0f / sqrtf((float)c->head_dim)) * c->mscale;
+}
 
 void tg_kv_advance(TGKvCache* c, uint32_t n_tokens) {
     if (!c) return;
@@ -286,7 +297,7 @@ int tg_kv_attention(TGKvCache* c, const float* q_dev, float* out_dev, uint32_t n
     }
     if (!tg_gpu_kv_attention(c->dtype, c->dev, c->max_seq, c->tmap, n_heads, c->n_kv_heads,
                              c->head_dim,
-                             q_dev, out_dev, c->npos, n_q, 1.0f / sqrtf((float)c->head_dim),
+                             q_dev, out_dev, c->npos, n_q, score_scale(c),
                              c->scratch, c->counters, stream)) {
         set_err("%s", tg_gpu_kv_error());
         return 0;
@@ -403,7 +414,7 @@ int tg_kv_batch_decode(TGKvBatch* b, const float* q, const float* k_new, const f
     call.out = out;
     call.n_pos = b->npos;
     call.n_items = b->n;
-    call.scale = 1.0f / sqrtf((float)b->head_dim);
+    call.scale = score_scale(b->caches[0]);
     if (!ensure_attn_scratch(b->be, &call, &b->scratch, &b->scratch_bytes, &b->counters,
                              &b->counter_slots))
         return 0;
