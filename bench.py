@@ -46,6 +46,9 @@ WORKLOADS = {
                  desc="configs[4]: 1 seq, L=131072, 32 layers, 32q/8kv, hd128, bf16"),
     "cfg2": dict(n_seq=1, layers=24, nh=16, nkv=4, hd=128, lmin=4096, lmax=4096,
                  desc="configs[1] at its largest context: 1 seq, L=4096, 24 layers, 16q/4kv, hd128, bf16"),
+    "cfg3": dict(n_seq=1, layers=24, nh=16, nkv=4, hd=128, lmin=64, lmax=512,
+                 desc="configs[2]: multi-turn LCP reuse, keep U[50%,95%] of history, append a "
+                      "U[64,512]-token suffix, causal suffix attention; 24 layers, 16q/4kv, hd128, bf16"),
 }
 
 
@@ -415,6 +418,82 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def turn_script(seed, n_turns, lmin, lmax, vocab=32000):
+    """configs[2]'s turns: (lcp, suffix length) per turn.  Token ids only
+    matter through the LCP (K/V are synthetic), so the script keeps lengths."""
+    rng = np.random.default_rng([seed, 3])
+    hist, out = 0, []
+    for _ in range(n_turns):
+        lcp = int(hist * rng.uniform(0.5, 0.95))
+        n = int(rng.integers(lmin, lmax + 1))
+        out.append((lcp, n))
+        hist = lcp + n
+    return out
+
+
+def run_cfg3(args):
+    """One step = one chat turn over all layers: truncate every layer's cache
+    to the turn's LCP, append the suffix's K/V, attend the suffix queries
+    causally.  tokens/s counts suffix tokens through all layers."""
+    import torch
+    import tgkv
+    lib = tgkv.load()
+    tgkv.check(lib.tg_be_select(b"cuda"), lib, "tg_be_select")
+    wl = WORKLOADS["cfg3"]
+    nh, nkv, hd, layers = wl["nh"], wl["nkv"], wl["hd"], wl["layers"]
+    kvd = nkv * hd
+    turns = turn_script(args.seed, args.warmup + args.steps, wl["lmin"], wl["lmax"])
+    max_len = max(l + n for l, n in turns)
+    stream = torch.cuda.current_stream()
+    sh = tgkv.stream_handle(stream)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed)
+    caches = []
+    for _ in range(layers):
+        c = lib.tg_kv_create_ex(max_len, nkv, hd, tgkv.TG_KV_BF16)
+        tgkv.check(c, lib, "tg_kv_create_ex")
+        caches.append(c)
+    nmax = wl["lmax"]
+    q = [torch.randn(nmax, nh, hd, device="cuda", generator=gen) for _ in range(layers)]
+    k = [torch.randn(nmax, kvd, device="cuda", generator=gen) for _ in range(layers)]
+    v = [torch.randn(nmax, kvd, device="cuda", generator=gen) for _ in range(layers)]
+    out = [torch.empty(nmax, nh, hd, device="cuda") for _ in range(layers)]
+
+    def turn(lcp, n):
+        for l in range(layers):
+            c = caches[l]
+            tgkv.check(lib.tg_kv_truncate(c, min(lcp, lib.tg_kv_len(c))), lib, "truncate")
+            tgkv.check(lib.tg_kv_append_dev(c, k[l].data_ptr(), v[l].data_ptr(), n, sh), lib,
+                       "append")
+            tgkv.check(lib.tg_kv_attention(c, q[l].data_ptr(), out[l].data_ptr(), nh, n, sh), lib,
+                       "attention")
+
+    for lcp, n in turns[:args.warmup]:
+        turn(lcp, n)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for lcp, n in turns[args.warmup:]:
+        turn(lcp, n)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    timed = turns[args.warmup:]
+    tokens = sum(n for _, n in timed)
+    # causal suffix attention FLOPs (QK^T + PV) over all layers
+    flops = sum(4.0 * nh * hd * sum(l + j + 1 for j in range(n)) for l, n in timed) * layers
+    for c in caches:
+        lib.tg_kv_destroy(c)
+    line = {"metric": METRIC, "value": tokens / (ms / 1000.0), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "cfg3", "desc": wl["desc"], "turns": timed},
+            "attention_tflops": flops / (ms / 1000.0) / 1e12}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -439,6 +518,8 @@ def main():
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "cfg3":
+        run_cfg3(args)
     else:
         run_ours(args)
 

@@ -61,6 +61,7 @@ typedef struct {
     uint32_t max_seq;
     uint32_t pad;
     uint64_t tmap;               /* from tg_cuda_kv_tmap_create / _write */
+    uint64_t tmap_sw;            /* bf16 head_dim 128 caches: tg_cuda_kv_tmap_sw_create, or 0 */
 } TGCudaCacheDesc;
 
 /* TMA tensor map of a cache buffer for the attention kernel, in device memory
@@ -70,6 +71,9 @@ void* tg_cuda_kv_tmap_create(int dtype, uint64_t base, uint32_t max_seq, uint32_
                              uint32_t head_dim);
 int   tg_cuda_kv_tmap_write(int dtype, uint64_t base, uint32_t max_seq, uint32_t n_kv_heads,
                             uint32_t head_dim, void* tmap_dev);
+/* The second map of a bf16 head_dim-128 cache for the tensor-core suffix
+ * kernel: 128-byte swizzle, box (64 dims, 128 positions, 1). */
+void* tg_cuda_kv_tmap_sw_create(uint64_t base, uint32_t max_seq, uint32_t n_kv_heads);
 
 /* Append rows (fp32 device sources [n_rows][kv_dim]) into one cache starting at
  * row `row0`, storing dtype (0 = fp32, 1 = bf16 round-to-nearest-even). */

@@ -91,8 +91,9 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 static EncodeTiledFn g_encode = NULL;
 
-static int encode_tmap(int dtype, uint64_t base, uint32_t max_seq, uint32_t n_kv_heads,
-                       uint32_t head_dim, CUtensorMap* out) {
+static int encode_tmap_box(int dtype, uint64_t base, uint32_t max_seq, uint32_t n_kv_heads,
+                           uint32_t head_dim, uint32_t box_x, uint32_t box_y, int swizzle128,
+                           CUtensorMap* out) {
     if (!g_encode) {
         enum cudaDriverEntryPointQueryResult q;
         void* fn = NULL;
@@ -111,18 +112,38 @@ static int encode_tmap(int dtype, uint64_t base, uint32_t max_seq, uint32_t n_kv
     }
     cuuint64_t dims[3] = {kv_dim, max_seq, 2};
     cuuint64_t strides[2] = {kv_dim * es, (uint64_t)max_seq * kv_dim * es};
-    cuuint32_t box[3] = {head_dim, TGKV_TILE, 1};
+    cuuint32_t box[3] = {box_x, box_y, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = g_encode(out, dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                           3, (void*)(uintptr_t)base, dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_err("cuTensorMapEncodeTiled failed (%d)", (int)r);
         return 0;
     }
     return 1;
+}
+
+static int encode_tmap(int dtype, uint64_t base, uint32_t max_seq, uint32_t n_kv_heads,
+                       uint32_t head_dim, CUtensorMap* out) {
+    return encode_tmap_box(dtype, base, max_seq, n_kv_heads, head_dim, head_dim, TGKV_TILE, 0,
+                           out);
+}
+
+void* tg_cuda_kv_tmap_sw_create(uint64_t base, uint32_t max_seq, uint32_t n_kv_heads) {
+    if (!g_ready && !tg_cuda_kv_init()) return NULL;
+    CUtensorMap m;
+    if (!encode_tmap_box(1, base, max_seq, n_kv_heads, 128, 64, 128, 1, &m)) return NULL;
+    void* d = tg_cuda_kv_malloc(sizeof(CUtensorMap));
+    if (!d) return NULL;
+    if (!cuda_ok(cudaMemcpy(d, &m, sizeof(m), cudaMemcpyHostToDevice), "tensor map h2d")) {
+        tg_cuda_kv_free(d);
+        return NULL;
+    }
+    return d;
 }
 
 int tg_cuda_kv_tmap_write(int dtype, uint64_t base, uint32_t max_seq, uint32_t n_kv_heads,
@@ -380,6 +401,23 @@ uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c) {
 
 uint32_t tg_cuda_kv_attn_last_launches(void) { return t_last_launches; }
 
+/* Blocks of query rows over one bf16 head_dim-128 cache go to the tensor-core
+ * kernel (tgkv_prefill.cu) when there are at least 128 (row, head) pairs:
+ * consecutive positions, group size 1/2/4/8, no fused append.  TGKV_PREFILL=0
+ * keeps them on the split-sequence kernel. */
+static int use_prefill(const TGCudaAttnCall* c) {
+    const char* e = getenv("TGKV_PREFILL");
+    if (e && e[0] == '0') return 0;
+    if (c->dtype != 1 || c->head_dim != 128 || c->table_dev || !c->cache.tmap_sw || c->k_new)
+        return 0;
+    const uint32_t g = c->n_heads / c->n_kv_heads;
+    if (!(g == 1 || g == 2 || g == 4 || g == 8)) return 0;
+    if ((uint64_t)c->n_items * g < 128) return 0;
+    for (uint32_t i = 1; i < c->n_items; i++)
+        if (c->n_pos[i] != c->n_pos[0] + i) return 0;
+    return 1;
+}
+
 int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
     t_last_launches = 0;
     if (!g_ready && !tg_cuda_kv_init()) return 0;
@@ -398,6 +436,21 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         set_err("attention: k_new and v_new go together");
         return 0;
     }
+    if (use_prefill(c)) {
+        TGKvPrefillParams pp;
+        pp.tmap_sw = c->cache.tmap_sw;
+        pp.q = c->q;
+        pp.out = c->out;
+        pp.err = g_err_word;
+        pp.n_q = c->n_items;
+        pp.n_heads = c->n_heads;
+        pp.n_kv_heads = c->n_kv_heads;
+        pp.pos0 = c->n_pos[0] - 1;
+        pp.qscale = c->scale * 1.4426950408889634f;
+        if (!launch_rc(tgkv_launch_prefill(&pp, stream), "prefill kernel")) return 0;
+        t_last_launches = 1;
+        return 1;
+    }
     if (!c->scratch || !c->counters) {
         set_err("attention: split-sequence scratch not provided");
         return 0;
@@ -411,6 +464,7 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         p.cache0.base = c->cache.base;
         p.cache0.max_seq = c->cache.max_seq;
         p.cache0.tmap = c->cache.tmap;
+        p.cache0.tmap_sw = c->cache.tmap_sw;
         p.q = c->q;
         p.out = c->out;
         p.k_new = c->k_new ? c->k_new + (uint64_t)b0 * c->n_kv_heads * c->head_dim : NULL;

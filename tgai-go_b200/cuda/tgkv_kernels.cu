@@ -31,100 +31,19 @@
 #include <string.h>
 #include <mutex>
 #include "tgkv_launch.h"
+#include "tgkv_ptx.cuh"
 
 namespace tgkv {
 
 constexpr int kTile = TGKV_TILE;     // positions per stage
 constexpr int kConsumerWarps = 4;    // 8 positions of a stage per warp
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s
 constexpr int kFacBlock = 256;       // partials merged per block in the combine
 
 
 // Error codes written to p.err.
 constexpr int kErrFullTimeout = 1;
 constexpr int kErrEmptyTimeout = 2;
-
-// ---------------------------------------------------------------- PTX helpers
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
-                 : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ unsigned long long global_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Wait for the phase with the given parity to complete; false after ~2 s.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = global_ns();
-    for (;;) {
-        for (int i = 0; i < 256; ++i)
-            if (mbar_try_wait(bar, parity)) return true;
-        if (global_ns() - t0 > kWaitLimitNs) return false;
-    }
-}
-
-// Tiled TMA load of one box of a 3-D tensor map into shared memory.
-__device__ __forceinline__ void tma_load_3d(void* dst, uint64_t tmap, int x, int y, int z,
-                                            uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
-        "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void prefetch_tmap(uint64_t tmap) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
-}
-
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-    return __ffma2_rn(a, b, c);
-}
-
-__device__ __forceinline__ float2 bf16pair_to_f2(uint32_t w) {
-    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
-}
-
-__device__ __forceinline__ uint16_t f32_to_bf16_rne(float f) {
-    // Same rule as the host oracle: NaN stays a quiet NaN, else round to
-    // nearest even on the upper 16 bits.
-    uint32_t u = __float_as_uint(f);
-    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu))
-        return static_cast<uint16_t>((u >> 16) | 0x0040u);
-    u += 0x7fffu + ((u >> 16) & 1u);
-    return static_cast<uint16_t>(u >> 16);
-}
 
 }  // namespace tgkv
 

@@ -25,6 +25,7 @@ typedef struct {
     uint32_t max_seq;
     uint32_t pad;
     uint64_t tmap;               /* device address of a 64-byte aligned CUtensorMap */
+    uint64_t tmap_sw;            /* bf16, head_dim 128: 128B-swizzled map, box (64,128,1), or 0 */
 } TGKvCacheDesc;
 
 /* Split-sequence decode attention.
@@ -88,7 +89,23 @@ typedef struct {
     int      dtype;
 } TGKvRopeParams;
 
-/* Launchers (tgkv_kernels.cu).  Return 0 on success, else a cudaError_t. */
+/* Tensor-core causal attention of n_q consecutive query rows over one bf16
+ * cache with head_dim 128 (tgkv_prefill.cu).  Query row t sits at position
+ * pos0 + t.  Grid (ceil(n_q / (128/G)), n_kv_heads), G = n_heads/n_kv_heads
+ * in {1, 2, 4, 8}. */
+typedef struct {
+    uint64_t     tmap_sw;        /* device address: tensor map with 128B swizzle, box (64,128,1) */
+    const float* q;              /* [n_q][n_heads][128] fp32 */
+    float*       out;            /* same shape */
+    int32_t*     err;
+    uint32_t n_q, n_heads, n_kv_heads;
+    uint32_t pos0;
+    float    qscale;             /* softmax scale * log2(e) */
+} TGKvPrefillParams;
+
+/* Launchers (tgkv_kernels.cu, tgkv_prefill.cu).  Return 0 on success, else a
+ * cudaError_t. */
+int tgkv_launch_prefill(const TGKvPrefillParams* p, void* stream);
 int tgkv_launch_attention(const TGKvAttnParams* p, int dtype, uint32_t head_dim,
                           uint32_t g_tile, uint32_t grid, void* stream);
 int tgkv_launch_append(const TGKvAppendParams* p, int dtype, void* stream);

@@ -149,7 +149,7 @@ int tg_gpu_kv_append_dev(int dtype, void* base, uint32_t max_seq, uint32_t kv_di
                          uint32_t row0, const float* k, const float* v, uint32_t n,
                          void* stream) {
     if (!route_begin()) return 0;
-    TGCudaCacheDesc d = {(uint64_t)(uintptr_t)base, max_seq, 0, 0};
+    TGCudaCacheDesc d = {(uint64_t)(uintptr_t)base, max_seq, 0, 0, 0};
     return route_end(tg_cuda_kv_append(dtype, d, kv_dim, row0, k, v, n, stream));
 }
 

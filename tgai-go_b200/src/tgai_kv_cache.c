@@ -34,6 +34,7 @@ struct TGKvCache {
     float*   staging;             /* device staging of host rows (bf16 append) */
     size_t   staging_bytes;
     void*    tmap;                /* TMA tensor map of dev (NULL: no attention kernel) */
+    void*    tmap_sw;             /* swizzled map for the tensor-core suffix kernel, or NULL */
     uint32_t* npos;               /* host item table for attention */
     uint32_t npos_cap;
     float    mscale;              /* YaRN temperature on the 1/sqrt(head_dim) scale */
@@ -100,6 +101,17 @@ TGKvCache* tg_kv_create_ex(uint32_t max_seq, uint32_t n_kv_heads, uint32_t head_
                                          head_dim);
         if (!c->tmap) {
             set_err("tensor map: %s", tg_cuda_kv_last_error());
+            b->free(c->dev);
+            free(c);
+            return NULL;
+        }
+    }
+    if (dtype == TG_KV_BF16 && head_dim == 128) {
+        c->tmap_sw = tg_cuda_kv_tmap_sw_create((uint64_t)(uintptr_t)c->dev, max_seq, n_kv_heads);
+        if (!c->tmap_sw) {
+            set_err("tensor map: %s", tg_cuda_kv_last_error());
+            if (c->tmap) tg_cuda_kv_free(c->tmap);
+    if (c->tmap_sw) tg_cuda_kv_free(c->tmap_sw);
             b->free(c->dev);
             free(c);
             return NULL;
@@ -286,6 +298,7 @@ int tg_kv_attention(TGKvCache* c, const float* q_dev, float* out_dev, uint32_t n
     call.cache.base = (uint64_t)(uintptr_t)c->dev;
     call.cache.max_seq = c->max_seq;
     call.cache.tmap = (uint64_t)(uintptr_t)c->tmap;
+    call.cache.tmap_sw = (uint64_t)(uintptr_t)c->tmap_sw;
     call.n_pos = c->npos;
     call.n_items = n_q;
     if (!ensure_attn_scratch(c->be, &call, &c->scratch, &c->scratch_bytes, &c->counters,

@@ -28,7 +28,7 @@ class TGBackendInfo(C.Structure):
 
 
 class TGCudaCacheDesc(C.Structure):
-    _fields_ = [("base", u64), ("max_seq", u32), ("pad", u32), ("tmap", u64)]
+    _fields_ = [("base", u64), ("max_seq", u32), ("pad", u32), ("tmap", u64), ("tmap_sw", u64)]
 
 
 # struct TGBackend of include/tgai_backend.h (src/tgai_backend.h:55-94 order)
@@ -128,6 +128,7 @@ PROTOS = {
     "tg_cuda_kv_inject_alloc_failures": (None, [i32]),
     "tg_cuda_kv_tmap_create": (vp, [i32, u64, u32, u32, u32]),
     "tg_cuda_kv_tmap_write": (i32, [i32, u64, u32, u32, u32, vp]),
+    "tg_cuda_kv_tmap_sw_create": (vp, [u64, u32, u32]),
     "tg_cuda_kv_append": (i32, [i32, TGCudaCacheDesc, u32, u32, vp, vp, u32, vp]),
     "tg_cuda_kv_append_batch": (i32, [i32, vp, u32, PU32, u32, vp, vp, vp]),
     "tg_cuda_kv_attn_supported": (i32, [i32, u32]),
