@@ -479,6 +479,7 @@ def run_cfg3(args):
     t1.record(stream)
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1)
+    kernel = {1: "split-sequence", 2: "tcgen05 suffix"}.get(lib.tg_cuda_kv_attn_last_kernel(), "?")
     timed = turns[args.warmup:]
     tokens = sum(n for _, n in timed)
     # causal suffix attention FLOPs (QK^T + PV) over all layers
@@ -489,7 +490,8 @@ def run_cfg3(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": "cfg3", "desc": wl["desc"], "turns": timed},
+            "config": {"workload": "cfg3", "desc": wl["desc"], "turns": timed,
+                       "attention_kernel": kernel},
             "attention_tflops": flops / (ms / 1000.0) / 1e12}
     print(json.dumps(line), flush=True)
 

@@ -110,6 +110,12 @@ uint64_t tg_cuda_kv_attn_scratch_bytes(const TGCudaAttnCall* c);
 uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c);
 /* Launches made by the last tg_cuda_kv_attention on this thread. */
 uint32_t tg_cuda_kv_attn_last_launches(void);
+/* Kernel family of this thread's last tg_cuda_kv_attention call:
+ * 0 none, 1 split-sequence (tgkv_kernels.cu), 2 tensor-core suffix
+ * (tgkv_prefill.cu). */
+int tg_cuda_kv_attn_last_kernel(void);
+/* CTAs per row block (KV split) of the last tensor-core suffix launch. */
+uint32_t tg_cuda_kv_attn_last_split(void);
 int      tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream);
 
 /* RoPE + KV write, shaders/rope.comp semantics (see TGBackend.rope). */

@@ -42,8 +42,10 @@ const void* tg_gpu_kv_lookup_tmap(const void* base, uint32_t max_seq, uint32_t n
 int tg_gpu_kv_append_dev(int dtype, void* base, uint32_t max_seq, uint32_t kv_dim,
                          uint32_t row0, const float* k, const float* v, uint32_t n,
                          void* stream);
+/* tmap: the cache's tensor map; tmap_sw: its 128B-swizzled map (bf16
+ * head_dim-128 caches, for the tensor-core suffix kernel) or NULL. */
 int tg_gpu_kv_attention(int dtype, void* base, uint32_t max_seq, const void* tmap,
-                        uint32_t n_heads,
+                        const void* tmap_sw, uint32_t n_heads,
                         uint32_t n_kv_heads, uint32_t head_dim, const float* q, float* out,
                         const uint32_t* n_pos, uint32_t n_items, float scale,
                         void* scratch, uint32_t* counters, void* stream);

@@ -21,6 +21,8 @@
 
 static _Thread_local char t_err[256] = "cuda bridge: no error";
 static _Thread_local uint32_t t_last_launches = 0;
+static _Thread_local int t_last_kernel = 0;
+static _Thread_local uint32_t t_last_split = 0;
 
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
 static int g_ready = 0;
@@ -400,10 +402,13 @@ uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c) {
 }
 
 uint32_t tg_cuda_kv_attn_last_launches(void) { return t_last_launches; }
+int tg_cuda_kv_attn_last_kernel(void) { return t_last_kernel; }
+uint32_t tg_cuda_kv_attn_last_split(void) { return t_last_split; }
 
 /* Blocks of query rows over one bf16 head_dim-128 cache go to the tensor-core
  * kernel (tgkv_prefill.cu) when there are at least 128 (row, head) pairs:
- * consecutive positions, group size 1/2/4/8, no fused append.  TGKV_PREFILL=0
+ * consecutive positions, group size 1/2/4/8, no fused append, q and out
+ * 16-byte aligned.  TGKV_PREFILL=0
  * keeps them on the split-sequence kernel. */
 static int use_prefill(const TGCudaAttnCall* c) {
     const char* e = getenv("TGKV_PREFILL");
@@ -413,13 +418,36 @@ static int use_prefill(const TGCudaAttnCall* c) {
     const uint32_t g = c->n_heads / c->n_kv_heads;
     if (!(g == 1 || g == 2 || g == 4 || g == 8)) return 0;
     if ((uint64_t)c->n_items * g < 128) return 0;
+    if (((uintptr_t)c->q | (uintptr_t)c->out) & 15u) return 0;   /* float4 rows */
     for (uint32_t i = 1; i < c->n_items; i++)
         if (c->n_pos[i] != c->n_pos[0] + i) return 0;
     return 1;
 }
 
+/* KV split of the suffix kernel: the most CTAs per row block (<= 8) that
+ * keep the launch to one wave of clusters, no more than the first row block
+ * has tiles.  TGKV_PF_SPLIT=n forces n (clamped to the same limits). */
+static uint32_t prefill_split(const TGCudaAttnCall* c, uint32_t pos0) {
+    const uint32_t g = c->n_heads / c->n_kv_heads;
+    const uint32_t toks = 128 / g;
+    const uint32_t blocks = (c->n_items + toks - 1) / toks * c->n_kv_heads;
+    const uint32_t first = c->n_items < toks ? c->n_items : toks;
+    const uint32_t tiles0 = (pos0 + first - 1) / 128 + 1;
+    const char* e = getenv("TGKV_PF_SPLIT");
+    uint32_t cap = e && atoi(e) > 0 ? (uint32_t)atoi(e) : 8;
+    if (cap > 8) cap = 8;
+    if (cap > tiles0) cap = tiles0;
+    for (uint32_t ns = cap; ns > 1; ns--) {
+        if (e && atoi(e) > 0) return ns;
+        if ((uint64_t)blocks * ns <= (uint64_t)g_sm_count && blocks <= tgkv_prefill_max_clusters(ns)) return ns;
+    }
+    return 1;
+}
+
 int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
     t_last_launches = 0;
+    t_last_kernel = 0;
+    t_last_split = 0;
     if (!g_ready && !tg_cuda_kv_init()) return 0;
     AttnPlan pl;
     if (!plan_attention(c, &pl)) return 0;
@@ -447,8 +475,11 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         pp.n_kv_heads = c->n_kv_heads;
         pp.pos0 = c->n_pos[0] - 1;
         pp.qscale = c->scale * 1.4426950408889634f;
+        pp.n_split = prefill_split(c, pp.pos0);
+        t_last_split = pp.n_split;
         if (!launch_rc(tgkv_launch_prefill(&pp, stream), "prefill kernel")) return 0;
         t_last_launches = 1;
+        t_last_kernel = 2;
         return 1;
     }
     if (!c->scratch || !c->counters) {
@@ -493,6 +524,7 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
                        "attention kernel"))
             return 0;
         t_last_launches++;
+        t_last_kernel = 1;
     }
     return 1;
 }

@@ -91,21 +91,26 @@ typedef struct {
 
 /* Tensor-core causal attention of n_q consecutive query rows over one bf16
  * cache with head_dim 128 (tgkv_prefill.cu).  Query row t sits at position
- * pos0 + t.  Grid (ceil(n_q / (128/G)), n_kv_heads), G = n_heads/n_kv_heads
- * in {1, 2, 4, 8}. */
+ * pos0 + t.  Grid (ceil(n_q / (128/G)), n_kv_heads, n_split) in clusters of
+ * (1, 1, n_split): the n_split CTAs of a row block share its KV tiles and
+ * merge through distributed shared memory.  G = n_heads/n_kv_heads in
+ * {1, 2, 4, 8}; n_split in [1, 8]. */
 typedef struct {
     uint64_t     tmap_sw;        /* device address: tensor map with 128B swizzle, box (64,128,1) */
-    const float* q;              /* [n_q][n_heads][128] fp32 */
+    const float* q;              /* [n_q][n_heads][128] fp32, 16-byte aligned */
     float*       out;            /* same shape */
     int32_t*     err;
     uint32_t n_q, n_heads, n_kv_heads;
     uint32_t pos0;
     float    qscale;             /* softmax scale * log2(e) */
+    uint32_t n_split;
 } TGKvPrefillParams;
 
 /* Launchers (tgkv_kernels.cu, tgkv_prefill.cu).  Return 0 on success, else a
  * cudaError_t. */
 int tgkv_launch_prefill(const TGKvPrefillParams* p, void* stream);
+/* Clusters of n_split prefill CTAs resident at once on the current device. */
+uint32_t tgkv_prefill_max_clusters(uint32_t n_split);
 int tgkv_launch_attention(const TGKvAttnParams* p, int dtype, uint32_t head_dim,
                           uint32_t g_tile, uint32_t grid, void* stream);
 int tgkv_launch_append(const TGKvAppendParams* p, int dtype, void* stream);

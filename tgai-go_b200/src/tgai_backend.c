@@ -119,7 +119,7 @@ static int cu_attention(void* q, void* kvc, void* out, uint32_t nh, uint32_t nkv
         ok = g_counters != NULL;
     }
     if (ok)
-        ok = tg_gpu_kv_attention(dtype, kvc, max_seq, tmap, nh, nkvh, hd, c.q, c.out, &n, 1,
+        ok = tg_gpu_kv_attention(dtype, kvc, max_seq, tmap, NULL, nh, nkvh, hd, c.q, c.out, &n, 1,
                                  c.scale,
                                  g_scratch, g_counters, NULL) &&
              tg_cuda_kv_sync(NULL);

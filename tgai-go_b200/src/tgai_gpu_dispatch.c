@@ -154,7 +154,7 @@ int tg_gpu_kv_append_dev(int dtype, void* base, uint32_t max_seq, uint32_t kv_di
 }
 
 int tg_gpu_kv_attention(int dtype, void* base, uint32_t max_seq, const void* tmap,
-                        uint32_t n_heads,
+                        const void* tmap_sw, uint32_t n_heads,
                         uint32_t n_kv_heads, uint32_t head_dim, const float* q, float* out,
                         const uint32_t* n_pos, uint32_t n_items, float scale,
                         void* scratch, uint32_t* counters, void* stream) {
@@ -168,6 +168,7 @@ int tg_gpu_kv_attention(int dtype, void* base, uint32_t max_seq, const void* tma
     c.cache.base = (uint64_t)(uintptr_t)base;
     c.cache.max_seq = max_seq;
     c.cache.tmap = (uint64_t)(uintptr_t)tmap;
+    c.cache.tmap_sw = (uint64_t)(uintptr_t)tmap_sw;
     c.q = q;
     c.out = out;
     c.n_pos = n_pos;

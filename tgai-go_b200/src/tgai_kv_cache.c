@@ -308,7 +308,8 @@ int tg_kv_attention(TGKvCache* c, const float* q_dev, float* out_dev, uint32_t n
         set_err("attention: no kernel for dtype %d head_dim %u", c->dtype, c->head_dim);
         return 0;
     }
-    if (!tg_gpu_kv_attention(c->dtype, c->dev, c->max_seq, c->tmap, n_heads, c->n_kv_heads,
+    if (!tg_gpu_kv_attention(c->dtype, c->dev, c->max_seq, c->tmap, c->tmap_sw, n_heads,
+                             c->n_kv_heads,
                              c->head_dim,
                              q_dev, out_dev, c->npos, n_q, score_scale(c),
                              c->scratch, c->counters, stream)) {

@@ -106,7 +106,7 @@ PROTOS = {
     "tg_gpu_kv_unregister": (None, [vp]),
     "tg_gpu_kv_lookup_dtype": (i32, [vp]),
     "tg_gpu_kv_append_dev": (i32, [i32, vp, u32, u32, u32, vp, vp, u32, vp]),
-    "tg_gpu_kv_attention": (i32, [i32, vp, u32, vp, u32, u32, u32, vp, vp, PU32, u32, fp,
+    "tg_gpu_kv_attention": (i32, [i32, vp, u32, vp, vp, u32, u32, u32, vp, vp, PU32, u32, fp,
                                   vp, vp, vp]),
     "tg_gpu_kv_error": (cp, []),
     # tgai_cuda_bridge.h
@@ -135,6 +135,8 @@ PROTOS = {
     "tg_cuda_kv_attn_scratch_bytes": (u64, [vp]),
     "tg_cuda_kv_attn_counters": (u64, [vp]),
     "tg_cuda_kv_attn_last_launches": (u32, []),
+    "tg_cuda_kv_attn_last_kernel": (i32, []),
+    "tg_cuda_kv_attn_last_split": (u32, []),
     "tg_cuda_kv_attention": (i32, [vp, vp]),
     "tg_cuda_kv_rope_append": (i32, [i32, vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32,
                                      vp]),
