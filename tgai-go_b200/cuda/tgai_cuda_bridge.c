@@ -93,19 +93,23 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 static EncodeTiledFn g_encode = NULL;
 
+static int resolve_encode(void) {
+    if (g_encode) return 1;
+    enum cudaDriverEntryPointQueryResult q;
+    void* fn = NULL;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+            cudaSuccess || !fn) {
+        set_err("cuTensorMapEncodeTiled unavailable");
+        return 0;
+    }
+    g_encode = (EncodeTiledFn)fn;
+    return 1;
+}
+
 static int encode_tmap_box(int dtype, uint64_t base, uint32_t max_seq, uint32_t n_kv_heads,
                            uint32_t head_dim, uint32_t box_x, uint32_t box_y, int swizzle128,
                            CUtensorMap* out) {
-    if (!g_encode) {
-        enum cudaDriverEntryPointQueryResult q;
-        void* fn = NULL;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
-                cudaSuccess || !fn) {
-            set_err("cuTensorMapEncodeTiled unavailable");
-            return 0;
-        }
-        g_encode = (EncodeTiledFn)fn;
-    }
+    if (!resolve_encode()) return 0;
     const uint64_t es = dtype == 1 ? 2 : 4;
     const uint64_t kv_dim = (uint64_t)n_kv_heads * head_dim;
     if ((base & 15u) || (kv_dim * es) % 16 || (head_dim * es) % 16 || head_dim > 256) {
@@ -133,6 +137,25 @@ static int encode_tmap(int dtype, uint64_t base, uint32_t max_seq, uint32_t n_kv
                        uint32_t head_dim, CUtensorMap* out) {
     return encode_tmap_box(dtype, base, max_seq, n_kv_heads, head_dim, head_dim, TGKV_TILE, 0,
                            out);
+}
+
+/* The suffix kernel's map over q [n_q][n_heads][128] fp32: dims (128,
+ * n_heads, n_q), 128B swizzle, box (32, g, 128/g) -- 32 head dims of the 128
+ * (token, head) rows one CTA owns; rows past n_q read as zero. */
+static int encode_qmap(const float* q, uint32_t n_heads, uint32_t n_q, uint32_t g, CUtensorMap* out) {
+    if (!resolve_encode()) return 0;
+    cuuint64_t dims[3] = {128, n_heads, n_q};
+    cuuint64_t strides[2] = {128 * 4, (uint64_t)n_heads * 128 * 4};
+    cuuint32_t box[3] = {32, g, 128 / g};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)q, dims, strides, box,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_err("cuTensorMapEncodeTiled (q) failed (%d)", (int)r);
+        return 0;
+    }
+    return 1;
 }
 
 void* tg_cuda_kv_tmap_sw_create(uint64_t base, uint32_t max_seq, uint32_t n_kv_heads) {
@@ -476,6 +499,8 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         pp.pos0 = c->n_pos[0] - 1;
         pp.qscale = c->scale * 1.4426950408889634f;
         pp.n_split = prefill_split(c, pp.pos0);
+        if (!encode_qmap(c->q, c->n_heads, c->n_items, c->n_heads / c->n_kv_heads, &pp.qmap))
+            return 0;
         t_last_split = pp.n_split;
         if (!launch_rc(tgkv_launch_prefill(&pp, stream), "prefill kernel")) return 0;
         t_last_launches = 1;

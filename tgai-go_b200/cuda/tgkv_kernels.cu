@@ -539,8 +539,11 @@ namespace tgkv {
 // ------------------------------------------------------------ append
 // One thread moves 8 consecutive elements of one K or V row (blockIdx.y picks
 // K or V): two 16-byte loads of fp32, one or two 16-byte stores.
+// The attention launched next (a programmatic dependent) may start its
+// setup right away; it reads nothing before this grid has completed.
 template <int DT>
 __global__ void __launch_bounds__(256) append_kernel(const __grid_constant__ TGKvAppendParams p) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint64_t vec_per_row = p.kv_dim / 8;
     const uint64_t rows = (uint64_t)p.n_items * p.rows_per_item;
     const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;

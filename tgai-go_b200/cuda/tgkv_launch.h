@@ -9,6 +9,7 @@
 #ifndef TGKV_LAUNCH_H
 #define TGKV_LAUNCH_H
 #include <stdint.h>
+#include <cuda.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -96,6 +97,9 @@ typedef struct {
  * merge through distributed shared memory.  G = n_heads/n_kv_heads in
  * {1, 2, 4, 8}; n_split in [1, 8]. */
 typedef struct {
+    /* q as a 3-D map (128 head dims, n_heads, n_q), fp32, 128B swizzle, box
+     * (32, G, 128/G): one box = 32 head dims of a CTA's 128 rows */
+    CUtensorMap  qmap;
     uint64_t     tmap_sw;        /* device address: tensor map with 128B swizzle, box (64,128,1) */
     const float* q;              /* [n_q][n_heads][128] fp32, 16-byte aligned */
     float*       out;            /* same shape */
