@@ -348,32 +348,47 @@ typedef struct {
 
 static uint32_t round_up32(uint64_t x) { return (uint32_t)((x + TGKV_TILE - 1) / TGKV_TILE * TGKV_TILE); }
 
-/* Chunk length (one CTA per chunk; the hardware block scheduler balances
- * uneven CTAs): about eight waves of two CTAs per SM over the whole call, but
- * at least 48 tiles (1536 positions) per CTA as long as that still fills one
- * wave -- short chunks pay the per-CTA start-up and more partials to merge --
- * and never below 128 positions.  A multiple of the TMA tile.  TGKV_CHUNK
- * overrides (tests use it to force split boundaries), TGKV_WAVES changes the
- * wave target. */
-__attribute__((visibility("hidden"))) uint32_t tgkv_pick_chunk(uint64_t total_positions,
-                                                             uint32_t sm_count) {
-    const char* e = getenv("TGKV_CHUNK");
-    if (e && e[0] && atol(e) >= 1) return round_up32((uint64_t)atol(e));
-    const char* w = getenv("TGKV_WAVES");
-    const uint64_t waves = (w && w[0] && atol(w) >= 1) ? (uint64_t)atol(w) : 8;
-    const uint64_t slots = (uint64_t)(sm_count ? sm_count : 148) * 2;
-    uint64_t c = (total_positions + slots * waves - 1) / (slots * waves);
-    if (c < 1536) {
-        const uint64_t one_wave = (total_positions + slots - 1) / slots;
-        c = one_wave < 1536 ? one_wave : 1536;
-    }
-    if (c < 128) c = 128;
-    if (c > (1u << 30)) c = 1u << 30;
-    return round_up32(c);
+/* Chunk length (one CTA per chunk of one item's positions for one KV head
+ * and head subset).  CTAs run in waves of two per SM, and every wave costs a
+ * fixed start-up, tail and merge time besides its streaming, measured on B200
+ * at about the time of 768 positions per CTA (cfg5: 103 / 124 / 139 us per
+ * layer at 1 / 2 / 3 waves against 83 us of pure streaming).  So the planner
+ * takes, over targets of 1 to 16 waves, the chunk whose exact CTA count
+ * minimises waves x (chunk + 768); never below 128 positions, a multiple of
+ * the TMA tile.  TGKV_CHUNK overrides (tests use it to force split
+ * boundaries); TGKV_WAVES fixes the wave target. */
+enum { kWaveOverheadPositions = 768 };
+
+static uint64_t count_chunks(const uint32_t* n_pos, uint32_t n_items, uint64_t chunk, uint32_t mult) {
+    uint64_t n = 0;
+    for (uint32_t i = 0; i < n_items; i++) n += (n_pos[i] + chunk - 1) / chunk;
+    return n * mult;
 }
 
-static uint32_t pick_chunk(uint64_t total_positions) {
-    return tgkv_pick_chunk(total_positions, (uint32_t)g_sm_count);
+__attribute__((visibility("hidden"))) uint32_t tgkv_pick_chunk(const uint32_t* n_pos, uint32_t n_items,
+                                                             uint32_t mult, uint32_t sm_count) {
+    const char* e = getenv("TGKV_CHUNK");
+    if (e && e[0] && atol(e) >= 1) return round_up32((uint64_t)atol(e));
+    const uint64_t slots = (uint64_t)(sm_count ? sm_count : 148) * 2;
+    uint64_t total = 0;
+    for (uint32_t i = 0; i < n_items; i++) total += n_pos[i];
+    total *= mult;
+    const char* w = getenv("TGKV_WAVES");
+    const uint64_t forced = (w && w[0] && atol(w) >= 1) ? (uint64_t)atol(w) : 0;
+    uint64_t best_cost = ~0ull, best = 128;
+    for (uint64_t waves = forced ? forced : 1; waves <= (forced ? forced : 16); waves++) {
+        uint64_t c = (total + slots * waves - 1) / (slots * waves);
+        if (c < 128) c = 128;
+        if (c > (1u << 30)) c = 1u << 30;
+        c = round_up32(c);
+        const uint64_t n = count_chunks(n_pos, n_items, c, mult);
+        const uint64_t cost = (n + slots - 1) / slots * (c + kWaveOverheadPositions);
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = c;
+        }
+    }
+    return (uint32_t)best;
 }
 
 static int plan_attention(const TGCudaAttnCall* c, AttnPlan* pl) {
@@ -388,12 +403,9 @@ static int plan_attention(const TGCudaAttnCall* c, AttnPlan* pl) {
     const uint32_t group = c->n_heads / c->n_kv_heads;
     pl->gt = tgkv_attention_g_tile(c->head_dim, group);
     pl->n_sub = group / pl->gt;
-    uint64_t total = 0;
-    for (uint32_t i = 0; i < c->n_items; i++) {
+    for (uint32_t i = 0; i < c->n_items; i++)
         if (c->n_pos[i] == 0) { set_err("attention: item %u attends no position", i); return 0; }
-        total += (uint64_t)c->n_pos[i] * c->n_kv_heads * pl->n_sub;
-    }
-    pl->chunk = pick_chunk(total);
+    pl->chunk = tgkv_pick_chunk(c->n_pos, c->n_items, c->n_kv_heads * pl->n_sub, (uint32_t)g_sm_count);
     pl->max_chunks = 0;
     for (uint32_t b0 = 0; b0 < c->n_items; b0 += TGKV_MAX_ITEMS) {
         const uint32_t n = (c->n_items - b0) < TGKV_MAX_ITEMS ? (c->n_items - b0) : TGKV_MAX_ITEMS;

@@ -813,15 +813,13 @@ extern "C" __attribute__((visibility("default"))) int tg_kv_attention_static(
     const uint32_t group = n_heads / n_kv_heads;
     const uint32_t gt = tgkv_attention_g_tile(head_dim, group);
     const uint32_t n_sub = group / gt;
-    uint64_t total = 0;
-    for (uint32_t t = 0; t < n_q; ++t) total += (uint64_t)(kv_len - n_q + t + 1) * n_kv_heads * n_sub;
-    const uint64_t chunk = tgkv_pick_chunk(total, (uint32_t)g_sms[dev]);
     TGKvAttnParams p;                     // ~8 KB on the stack: no heap, no device memory
     memset(&p, 0, offsetof(TGKvAttnParams, n_pos));
+    for (uint32_t t = 0; t < n_q; ++t) p.n_pos[t] = kv_len - n_q + t + 1;
+    const uint64_t chunk = tgkv_pick_chunk(p.n_pos, n_q, n_kv_heads * n_sub, (uint32_t)g_sms[dev]);
     uint64_t n_chunks = 0;
     for (uint32_t t = 0; t < n_q; ++t) {
-        const uint32_t np = kv_len - n_q + t + 1;
-        p.n_pos[t] = np;
+        const uint32_t np = p.n_pos[t];
         p.chunk_prefix[t] = (uint32_t)n_chunks;
         n_chunks += (uint64_t)((np + chunk - 1) / chunk) * n_kv_heads * n_sub;
     }

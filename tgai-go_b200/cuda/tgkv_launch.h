@@ -120,7 +120,7 @@ int tgkv_launch_attention(const TGKvAttnParams* p, int dtype, uint32_t head_dim,
 int tgkv_launch_append(const TGKvAppendParams* p, int dtype, void* stream);
 int tgkv_launch_rope_append(const TGKvRopeParams* p, void* stream);
 /* Chunk length the planner uses for a launch of total_positions (bridge). */
-uint32_t tgkv_pick_chunk(uint64_t total_positions, uint32_t sm_count);
+uint32_t tgkv_pick_chunk(const uint32_t* n_pos, uint32_t n_items, uint32_t mult, uint32_t sm_count);
 /* Heads per CTA the attention kernel supports for this head_dim (<= G). */
 uint32_t tgkv_attention_g_tile(uint32_t head_dim, uint32_t group);
 /* 1 if (dtype, head_dim) has an attention kernel. */
