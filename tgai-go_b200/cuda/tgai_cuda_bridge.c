@@ -359,9 +359,9 @@ static uint32_t round_up32(uint64_t x) { return (uint32_t)((x + TGKV_TILE - 1) /
  * boundaries); TGKV_WAVES fixes the wave target. */
 enum { kWaveOverheadPositions = 768 };
 
-static uint64_t count_chunks(const uint32_t* n_pos, uint32_t n_items, uint64_t chunk, uint32_t mult) {
+static uint64_t count_chunks(const uint32_t* n_pos, uint32_t n_items, uint32_t chunk, uint32_t mult) {
     uint64_t n = 0;
-    for (uint32_t i = 0; i < n_items; i++) n += (n_pos[i] + chunk - 1) / chunk;
+    for (uint32_t i = 0; i < n_items; i++) n += (n_pos[i] + chunk - 1) / chunk;   /* 32-bit */
     return n * mult;
 }
 
@@ -381,7 +381,7 @@ __attribute__((visibility("hidden"))) uint32_t tgkv_pick_chunk(const uint32_t* n
         if (c < 128) c = 128;
         if (c > (1u << 30)) c = 1u << 30;
         c = round_up32(c);
-        const uint64_t n = count_chunks(n_pos, n_items, c, mult);
+        const uint64_t n = count_chunks(n_pos, n_items, (uint32_t)c, mult);
         const uint64_t cost = (n + slots - 1) / slots * (c + kWaveOverheadPositions);
         if (cost < best_cost) {
             best_cost = cost;
@@ -423,23 +423,6 @@ static uint64_t part_o_bytes(const AttnPlan* pl, uint32_t head_dim) {
     return (pl->max_chunks * pl->gt * head_dim * 4 + 255) / 256 * 256;
 }
 
-uint64_t tg_cuda_kv_attn_scratch_bytes(const TGCudaAttnCall* c) {
-    AttnPlan pl;
-    if (!plan_attention(c, &pl)) return 0;
-    return part_o_bytes(&pl, c->head_dim) + pl.max_chunks * pl.gt * 2 * 4;
-}
-
-/* One arrival counter per segment. */
-uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c) {
-    AttnPlan pl;
-    if (!plan_attention(c, &pl)) return 0;
-    return (uint64_t)c->n_items * c->n_kv_heads * pl.n_sub;
-}
-
-uint32_t tg_cuda_kv_attn_last_launches(void) { return t_last_launches; }
-int tg_cuda_kv_attn_last_kernel(void) { return t_last_kernel; }
-uint32_t tg_cuda_kv_attn_last_split(void) { return t_last_split; }
-
 /* Blocks of query rows over one bf16 head_dim-128 cache go to the tensor-core
  * kernel (tgkv_prefill.cu) when there are at least 128 (row, head) pairs:
  * consecutive positions, group size 1/2/4/8, no fused append, q and out
@@ -448,6 +431,9 @@ uint32_t tg_cuda_kv_attn_last_split(void) { return t_last_split; }
 static int use_prefill(const TGCudaAttnCall* c) {
     const char* e = getenv("TGKV_PREFILL");
     if (e && e[0] == '0') return 0;
+    if (!c || !c->n_kv_heads || !c->n_heads || c->n_heads % c->n_kv_heads || !c->n_pos ||
+        !c->n_items || c->n_pos[0] == 0)
+        return 0;
     if (c->dtype != 1 || c->head_dim != 128 || c->table_dev || !c->cache.tmap_sw || c->k_new)
         return 0;
     const uint32_t g = c->n_heads / c->n_kv_heads;
@@ -479,13 +465,36 @@ static uint32_t prefill_split(const TGCudaAttnCall* c, uint32_t pos0) {
     return 1;
 }
 
+/* Calls that go to the tensor-core kernel need no split scratch: one token
+ * byte and one counter keep the caller's sizing logic uniform. */
+uint64_t tg_cuda_kv_attn_scratch_bytes(const TGCudaAttnCall* c) {
+    if (use_prefill(c)) return 256;
+    AttnPlan pl;
+    if (!plan_attention(c, &pl)) return 0;
+    return part_o_bytes(&pl, c->head_dim) + pl.max_chunks * pl.gt * 2 * 4;
+}
+
+/* One arrival counter per segment. */
+uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c) {
+    if (use_prefill(c)) return 1;
+    AttnPlan pl;
+    if (!plan_attention(c, &pl)) return 0;
+    return (uint64_t)c->n_items * c->n_kv_heads * pl.n_sub;
+}
+
+uint32_t tg_cuda_kv_attn_last_launches(void) { return t_last_launches; }
+int tg_cuda_kv_attn_last_kernel(void) { return t_last_kernel; }
+uint32_t tg_cuda_kv_attn_last_split(void) { return t_last_split; }
+
 int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
     t_last_launches = 0;
     t_last_kernel = 0;
     t_last_split = 0;
     if (!g_ready && !tg_cuda_kv_init()) return 0;
+    /* the tensor-core route needs none of the split planning */
+    const int prefill = use_prefill(c);
     AttnPlan pl;
-    if (!plan_attention(c, &pl)) return 0;
+    if (!prefill && !plan_attention(c, &pl)) return 0;
     if (c->n_items == 0) return 1;
     if (!c->q || !c->out || (!c->table_dev && (!c->cache.base || !c->cache.tmap))) {
         set_err("attention: NULL pointer");
@@ -499,7 +508,7 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         set_err("attention: k_new and v_new go together");
         return 0;
     }
-    if (use_prefill(c)) {
+    if (prefill) {
         TGKvPrefillParams pp;
         pp.tmap_sw = c->cache.tmap_sw;
         pp.q = c->q;

@@ -651,33 +651,40 @@ extern "C" int tgkv_launch_prefill(const TGKvPrefillParams* p, void* stream) {
 }
 
 // Clusters of n_split prefill CTAs that fit on the current device at once
-// (0 if the query fails); the planner sizes the split with it.
+// (0 if the query fails); the planner sizes the split with it.  The first
+// call on a device asks for every split size, so that no later call pays
+// for the occupancy query.
 extern "C" uint32_t tgkv_prefill_max_clusters(uint32_t n_split) {
     using namespace tgkv::prefill;
     if (n_split == 0 || n_split > kMaxSplit) return 0;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
     static uint32_t cache[64][kMaxSplit + 1];
-    if (cache[dev][n_split]) return cache[dev][n_split];
-    if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SMEM_BYTES) != cudaSuccess)
-        return 0;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(1, 1, n_split);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = SMEM_BYTES;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 1;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = n_split;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, prefill_kernel, &cfg) != cudaSuccess || n <= 0) {
-        cudaGetLastError();
-        return 0;
+    static bool filled[64];
+    if (!filled[dev]) {
+        if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 SMEM_BYTES) != cudaSuccess)
+            return 0;
+        for (uint32_t ns = 1; ns <= kMaxSplit; ++ns) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(1, 1, ns);
+            cfg.blockDim = dim3(kThreads, 1, 1);
+            cfg.dynamicSmemBytes = SMEM_BYTES;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = 1;
+            at[0].val.clusterDim.y = 1;
+            at[0].val.clusterDim.z = ns;
+            cfg.attrs = at;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, prefill_kernel, &cfg) != cudaSuccess || n < 0) {
+                cudaGetLastError();
+                n = 0;
+            }
+            cache[dev][ns] = (uint32_t)n;
+        }
+        filled[dev] = true;
     }
-    cache[dev][n_split] = (uint32_t)n;
-    return (uint32_t)n;
+    return cache[dev][n_split];
 }
