@@ -272,20 +272,39 @@ def run_ours(args):
     out = [torch.empty(n_seq, nh, hd, device="cuda") for _ in range(layers)]
     gathered = ([torch.empty(world, n_seq, nh, hd, device="cuda") for _ in range(layers)]
                 if heads_sharded else None)
+    # in-kernel gather over NVLink: every rank's attention stores its heads'
+    # outputs into every rank's gathered buffer (CUDA IPC peer memory)
+    fused = heads_sharded and args.gather == "fused"
+    gathers = []
+    if fused:
+        for l in range(layers):
+            g = lib.tg_kv_gather_create(world, rank, n_seq * nh * hd)
+            tgkv.check(g, lib, "tg_kv_gather_create")
+            h = (C.c_uint8 * 64)()
+            tgkv.check(lib.tg_kv_gather_export(g, h), lib, "tg_kv_gather_export")
+            allh = [None] * world
+            dist.all_gather_object(allh, bytes(h))
+            tgkv.check(lib.tg_kv_gather_import(g, b"".join(allh)), lib, "tg_kv_gather_import")
+            gathers.append(g)
     launches = [0]
 
     def step(events=None):
         for l in range(layers):
             if events is not None:
                 events[l][0].record(stream)
-            ok = lib.tg_kv_batch_decode(plans[l], q[l].data_ptr(), kn[l].data_ptr(),
-                                        vn[l].data_ptr(), out[l].data_ptr(), sh)
+            if fused:
+                ok = lib.tg_kv_batch_decode_gather(plans[l], q[l].data_ptr(), kn[l].data_ptr(),
+                                                   vn[l].data_ptr(), out[l].data_ptr(),
+                                                   gathers[l], sh)
+            else:
+                ok = lib.tg_kv_batch_decode(plans[l], q[l].data_ptr(), kn[l].data_ptr(),
+                                            vn[l].data_ptr(), out[l].data_ptr(), sh)
             if not ok:
                 raise RuntimeError(lib.tg_kv_last_error().decode())
             launches[0] += lib.tg_kv_batch_last_launches(plans[l])
             if events is not None:
                 events[l][1].record(stream)
-            if heads_sharded:
+            if heads_sharded and not fused:
                 dist.all_gather_into_tensor(gathered[l], out[l])
 
     def barrier():
@@ -329,15 +348,22 @@ def run_ours(args):
               for l in range(layers)]
         kh = [torch.randn(n_seq, kvd).pin_memory() for _ in range(layers)]
         vh = [torch.randn(n_seq, kvd).pin_memory() for _ in range(layers)]
-        oh = [torch.empty(n_seq, nh, hd).pin_memory() for _ in range(layers)]
+        oh = [torch.empty((world if fused else 1) * n_seq, nh, hd).pin_memory()
+              for _ in range(layers)]
 
         def step_host():
             for l in range(layers):
-                ok = lib.tg_kv_batch_decode_host(plans[l], qh[l].data_ptr(), kh[l].data_ptr(),
-                                                 vh[l].data_ptr(), oh[l].data_ptr(), sh)
+                if fused:       # out_host receives every rank's outputs
+                    ok = lib.tg_kv_batch_decode_gather_host(
+                        plans[l], qh[l].data_ptr(), kh[l].data_ptr(), vh[l].data_ptr(),
+                        oh[l].data_ptr(), gathers[l], sh)
+                else:
+                    ok = lib.tg_kv_batch_decode_host(plans[l], qh[l].data_ptr(),
+                                                     kh[l].data_ptr(), vh[l].data_ptr(),
+                                                     oh[l].data_ptr(), sh)
                 if not ok:
                     raise RuntimeError(lib.tg_kv_last_error().decode())
-                if heads_sharded:
+                if heads_sharded and not fused:
                     dist.all_gather_into_tensor(gathered[l], out[l])
 
         for _ in range(e2e_warm):
@@ -358,6 +384,10 @@ def run_ours(args):
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e_ms}
 
     err = lib.tg_cuda_kv_device_error()
+    if gathers:
+        barrier()                 # no rank still writes into a peer's buffer
+        for g in gathers:
+            lib.tg_kv_gather_destroy(g)
     for b in plans:
         lib.tg_kv_batch_destroy(b)
     for row in caches:
@@ -396,7 +426,8 @@ def run_ours(args):
                        "sequences_per_gpu": n_seq,
                        "kv_heads_per_gpu": nkv, "context_mean": float(lens0.mean()),
                        "l2": "inputs larger than L2 (K/V read per step >> 126 MB)",
-                       "parallelism": (f"kv-head groups x{world} + NCCL all-gather"
+                       "parallelism": (f"kv-head groups x{world} + "
+                                       + ("in-kernel NVLink gather" if fused else "NCCL all-gather")
                                        if heads_sharded else
                                        f"sequences x{world} ({'LPT split' if args.shard_seqs else 'own set per GPU'}), no collective"),
                        "fill_s": round(t_fill, 1)},
@@ -511,6 +542,9 @@ def main():
     ap.add_argument("--shard-seqs", action="store_true",
                     help="cfg4: split the workload's sequences over ranks (LPT, strong scaling) "
                          "instead of a full set per GPU (weak scaling)")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="KV heads split over ranks (cfg5/cfg2 at N>1): outputs gathered by the "
+                         "attention kernel over NVLink (fused) or by an NCCL all-gather")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-baseline-s", type=float, default=12.0)

@@ -49,6 +49,18 @@ int   tg_cuda_kv_sync(void* stream);
  * expired (0 = none).  Blocks on the whole device. */
 int   tg_cuda_kv_device_error(void);
 
+/* CUDA IPC between the processes of one node (one per GPU): the 64-byte
+ * handle of a tg_cuda_kv_malloc'ed buffer, a peer's buffer opened from its
+ * handle (peer access enabled; NULL on failure), and closing it again. */
+int   tg_cuda_kv_ipc_handle(const void* dev, void* handle64);
+void* tg_cuda_kv_ipc_open(const void* handle64);
+void  tg_cuda_kv_ipc_close(void* dev);
+
+/* Queue a wait on stream until the 32-bit counter at flag (device memory)
+ * reaches target (wrap-safe compare; acquire at system scope).  Bounded: after
+ * ~2 s the device error word is set and the stream moves on. */
+int   tg_cuda_kv_gather_wait(const uint32_t* flag, uint32_t target, void* stream);
+
 /* Testing hook: make the next `n` tg_cuda_kv_malloc calls fail (0 = off).
  * Also set at start-up from TGKV_FAIL_ALLOC. */
 void  tg_cuda_kv_inject_alloc_failures(int n);
@@ -103,6 +115,15 @@ typedef struct {
     float           scale;          /* softmax scale (1/sqrt(head_dim)) */
     void*           scratch;        /* device, >= tg_cuda_kv_attn_scratch_bytes() */
     uint32_t*       counters;       /* device, zeroed, >= tg_cuda_kv_attn_counters() */
+    /* Optional output gather over NVLink (gather_world 0 = off; at most 8):
+     * every output element is also stored at gather_out[r][gather_base + its
+     * index in out] on each rank r, and each finished (item, KV head, head
+     * subset) adds 1 to every rank's *gather_flag[r].  Peer pointers come from
+     * tg_cuda_kv_ipc_open; index gather_world-1 may be this rank's own. */
+    float*          gather_out[8];
+    uint32_t*       gather_flag[8];
+    uint64_t        gather_base;
+    uint32_t        gather_world;
 } TGCudaAttnCall;
 
 int      tg_cuda_kv_attn_supported(int dtype, uint32_t head_dim);

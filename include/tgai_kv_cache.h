@@ -172,6 +172,46 @@ int tg_kv_batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_ho
 /* Number of kernel launches the last tg_kv_batch_decode made (for reports). */
 uint32_t tg_kv_batch_last_launches(const TGKvBatch* b);
 
+/* ---- Output gather over NVLink (KV heads split over the GPUs of a node) --
+ *
+ * With the KV heads of one long context split into groups, one per GPU (one
+ * process each), every rank attends its own heads and all ranks need every
+ * head's output.  The attention kernel itself stores each finished output
+ * element into every rank's gathered buffer (peer memory over NVLink) and
+ * counts arrivals there, replacing a separate all-gather.  Without a GPU
+ * fault nobody waits forever: the wait is bounded (~2 s) and reports through
+ * tg_cuda_kv_device_error. */
+
+typedef struct TGKvGather TGKvGather;
+
+/* This rank's side of a gather among `world` ranks (<= 8): one device
+ * allocation holding the gathered outputs [world][elems] fp32 (rank r's at
+ * [r*elems, (r+1)*elems)) and an arrival counter.  NULL on failure. */
+TGKvGather* tg_kv_gather_create(uint32_t world, uint32_t rank, uint64_t elems);
+/* Closes the peers' buffers and frees this rank's.  Call on every rank after
+ * all ranks have finished their last gathered step (a barrier). */
+void        tg_kv_gather_destroy(TGKvGather* g);
+/* This rank's 64-byte IPC handle. */
+int tg_kv_gather_export(const TGKvGather* g, void* handle64);
+/* Open the other ranks' allocations: `world` handles of 64 bytes in rank
+ * order (this rank's own entry is not opened).  Every rank exports before any
+ * rank imports. */
+int tg_kv_gather_import(TGKvGather* g, const void* handles);
+/* Device address of this rank's gathered outputs [world][elems]. */
+float* tg_kv_gather_buffer(const TGKvGather* g);
+
+/* tg_kv_batch_decode whose outputs also land in every rank's gathered buffer
+ * (this rank's slice: elems = n * n_heads * head_dim), followed by a wait on
+ * `stream` until every rank's outputs of this step have arrived here.  All
+ * ranks make the same sequence of calls with plans of the same shape. */
+int tg_kv_batch_decode_gather(TGKvBatch* b, const float* q, const float* k_new,
+                              const float* v_new, float* out, TGKvGather* g, void* stream);
+/* The same from host buffers; out_host receives the whole gathered
+ * [world][n][n_heads][head_dim]. */
+int tg_kv_batch_decode_gather_host(TGKvBatch* b, const float* q_host, const float* k_host,
+                                   const float* v_host, float* out_host, TGKvGather* g,
+                                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -245,6 +245,38 @@ void tg_cuda_kv_free(void* p) {
     if (p) cudaFree(p);
 }
 
+static int launch_rc(int rc, const char* what);
+
+int tg_cuda_kv_ipc_handle(const void* dev, void* handle64) {
+    if (!g_ready && !tg_cuda_kv_init()) return 0;
+    if (!dev || !handle64) { set_err("ipc: null argument"); return 0; }
+    cudaIpcMemHandle_t h;
+    if (!cuda_ok(cudaIpcGetMemHandle(&h, (void*)dev), "cudaIpcGetMemHandle")) return 0;
+    memcpy(handle64, &h, sizeof(h) < 64 ? sizeof(h) : 64);
+    return 1;
+}
+
+void* tg_cuda_kv_ipc_open(const void* handle64) {
+    if (!g_ready && !tg_cuda_kv_init()) return NULL;
+    if (!handle64) { set_err("ipc: null handle"); return NULL; }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    void* p = NULL;
+    if (!cuda_ok(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle"))
+        return NULL;
+    return p;
+}
+
+void tg_cuda_kv_ipc_close(void* dev) {
+    if (dev) cudaIpcCloseMemHandle(dev);
+}
+
+int tg_cuda_kv_gather_wait(const uint32_t* flag, uint32_t target, void* stream) {
+    if (!g_ready && !tg_cuda_kv_init()) return 0;
+    if (!flag) { set_err("gather wait: null flag"); return 0; }
+    return launch_rc(tgkv_launch_gather_wait(flag, target, g_err_word, stream), "gather wait");
+}
+
 int tg_cuda_kv_h2d(void* dst, const void* src, size_t bytes, void* stream) {
     if (!bytes) return 1;
     if (!stream) return cuda_ok(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice), "h2d");
@@ -508,6 +540,19 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         set_err("attention: k_new and v_new go together");
         return 0;
     }
+    if (c->gather_world > TGKV_MAX_RANKS) {
+        set_err("attention: gather over %u ranks, at most %d", c->gather_world, TGKV_MAX_RANKS);
+        return 0;
+    }
+    for (uint32_t r = 0; r < c->gather_world; r++)
+        if (!c->gather_out[r] || !c->gather_flag[r]) {
+            set_err("attention: gather rank %u has no buffer or flag", r);
+            return 0;
+        }
+    if (c->gather_world && prefill) {
+        set_err("attention: the output gather is for decode calls (one query row per item)");
+        return 0;
+    }
     if (prefill) {
         TGKvPrefillParams pp;
         pp.tmap_sw = c->cache.tmap_sw;
@@ -558,6 +603,12 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         p.chunk = pl.chunk;
         p.qscale = c->scale * 1.4426950408889634f;
         p.item_base = b0;
+        p.gather_world = c->gather_world;
+        p.gather_base = c->gather_base;
+        for (uint32_t r = 0; r < c->gather_world; r++) {
+            p.gather_out[r] = c->gather_out[r];
+            p.gather_flag[r] = c->gather_flag[r];
+        }
         uint32_t acc = 0;
         for (uint32_t i = 0; i < n; i++) {
             const uint32_t np = c->n_pos[b0 + i];

@@ -44,6 +44,7 @@ constexpr int kFacBlock = 256;       // partials merged per block in the combine
 // Error codes written to p.err.
 constexpr int kErrFullTimeout = 1;
 constexpr int kErrEmptyTimeout = 2;
+constexpr int kErrGatherTimeout = 4;
 
 }  // namespace tgkv
 
@@ -176,6 +177,20 @@ __device__ __forceinline__ Chunk decode_chunk(const TGKvAttnParams& p, uint32_t 
     return c;
 }
 
+// Output gather over NVLink: one finished element to every rank's buffer.
+__device__ __forceinline__ void gather_store(const TGKvAttnParams& p, uint64_t idx, float v) {
+    for (uint32_t r = 0; r < p.gather_world; ++r) p.gather_out[r][p.gather_base + idx] = v;
+}
+
+// After the CTA's 128 consumer threads stored a segment's outputs to every
+// rank: system fence per thread, then one arrival per rank.
+__device__ __noinline__ void gather_signal(const TGKvAttnParams& p, int tid) {
+    __threadfence_system();
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (tid == 0)
+        for (uint32_t r = 0; r < p.gather_world; ++r) atomicAdd_system(p.gather_flag[r], 1u);
+}
+
 // Merge the nparts partials of one segment (slots first .. first+nparts-1;
 // this CTA finished last): per-head maxima, then blocks of per-partial
 // factors in shared memory and coalesced weighted sums.  Kept out of line so
@@ -264,9 +279,12 @@ __device__ __noinline__ void combine_segment(const TGKvAttnParams& p, uint32_t f
             float L = 0.f;
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) L += sm_red[(w * GT + h) * 2 + 1];
-            p.out[row + (uint64_t)(head0 + h) * HD + d] = (L > 0.f) ? acc[k] / L : 0.f;
+            const float o = (L > 0.f) ? acc[k] / L : 0.f;
+            p.out[row + (uint64_t)(head0 + h) * HD + d] = o;
+            if (p.gather_world) gather_store(p, row + (uint64_t)(head0 + h) * HD + d, o);
         }
     }
+    if (p.gather_world) gather_signal(p, tid);
 }
 
 template <int DT, int HD, int GT>
@@ -506,7 +524,9 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
             L += sm_cml[(w * GT + h) * 2 + 1] * f;
         }
         if (whole) {
-            p.out[row + (uint64_t)(head0 + h) * HD + d] = (L > 0.f) ? O / L : 0.f;
+            const float o = (L > 0.f) ? O / L : 0.f;
+            p.out[row + (uint64_t)(head0 + h) * HD + d] = o;
+            if (p.gather_world) gather_store(p, row + (uint64_t)(head0 + h) * HD + d, o);
         } else {
             p.part_o[((uint64_t)u * GT + h) * HD + d] = O;
             if (d == 0) {
@@ -515,7 +535,10 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
             }
         }
     }
-    if (whole) return;
+    if (whole) {
+        if (p.gather_world) gather_signal(p, tid);
+        return;
+    }
 
     // ---- the last chunk of the segment to finish merges them all
     __threadfence();
@@ -693,6 +716,29 @@ extern "C" int tgkv_launch_append(const TGKvAppendParams* p, int dtype, void* st
         tgkv::append_kernel<0><<<grid, 256, 0, (cudaStream_t)stream>>>(*p);
     else
         tgkv::append_kernel<1><<<grid, 256, 0, (cudaStream_t)stream>>>(*p);
+    return (int)cudaGetLastError();
+}
+
+namespace tgkv {
+__global__ void gather_wait_kernel(const uint32_t* flag, uint32_t target, int32_t* err) {
+    if (threadIdx.x != 0) return;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if ((int32_t)(v - target) >= 0) break;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            atomicExch(err, kErrGatherTimeout);
+            break;
+        }
+        __nanosleep(64);
+    }
+}
+}  // namespace tgkv
+
+extern "C" int tgkv_launch_gather_wait(const uint32_t* flag, uint32_t target, int32_t* err,
+                                       void* stream) {
+    tgkv::gather_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flag, target, err);
     return (int)cudaGetLastError();
 }
 

@@ -16,6 +16,7 @@ extern "C" {
 #endif
 
 #define TGKV_MAX_ITEMS 1024      /* items (query rows / caches) per launch */
+#define TGKV_MAX_RANKS 8         /* GPUs of one node in an output gather */
 #define TGKV_TILE      32        /* positions per pipeline stage */
 
 /* One cache buffer [2][max_seq][kv_dim] in device memory, with the device
@@ -60,6 +61,15 @@ typedef struct {
     uint32_t chunk;              /* positions per chunk, multiple of TGKV_TILE */
     float    qscale;             /* softmax scale * log2(e) */
     uint32_t item_base;          /* first item of this launch (q/out/counter offset) */
+    /* Output gather over NVLink (KV heads split over ranks).  When
+     * gather_world > 0 every finished output element is also stored at
+     * gather_out[r][gather_base + its index in out] for each rank r (peer
+     * memory), and the CTA that finished a segment then adds 1 to each rank's
+     * *gather_flag[r] (system scope, after a system fence). */
+    float*    gather_out[TGKV_MAX_RANKS];
+    uint32_t* gather_flag[TGKV_MAX_RANKS];
+    uint64_t  gather_base;
+    uint32_t  gather_world;
     uint32_t n_pos[TGKV_MAX_ITEMS];
     uint32_t chunk_prefix[TGKV_MAX_ITEMS + 1];
 } TGKvAttnParams;
@@ -118,6 +128,9 @@ uint32_t tgkv_prefill_max_clusters(uint32_t n_split);
 int tgkv_launch_attention(const TGKvAttnParams* p, int dtype, uint32_t head_dim,
                           uint32_t g_tile, uint32_t grid, void* stream);
 int tgkv_launch_append(const TGKvAppendParams* p, int dtype, void* stream);
+/* One thread waits (acquire, system scope; bounded, error word on expiry)
+ * until *flag has reached target (wrap-safe). */
+int tgkv_launch_gather_wait(const uint32_t* flag, uint32_t target, int32_t* err, void* stream);
 int tgkv_launch_rope_append(const TGKvRopeParams* p, void* stream);
 /* Chunk length the planner uses for a launch of total_positions (bridge). */
 uint32_t tgkv_pick_chunk(const uint32_t* n_pos, uint32_t n_items, uint32_t mult, uint32_t sm_count);

@@ -408,9 +408,84 @@ void tg_kv_batch_destroy(TGKvBatch* b) {
 
 uint32_t tg_kv_batch_last_launches(const TGKvBatch* b) { return b ? b->last_launches : 0; }
 
-int tg_kv_batch_decode(TGKvBatch* b, const float* q, const float* k_new, const float* v_new,
-                       float* out, void* stream) {
+/* ---- output gather over NVLink ------------------------------------------ */
+
+#define TGKV_GATHER_MAX 8
+
+struct TGKvGather {
+    uint32_t world, rank;
+    uint64_t elems;                   /* outputs of one rank */
+    uint64_t flag_off;                /* byte offset of the arrival counter */
+    unsigned char* mem;               /* this rank's allocation */
+    unsigned char* peer[TGKV_GATHER_MAX];   /* every rank's allocation (own at [rank]) */
+    int imported;
+    uint32_t target;                  /* arrivals expected after the last step */
+};
+
+TGKvGather* tg_kv_gather_create(uint32_t world, uint32_t rank, uint64_t elems) {
+    if (world == 0 || world > TGKV_GATHER_MAX || rank >= world || elems == 0) {
+        set_err("gather: bad shape (world %u, rank %u, %llu elements)", world, rank,
+                (unsigned long long)elems);
+        return NULL;
+    }
+    TGKvGather* g = (TGKvGather*)calloc(1, sizeof(TGKvGather));
+    if (!g) { set_err("out of host memory"); return NULL; }
+    g->world = world;
+    g->rank = rank;
+    g->elems = elems;
+    g->flag_off = ((uint64_t)world * elems * 4 + 255) / 256 * 256;
+    g->mem = (unsigned char*)tg_cuda_kv_malloc((size_t)(g->flag_off + 256));   /* zeroed */
+    if (!g->mem) {
+        set_err("gather: %s", tg_cuda_kv_last_error());
+        free(g);
+        return NULL;
+    }
+    g->peer[rank] = g->mem;
+    g->imported = world == 1;
+    return g;
+}
+
+void tg_kv_gather_destroy(TGKvGather* g) {
+    if (!g) return;
+    for (uint32_t r = 0; r < g->world; r++)
+        if (r != g->rank && g->peer[r]) tg_cuda_kv_ipc_close(g->peer[r]);
+    tg_cuda_kv_free(g->mem);
+    free(g);
+}
+
+int tg_kv_gather_export(const TGKvGather* g, void* handle64) {
+    if (!g || !handle64) { set_err("null argument"); return 0; }
+    if (!tg_cuda_kv_ipc_handle(g->mem, handle64)) { set_err("%s", tg_cuda_kv_last_error()); return 0; }
+    return 1;
+}
+
+int tg_kv_gather_import(TGKvGather* g, const void* handles) {
+    if (!g || !handles) { set_err("null argument"); return 0; }
+    for (uint32_t r = 0; r < g->world; r++) {
+        if (r == g->rank || g->peer[r]) continue;
+        g->peer[r] = (unsigned char*)tg_cuda_kv_ipc_open((const unsigned char*)handles + 64u * r);
+        if (!g->peer[r]) {
+            set_err("gather: rank %u: %s", r, tg_cuda_kv_last_error());
+            return 0;
+        }
+    }
+    g->imported = 1;
+    return 1;
+}
+
+float* tg_kv_gather_buffer(const TGKvGather* g) { return g ? (float*)g->mem : NULL; }
+
+/* One decode step of the plan; with g, the outputs also go to every rank's
+ * gathered buffer and the stream then waits for all ranks' outputs. */
+static int batch_decode(TGKvBatch* b, const float* q, const float* k_new, const float* v_new,
+                        float* out, TGKvGather* g, void* stream) {
     if (!b || !q || !k_new || !v_new || !out) { set_err("null argument"); return 0; }
+    if (g && !g->imported) { set_err("gather: peers not imported"); return 0; }
+    if (g && (uint64_t)b->n * b->n_heads * b->head_dim != g->elems) {
+        set_err("gather: plan outputs %llu elements, gather slices hold %llu",
+                (unsigned long long)b->n * b->n_heads * b->head_dim, (unsigned long long)g->elems);
+        return 0;
+    }
     b->last_launches = 0;
     for (uint32_t i = 0; i < b->n; i++) {
         const TGKvCache* c = b->caches[i];
@@ -436,6 +511,14 @@ int tg_kv_batch_decode(TGKvBatch* b, const float* q, const float* k_new, const f
     call.counters = b->counters;
     call.k_new = k_new;               /* the append runs inside the attention launch */
     call.v_new = v_new;
+    if (g) {
+        call.gather_world = g->world;
+        call.gather_base = (uint64_t)g->rank * g->elems;
+        for (uint32_t r = 0; r < g->world; r++) {
+            call.gather_out[r] = (float*)g->peer[r];
+            call.gather_flag[r] = (uint32_t*)(g->peer[r] + g->flag_off);
+        }
+    }
     if (tg_be_current() != &tg_backend_cuda) {
         set_err("KV-cache path needs the cuda backend; no fallback");
         return 0;
@@ -446,11 +529,34 @@ int tg_kv_batch_decode(TGKvBatch* b, const float* q, const float* k_new, const f
     }
     b->last_launches += tg_cuda_kv_attn_last_launches();
     for (uint32_t i = 0; i < b->n; i++) b->caches[i]->len++;
+    if (g) {
+        /* every rank finishes the same number of segments and signals each
+         * rank once per segment */
+        g->target += g->world * (uint32_t)tg_cuda_kv_attn_counters(&call);
+        if (!tg_cuda_kv_gather_wait((const uint32_t*)(g->mem + g->flag_off), g->target, stream)) {
+            set_err("%s", tg_cuda_kv_last_error());
+            return 0;
+        }
+        b->last_launches++;
+    }
     return 1;
 }
 
-int tg_kv_batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_host,
-                            const float* v_host, float* out_host, void* stream) {
+int tg_kv_batch_decode(TGKvBatch* b, const float* q, const float* k_new, const float* v_new,
+                       float* out, void* stream) {
+    return batch_decode(b, q, k_new, v_new, out, NULL, stream);
+}
+
+int tg_kv_batch_decode_gather(TGKvBatch* b, const float* q, const float* k_new,
+                              const float* v_new, float* out, TGKvGather* g, void* stream) {
+    if (!g) { set_err("null gather"); return 0; }
+    return batch_decode(b, q, k_new, v_new, out, g, stream);
+}
+
+/* The step from host buffers: stage q/k/v in, run it, copy the outputs (or,
+ * with g, the whole gathered buffer) back, all on `stream`. */
+static int batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_host,
+                             const float* v_host, float* out_host, TGKvGather* g, void* stream) {
     if (!b || !q_host || !k_host || !v_host || !out_host) { set_err("null argument"); return 0; }
     const uint64_t qb = (uint64_t)b->n * b->n_heads * b->head_dim * 4;
     const uint64_t kb = (uint64_t)b->n * b->kv_dim * 4;
@@ -477,7 +583,21 @@ int tg_kv_batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_ho
              tg_cuda_kv_h2d(v, v_host, kb, NULL);
     }
     if (!ok) { set_err("%s", tg_cuda_kv_last_error()); return 0; }
-    if (!tg_kv_batch_decode(b, q, k, v, o, st)) return 0;
-    if (!tg_cuda_kv_d2h(out_host, o, qb, st)) { set_err("%s", tg_cuda_kv_last_error()); return 0; }
+    if (!batch_decode(b, q, k, v, o, g, st)) return 0;
+    const void* src = g ? (const void*)g->mem : (const void*)o;
+    const uint64_t ob = g ? (uint64_t)g->world * g->elems * 4 : qb;
+    if (!tg_cuda_kv_d2h(out_host, src, ob, st)) { set_err("%s", tg_cuda_kv_last_error()); return 0; }
     return 1;
+}
+
+int tg_kv_batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_host,
+                            const float* v_host, float* out_host, void* stream) {
+    return batch_decode_host(b, q_host, k_host, v_host, out_host, NULL, stream);
+}
+
+int tg_kv_batch_decode_gather_host(TGKvBatch* b, const float* q_host, const float* k_host,
+                                   const float* v_host, float* out_host, TGKvGather* g,
+                                   void* stream) {
+    if (!g) { set_err("null gather"); return 0; }
+    return batch_decode_host(b, q_host, k_host, v_host, out_host, g, stream);
 }

@@ -86,6 +86,13 @@ PROTOS = {
     "tg_kv_batch_decode": (i32, [vp, vp, vp, vp, vp, vp]),
     "tg_kv_batch_decode_host": (i32, [vp, vp, vp, vp, vp, vp]),
     "tg_kv_batch_last_launches": (u32, [vp]),
+    "tg_kv_gather_create": (vp, [u32, u32, u64]),
+    "tg_kv_gather_destroy": (None, [vp]),
+    "tg_kv_gather_export": (i32, [vp, vp]),
+    "tg_kv_gather_import": (i32, [vp, vp]),
+    "tg_kv_gather_buffer": (vp, [vp]),
+    "tg_kv_batch_decode_gather": (i32, [vp, vp, vp, vp, vp, vp, vp]),
+    "tg_kv_batch_decode_gather_host": (i32, [vp, vp, vp, vp, vp, vp, vp]),
     # tgai_backend.h
     "tg_be_probe": (i32, []),
     "tg_be_select": (i32, [cp]),
@@ -137,6 +144,10 @@ PROTOS = {
     "tg_cuda_kv_attn_last_launches": (u32, []),
     "tg_cuda_kv_attn_last_kernel": (i32, []),
     "tg_cuda_kv_attn_last_split": (u32, []),
+    "tg_cuda_kv_ipc_handle": (i32, [vp, vp]),
+    "tg_cuda_kv_ipc_open": (vp, [vp]),
+    "tg_cuda_kv_ipc_close": (None, [vp]),
+    "tg_cuda_kv_gather_wait": (i32, [vp, u32, vp]),
     "tg_cuda_kv_attention": (i32, [vp, vp]),
     "tg_cuda_kv_rope_append": (i32, [i32, vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32,
                                      vp]),
