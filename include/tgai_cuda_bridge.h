@@ -49,6 +49,22 @@ int   tg_cuda_kv_sync(void* stream);
  * expired (0 = none).  Blocks on the whole device. */
 int   tg_cuda_kv_device_error(void);
 
+/* Streams and events, for overlapping host<->device copies with kernels.
+ * Streams are non-blocking (no implicit order with the legacy default stream,
+ * NULL); order them with events. */
+void* tg_cuda_kv_stream_create(void);
+void  tg_cuda_kv_stream_destroy(void* stream);
+void* tg_cuda_kv_event_create(void);
+void  tg_cuda_kv_event_destroy(void* event);
+int   tg_cuda_kv_event_record(void* event, void* stream);
+/* Later work on `stream` waits for `event`'s last record. */
+int   tg_cuda_kv_stream_wait(void* stream, void* event);
+
+/* The device address of page-locked host memory (the host address itself
+ * under unified addressing), or NULL for pageable memory: kernels can write
+ * results straight into it over PCIe. */
+void* tg_cuda_kv_host_device_ptr(const void* host);
+
 /* CUDA IPC between the processes of one node (one per GPU): the 64-byte
  * handle of a tg_cuda_kv_malloc'ed buffer, a peer's buffer opened from its
  * handle (peer access enabled; NULL on failure), and closing it again. */

@@ -245,6 +245,49 @@ void tg_cuda_kv_free(void* p) {
     if (p) cudaFree(p);
 }
 
+void* tg_cuda_kv_stream_create(void) {
+    if (!g_ready && !tg_cuda_kv_init()) return NULL;
+    cudaStream_t s = NULL;
+    if (!cuda_ok(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate")) return NULL;
+    return (void*)s;
+}
+
+void tg_cuda_kv_stream_destroy(void* stream) {
+    if (stream) cudaStreamDestroy((cudaStream_t)stream);
+}
+
+void* tg_cuda_kv_event_create(void) {
+    if (!g_ready && !tg_cuda_kv_init()) return NULL;
+    cudaEvent_t e = NULL;
+    if (!cuda_ok(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate")) return NULL;
+    return (void*)e;
+}
+
+void tg_cuda_kv_event_destroy(void* event) {
+    if (event) cudaEventDestroy((cudaEvent_t)event);
+}
+
+int tg_cuda_kv_event_record(void* event, void* stream) {
+    if (!event) { set_err("event record: null event"); return 0; }
+    return cuda_ok(cudaEventRecord((cudaEvent_t)event, (cudaStream_t)stream), "cudaEventRecord");
+}
+
+int tg_cuda_kv_stream_wait(void* stream, void* event) {
+    if (!event) { set_err("stream wait: null event"); return 0; }
+    return cuda_ok(cudaStreamWaitEvent((cudaStream_t)stream, (cudaEvent_t)event, 0),
+                   "cudaStreamWaitEvent");
+}
+
+void* tg_cuda_kv_host_device_ptr(const void* host) {
+    if (!host || (!g_ready && !tg_cuda_kv_init())) return NULL;
+    struct cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, host) != cudaSuccess) {
+        cudaGetLastError();
+        return NULL;
+    }
+    return a.type == cudaMemoryTypeHost ? a.devicePointer : NULL;
+}
+
 static int launch_rc(int rc, const char* what);
 
 int tg_cuda_kv_ipc_handle(const void* dev, void* handle64) {

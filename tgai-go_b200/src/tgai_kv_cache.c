@@ -331,8 +331,17 @@ struct TGKvBatch {
     uint64_t scratch_bytes;
     uint32_t* counters;
     uint64_t counter_slots;
-    float* io;                        /* device staging for the host-buffer variant */
-    uint64_t io_bytes;
+    /* host-buffer variant: two device staging slots, used in turn, so that a
+     * call's uploads (on the plan's copy stream) overlap the previous call's
+     * kernel; in_ready orders a slot's kernel after its uploads, slot_free a
+     * slot's next uploads after its last reader */
+    float* io[2];
+    uint64_t io_bytes[2];
+    void* copy_stream;
+    void* in_ready[2];
+    void* slot_free[2];
+    int slot_used[2];
+    uint32_t slot;
     uint32_t last_launches;
 };
 
@@ -399,8 +408,14 @@ void tg_kv_batch_destroy(TGKvBatch* b) {
         if (b->table_dev) b->be->free(b->table_dev);
         if (b->scratch) b->be->free(b->scratch);
         if (b->counters) b->be->free(b->counters);
-        if (b->io) b->be->free(b->io);
+        for (int i = 0; i < 2; i++)
+            if (b->io[i]) b->be->free(b->io[i]);
     }
+    for (int i = 0; i < 2; i++) {
+        tg_cuda_kv_event_destroy(b->in_ready[i]);
+        tg_cuda_kv_event_destroy(b->slot_free[i]);
+    }
+    tg_cuda_kv_stream_destroy(b->copy_stream);
     free(b->caches);
     free(b->npos);
     free(b);
@@ -553,40 +568,59 @@ int tg_kv_batch_decode_gather(TGKvBatch* b, const float* q, const float* k_new,
     return batch_decode(b, q, k_new, v_new, out, g, stream);
 }
 
-/* The step from host buffers: stage q/k/v in, run it, copy the outputs (or,
- * with g, the whole gathered buffer) back, all on `stream`. */
+/* The step from host buffers: upload q/k/v into one of the plan's two
+ * staging slots on the plan's copy stream (overlapping the previous call's
+ * kernel when the host buffers are pinned), run the step on `stream` once
+ * they are in, and bring the outputs back: a page-locked out_host receives
+ * them straight from the kernel (no copy; the stores overlap the streaming),
+ * else they are copied back on `stream` -- with g, the whole gathered buffer
+ * is copied.  Synchronising `stream` covers the results either way. */
 static int batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_host,
                              const float* v_host, float* out_host, TGKvGather* g, void* stream) {
     if (!b || !q_host || !k_host || !v_host || !out_host) { set_err("null argument"); return 0; }
     const uint64_t qb = (uint64_t)b->n * b->n_heads * b->head_dim * 4;
     const uint64_t kb = (uint64_t)b->n * b->kv_dim * 4;
     const uint64_t need = 2 * qb + 2 * kb + 64;
-    if (need > b->io_bytes) {
-        if (b->io) b->be->free(b->io);
-        b->io = (float*)b->be->alloc((size_t)need);
-        b->io_bytes = b->io ? need : 0;
-        if (!b->io) { set_err("batch: staging allocation failed"); return 0; }
+    if (!b->copy_stream) {
+        b->copy_stream = tg_cuda_kv_stream_create();
+        for (int i = 0; i < 2; i++) {
+            b->in_ready[i] = tg_cuda_kv_event_create();
+            b->slot_free[i] = tg_cuda_kv_event_create();
+        }
+        if (!b->copy_stream || !b->in_ready[0] || !b->in_ready[1] || !b->slot_free[0] ||
+            !b->slot_free[1]) {
+            set_err("batch: %s", tg_cuda_kv_last_error());
+            return 0;
+        }
     }
-    float* q = b->io;
+    const uint32_t s = b->slot;
+    if (need > b->io_bytes[s]) {
+        if (b->io[s]) b->be->free(b->io[s]);          /* cudaFree waits for its readers */
+        b->io[s] = (float*)b->be->alloc((size_t)need);
+        b->io_bytes[s] = b->io[s] ? need : 0;
+        if (!b->io[s]) { set_err("batch: staging allocation failed"); return 0; }
+    }
+    float* q = b->io[s];
     float* o = (float*)((char*)q + qb);
     float* k = (float*)((char*)o + qb);
     float* v = (float*)((char*)k + kb);
-    /* the queued copies need a real stream so they stay ordered with the
-     * kernels; NULL means the legacy default stream for both */
-    void* st = stream;
-    int ok;
-    if (st) {
-        ok = tg_cuda_kv_h2d(q, q_host, qb, st) && tg_cuda_kv_h2d(k, k_host, kb, st) &&
-             tg_cuda_kv_h2d(v, v_host, kb, st);
-    } else {
-        ok = tg_cuda_kv_h2d(q, q_host, qb, NULL) && tg_cuda_kv_h2d(k, k_host, kb, NULL) &&
-             tg_cuda_kv_h2d(v, v_host, kb, NULL);
-    }
+    void* cp = b->copy_stream;
+    int ok = (!b->slot_used[s] || tg_cuda_kv_stream_wait(cp, b->slot_free[s])) &&
+             tg_cuda_kv_h2d(q, q_host, qb, cp) && tg_cuda_kv_h2d(k, k_host, kb, cp) &&
+             tg_cuda_kv_h2d(v, v_host, kb, cp) && tg_cuda_kv_event_record(b->in_ready[s], cp) &&
+             tg_cuda_kv_stream_wait(stream, b->in_ready[s]);
     if (!ok) { set_err("%s", tg_cuda_kv_last_error()); return 0; }
-    if (!batch_decode(b, q, k, v, o, g, st)) return 0;
+    float* direct = g ? NULL : (float*)tg_cuda_kv_host_device_ptr(out_host);
+    if (!batch_decode(b, q, k, v, direct ? direct : o, g, stream)) return 0;
     const void* src = g ? (const void*)g->mem : (const void*)o;
     const uint64_t ob = g ? (uint64_t)g->world * g->elems * 4 : qb;
-    if (!tg_cuda_kv_d2h(out_host, src, ob, st)) { set_err("%s", tg_cuda_kv_last_error()); return 0; }
+    if ((!direct && !tg_cuda_kv_d2h(out_host, src, ob, stream)) ||
+        !tg_cuda_kv_event_record(b->slot_free[s], stream)) {
+        set_err("%s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    b->slot_used[s] = 1;
+    b->slot ^= 1u;
     return 1;
 }
 

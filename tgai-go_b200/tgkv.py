@@ -144,6 +144,13 @@ PROTOS = {
     "tg_cuda_kv_attn_last_launches": (u32, []),
     "tg_cuda_kv_attn_last_kernel": (i32, []),
     "tg_cuda_kv_attn_last_split": (u32, []),
+    "tg_cuda_kv_host_device_ptr": (vp, [vp]),
+    "tg_cuda_kv_stream_create": (vp, []),
+    "tg_cuda_kv_stream_destroy": (None, [vp]),
+    "tg_cuda_kv_event_create": (vp, []),
+    "tg_cuda_kv_event_destroy": (None, [vp]),
+    "tg_cuda_kv_event_record": (i32, [vp, vp]),
+    "tg_cuda_kv_stream_wait": (i32, [vp, vp]),
     "tg_cuda_kv_ipc_handle": (i32, [vp, vp]),
     "tg_cuda_kv_ipc_open": (vp, [vp]),
     "tg_cuda_kv_ipc_close": (None, [vp]),
