@@ -12,8 +12,10 @@
 // of one KV head -- and its KV tiles of 128 positions are divided among the
 // n_split CTAs of one thread-block cluster, so that a turn's few row blocks
 // still fill the GPU.  Each CTA keeps an unnormalised partial (O, running max
-// m, sum l) per row; after a cluster barrier every CTA merges a slice of the
-// rows from all partials over distributed shared memory and writes them out.
+// m, sum l) per row.  At the end each CTA finishes a slice of the rows: every
+// CTA copies its partial rows into the staging area of the CTA that finishes
+// them (shared-to-peer-shared bulk copies inside the cluster), and that CTA
+// merges them from its own shared memory and writes the output rows.
 //
 // Inside a CTA (320 threads):
 //   warps 0-7    softmax: row r = TMEM lane r is shared by warps r/32 and
@@ -24,8 +26,10 @@
 //                per tile: read S, mask the causal diagonal, online softmax
 //                in the log2 domain with lazy rescale, write P (bf16 hi, lo)
 //                over S in place; at the end read O and publish the partial;
-//   warp 8       TMA: K and V tiles (2 x 64-column boxes each, 128-byte
-//                swizzled) into separate 2-stage rings;
+//   warp 8       TMA: the q block (4 swizzled boxes of 32 head dims, rows past
+//                n_q zero-filled) into the staging area, then K and V tiles
+//                (2 x 64-column boxes each, 128-byte swizzled) into separate
+//                2-stage rings;
 //   warp 9       allocates the 512 TMEM columns; one lane issues the MMAs,
 //                both with the A operand in TMEM: S = (Q_hi + Q_lo) K^T into
 //                one of two S buffers, O += (P_hi + P_lo) V with V as an
