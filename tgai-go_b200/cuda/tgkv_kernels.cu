@@ -562,11 +562,15 @@ namespace tgkv {
 // ------------------------------------------------------------ append
 // One thread moves 8 consecutive elements of one K or V row (blockIdx.y picks
 // K or V): two 16-byte loads of fp32, one or two 16-byte stores.
-// The attention launched next (a programmatic dependent) may start its
-// setup right away; it reads nothing before this grid has completed.
+// Launched as a programmatic dependent itself: it may start while the
+// previous kernel finishes, but writes nothing before that kernel has
+// completed (an LCP re-append overwrites rows the last attention read).  The
+// attention launched next may start its setup right away; it reads nothing
+// before this grid has completed.
 template <int DT>
 __global__ void __launch_bounds__(256) append_kernel(const __grid_constant__ TGKvAppendParams p) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint64_t vec_per_row = p.kv_dim / 8;
     const uint64_t rows = (uint64_t)p.n_items * p.rows_per_item;
     const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -711,12 +715,21 @@ extern "C" int tgkv_launch_append(const TGKvAppendParams* p, int dtype, void* st
     const uint64_t vecs = (uint64_t)p->n_items * p->rows_per_item * (p->kv_dim / 8);
     if (vecs == 0) return 0;
     if (p->kv_dim % 8) return (int)cudaErrorInvalidValue;
-    dim3 grid((unsigned)((vecs + 255) / 256), 2);
-    if (dtype == 0)
-        tgkv::append_kernel<0><<<grid, 256, 0, (cudaStream_t)stream>>>(*p);
-    else
-        tgkv::append_kernel<1><<<grid, 256, 0, (cudaStream_t)stream>>>(*p);
-    return (int)cudaGetLastError();
+    static const bool pdl = [] {
+        const char* e = getenv("TGKV_PDL");
+        return !(e && e[0] == '0');
+    }();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((vecs + 255) / 256), 2);
+    cfg.blockDim = dim3(256);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    if (dtype == 0) return (int)cudaLaunchKernelEx(&cfg, tgkv::append_kernel<0>, *p);
+    return (int)cudaLaunchKernelEx(&cfg, tgkv::append_kernel<1>, *p);
 }
 
 namespace tgkv {
