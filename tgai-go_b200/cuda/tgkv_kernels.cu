@@ -244,25 +244,34 @@ __device__ __noinline__ void combine_segment(const TGKvAttnParams& p, uint32_t f
             }
         }
         consumer_bar();
+        // Weighted sums, all of this thread's outputs at once and kBatch
+        // partials per step, so that kOut * kBatch loads from L2 are in
+        // flight together (the merge sits on the launch's critical path).
+        constexpr int kBatch = 8;
+        const float* po[kOut];
+        const float* fc[kOut];
 #pragma unroll
         for (int k = 0; k < kOut; ++k) {
-            const int idx = tid + k * 128;
-            if (idx < GT * HD) {
-                const int h = idx / HD, d = idx % HD;
-                const float* po = p.part_o + ((uint64_t)(first + c0) * GT + h) * HD + d;
-                const float* fc = sm_fac + h * kFacBlock;
-                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-                uint32_t c = 0;
-                for (; c + 4 <= nb; c += 4) {
-                    a0 += __ldcg(po + (uint64_t)(c + 0) * GT * HD) * fc[c + 0];
-                    a1 += __ldcg(po + (uint64_t)(c + 1) * GT * HD) * fc[c + 1];
-                    a2 += __ldcg(po + (uint64_t)(c + 2) * GT * HD) * fc[c + 2];
-                    a3 += __ldcg(po + (uint64_t)(c + 3) * GT * HD) * fc[c + 3];
-                }
-                for (; c < nb; ++c) a0 += __ldcg(po + (uint64_t)c * GT * HD) * fc[c];
-                acc[k] += (a0 + a1) + (a2 + a3);
-            }
+            const int idx = min(tid + k * 128, GT * HD - 1);     // clamped: no stray reads
+            const int h = idx / HD, d = idx % HD;
+            po[k] = p.part_o + ((uint64_t)(first + c0) * GT + h) * HD + d;
+            fc[k] = sm_fac + h * kFacBlock;
         }
+        uint32_t c = 0;
+        for (; c + kBatch <= nb; c += kBatch) {
+            float x[kOut][kBatch];
+#pragma unroll
+            for (int k = 0; k < kOut; ++k)
+#pragma unroll
+                for (int u = 0; u < kBatch; ++u) x[k][u] = __ldcg(po[k] + (uint64_t)(c + u) * GT * HD);
+#pragma unroll
+            for (int k = 0; k < kOut; ++k)
+#pragma unroll
+                for (int u = 0; u < kBatch; ++u) acc[k] += x[k][u] * fc[k][c + u];
+        }
+        for (; c < nb; ++c)
+#pragma unroll
+            for (int k = 0; k < kOut; ++k) acc[k] += __ldcg(po[k] + (uint64_t)c * GT * HD) * fc[k][c];
     }
 #pragma unroll
     for (int h = 0; h < GT; ++h) {
