@@ -38,7 +38,6 @@ namespace tgkv {
 constexpr int kTile = TGKV_TILE;     // positions per stage
 constexpr int kConsumerWarps = 4;    // 8 positions of a stage per warp
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kFacBlock = 256;       // partials merged per block in the combine
 
 
 // Error codes written to p.err.
@@ -73,10 +72,12 @@ struct AttnCfg {
     static constexpr int OFF_ALPHA = OFF_P + kConsumerWarps * 32 * 4;
     static constexpr int OFF_CO = OFF_ALPHA + kConsumerWarps * 4 * 4;
     static constexpr int OFF_CML = OFF_CO + kConsumerWarps * GT * HD * 4;
-    static constexpr int OFF_FAC = OFF_CML + kConsumerWarps * GT * 2 * 4;   // [GT][kFacBlock]
-    static constexpr int OFF_RED = OFF_FAC + GT * kFacBlock * 4;               // [4][GT][2]
+    static constexpr int OFF_RED = OFF_CML + kConsumerWarps * GT * 2 * 4;   // [4][GT][2]
     static constexpr int OFF_FLAG = OFF_RED + kConsumerWarps * GT * 2 * 4;
     static constexpr int SMEM = OFF_FLAG + 16;
+    // the combine reuses the idle ring: (m, l) pairs, then 128 float4 sums
+    static constexpr int OFF_ACC = OFF_BAR - 128 * 16;
+    static constexpr int ML_CAP = OFF_ACC / (GT * 8);                  // partials
 };
 
 // Unpack one lane vector (VW bytes at p) into EPV/2 float2.
@@ -192,105 +193,127 @@ __device__ __noinline__ void gather_signal(const TGKvAttnParams& p, int tid) {
 }
 
 // Merge the nparts partials of one segment (slots first .. first+nparts-1;
-// this CTA finished last): per-head maxima, then blocks of per-partial
-// factors in shared memory and coalesced weighted sums.  Kept out of line so
-// the streaming loop keeps its registers.
-template <int GT, int HD>
+// this CTA finished last).  The merge sits on the launch's critical path and
+// is L2-latency bound, so it is built around few dependent round trips:
+//  - the first batch of partial outputs is requested before anything else;
+//  - one pass loads every (m, l) pair, reduces the per-head maxima and keeps
+//    the pairs in the idle K/V ring (sm_ml), where the factors
+//    exp2(m - M) then replace m in place;
+//  - the weighted sums read one float4 of a partial per thread (thread v of
+//    NV = GT*HD/4 vectors; 128/NV groups take every (128/NV)-th partial),
+//    kB partials per step, so 128 * kB * 16 bytes are in flight per CTA.
+// Segments of more than CAP partials reload the pairs block by block.
+// Kept out of line so the streaming loop keeps its registers.
+template <int GT, int HD, int CAP>
 __device__ __noinline__ void combine_segment(const TGKvAttnParams& p, uint32_t first,
                                              uint32_t nparts, uint64_t row, uint32_t head0,
-                                             float* sm_fac, float* sm_red, int tid, int lane,
-                                             int warp) {
-    float mloc[GT];
+                                             float2* sm_ml, float4* sm_acc, float* sm_red,
+                                             int tid, int lane, int warp) {
+    constexpr int NV = GT * HD / 4;            // float4 per partial output
+    constexpr int G = 128 / NV;                // groups of threads over the partials
+    constexpr int kB = 16;                     // partials per thread and step
+    constexpr int kMl = 8;                     // (m, l) pairs per thread and step
+    static_assert(NV <= 128 && 128 % NV == 0, "partial vectors");
+    const int v = tid % NV, g = tid / NV;
+    const int h = (v * 4) / HD;                 // head of this thread's vector
+    const int hm = tid % GT;                    // head of this thread's (m, l) pairs
+    const float4* po = reinterpret_cast<const float4*>(p.part_o) + (uint64_t)first * NV + v;
+    const float2* pml = reinterpret_cast<const float2*>(p.part_ml) + (uint64_t)first * GT;
+    const uint32_t nb0 = min((uint32_t)CAP, nparts);
+
+    // first step of block 0's weighted sums, in flight during the pair pass
+    float4 x[kB];
 #pragma unroll
-    for (int h = 0; h < GT; ++h) mloc[h] = -INFINITY;
-    for (uint32_t c = tid; c < nparts; c += 128) {
+    for (int u = 0; u < kB; ++u) {
+        const uint32_t c = (uint32_t)(g + u * G);
+        x[u] = c < nb0 ? __ldcg(po + (uint64_t)c * NV) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+
+    // ---- per-head maxima over all pairs; block 0's pairs stay in shared memory
+    const uint32_t ne = nparts * GT;
+    float mloc = -INFINITY;
+    for (uint32_t e0 = 0; e0 < ne; e0 += 128 * kMl) {
+        float2 y[kMl];
 #pragma unroll
-        for (int h = 0; h < GT; ++h)
-            mloc[h] = fmaxf(mloc[h], __ldcg(&p.part_ml[((uint64_t)(first + c) * GT + h) * 2]));
+        for (int k = 0; k < kMl; ++k) {
+            const uint32_t e = e0 + (uint32_t)(k * 128 + tid);
+            y[k] = e < ne ? __ldcg(pml + e) : make_float2(-INFINITY, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < kMl; ++k) {
+            const uint32_t e = e0 + (uint32_t)(k * 128 + tid);
+            mloc = fmaxf(mloc, y[k].x);
+            if (e < nb0 * GT) sm_ml[e] = y[k];
+        }
     }
 #pragma unroll
-    for (int h = 0; h < GT; ++h) {
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1)
-            mloc[h] = fmaxf(mloc[h], __shfl_xor_sync(0xffffffffu, mloc[h], o));
-        if (lane == 0) sm_red[(warp * GT + h) * 2] = mloc[h];
-    }
+    for (int o = 16; o >= GT; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+    if (lane < GT) sm_red[(warp * GT + lane) * 2] = mloc;
     consumer_bar();
-    float M[GT];
+    float Mh = -INFINITY;
 #pragma unroll
-    for (int h = 0; h < GT; ++h) {
-        M[h] = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) M[h] = fmaxf(M[h], sm_red[(w * GT + h) * 2]);
-    }
-    constexpr int kOut = (GT * HD + 127) / 128;    // outputs per thread
-    float acc[kOut];
-#pragma unroll
-    for (int k = 0; k < kOut; ++k) acc[k] = 0.f;
-    float lsum[GT];
-#pragma unroll
-    for (int h = 0; h < GT; ++h) lsum[h] = 0.f;
-    for (uint32_t c0 = 0; c0 < nparts; c0 += kFacBlock) {
-        const uint32_t nb = min((uint32_t)kFacBlock, nparts - c0);
-        consumer_bar();                           // the previous block's factors are used
-        for (uint32_t c = tid; c < nb; c += 128) {
-            const uint64_t sl = first + c0 + c;
-#pragma unroll
-            for (int h = 0; h < GT; ++h) {
-                const float mc = __ldcg(&p.part_ml[(sl * GT + h) * 2]);
-                const float f = (mc == -INFINITY) ? 0.f : exp2f(mc - M[h]);
-                sm_fac[h * kFacBlock + c] = f;
-                lsum[h] += __ldcg(&p.part_ml[(sl * GT + h) * 2 + 1]) * f;
-            }
+    for (int w = 0; w < kConsumerWarps; ++w) Mh = fmaxf(Mh, sm_red[(w * GT + hm) * 2]);
+
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float lsum = 0.f;
+    for (uint32_t b0 = 0; b0 < nparts; b0 += CAP) {
+        const uint32_t nb = min((uint32_t)CAP, nparts - b0);
+        if (b0) {                                  // later blocks: pairs from L2 again
+            consumer_bar();                        // the previous block's factors are used
+            for (uint32_t e = tid; e < nb * GT; e += 128) sm_ml[e] = __ldcg(pml + (uint64_t)b0 * GT + e);
+        }
+        // factors in place of m (each thread rewrites only the pairs it owns)
+        for (uint32_t e = tid; e < nb * GT; e += 128) {
+            const float2 ml = sm_ml[e];
+            const float f = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - Mh);
+            lsum += ml.y * f;
+            sm_ml[e].x = f;
         }
         consumer_bar();
-        // Weighted sums, all of this thread's outputs at once and kBatch
-        // partials per step, so that kOut * kBatch loads from L2 are in
-        // flight together (the merge sits on the launch's critical path).
-        constexpr int kBatch = 8;
-        const float* po[kOut];
-        const float* fc[kOut];
+        for (uint32_t c0 = 0; c0 < nb; c0 += (uint32_t)(G * kB)) {
+            if (b0 || c0) {
 #pragma unroll
-        for (int k = 0; k < kOut; ++k) {
-            const int idx = min(tid + k * 128, GT * HD - 1);     // clamped: no stray reads
-            const int h = idx / HD, d = idx % HD;
-            po[k] = p.part_o + ((uint64_t)(first + c0) * GT + h) * HD + d;
-            fc[k] = sm_fac + h * kFacBlock;
+                for (int u = 0; u < kB; ++u) {
+                    const uint32_t c = c0 + (uint32_t)(g + u * G);
+                    x[u] = c < nb ? __ldcg(po + (uint64_t)(b0 + c) * NV)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kB; ++u) {
+                const uint32_t c = c0 + (uint32_t)(g + u * G);
+                const float f = c < nb ? sm_ml[c * GT + h].x : 0.f;
+                acc.x += x[u].x * f;
+                acc.y += x[u].y * f;
+                acc.z += x[u].z * f;
+                acc.w += x[u].w * f;
+            }
         }
-        uint32_t c = 0;
-        for (; c + kBatch <= nb; c += kBatch) {
-            float x[kOut][kBatch];
-#pragma unroll
-            for (int k = 0; k < kOut; ++k)
-#pragma unroll
-                for (int u = 0; u < kBatch; ++u) x[k][u] = __ldcg(po[k] + (uint64_t)(c + u) * GT * HD);
-#pragma unroll
-            for (int k = 0; k < kOut; ++k)
-#pragma unroll
-                for (int u = 0; u < kBatch; ++u) acc[k] += x[k][u] * fc[k][c + u];
-        }
-        for (; c < nb; ++c)
-#pragma unroll
-            for (int k = 0; k < kOut; ++k) acc[k] += __ldcg(po[k] + (uint64_t)c * GT * HD) * fc[k][c];
     }
+
+    // ---- totals: l per head over threads and warps, outputs over groups
 #pragma unroll
-    for (int h = 0; h < GT; ++h) {
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) lsum[h] += __shfl_xor_sync(0xffffffffu, lsum[h], o);
-        if (lane == 0) sm_red[(warp * GT + h) * 2 + 1] = lsum[h];
-    }
+    for (int o = 16; o >= GT; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    if (lane < GT) sm_red[(warp * GT + lane) * 2 + 1] = lsum;
+    if (G > 1) sm_acc[g * NV + v] = acc;
     consumer_bar();
+    if (g == 0) {
 #pragma unroll
-    for (int k = 0; k < kOut; ++k) {
-        const int idx = tid + k * 128;
-        if (idx < GT * HD) {
-            const int h = idx / HD, d = idx % HD;
-            float L = 0.f;
+        for (int k = 1; k < G; ++k) {
+            const float4 a = sm_acc[k * NV + v];
+            acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+        }
+        float L = 0.f;
 #pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) L += sm_red[(w * GT + h) * 2 + 1];
-            const float o = (L > 0.f) ? acc[k] / L : 0.f;
-            p.out[row + (uint64_t)(head0 + h) * HD + d] = o;
-            if (p.gather_world) gather_store(p, row + (uint64_t)(head0 + h) * HD + d, o);
+        for (int w = 0; w < kConsumerWarps; ++w) L += sm_red[(w * GT + h) * 2 + 1];
+        const bool any = L > 0.f;
+        const float o[4] = {any ? acc.x / L : 0.f, any ? acc.y / L : 0.f,
+                            any ? acc.z / L : 0.f, any ? acc.w / L : 0.f};
+        const uint64_t base = row + (uint64_t)(head0 + h) * HD + (v * 4) % HD;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            p.out[base + k] = o[k];
+            if (p.gather_world) gather_store(p, base + k, o[k]);
         }
     }
     if (p.gather_world) gather_signal(p, tid);
@@ -307,7 +330,6 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
     float* sm_alpha = reinterpret_cast<float*>(smem + C::OFF_ALPHA);  // [4][4]
     float* sm_co = reinterpret_cast<float*>(smem + C::OFF_CO);        // [4][GT][HD]
     float* sm_cml = reinterpret_cast<float*>(smem + C::OFF_CML);      // [4][GT][2]
-    float* sm_fac = reinterpret_cast<float*>(smem + C::OFF_FAC);      // [GT][kFacBlock]
     float* sm_red = reinterpret_cast<float*>(smem + C::OFF_RED);      // [4][GT][2]
     int* sm_flag = reinterpret_cast<int*>(smem + C::OFF_FLAG);        // [0] abort, [1] last
 
@@ -560,7 +582,11 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
     consumer_bar();
     if (!sm_flag[1]) return;
     __threadfence();
-    combine_segment<GT, HD>(p, ck.first, ck.nch, row, head0, sm_fac, sm_red, tid, lane, warp);
+    if (!sm_flag[0])                              // the ring is idle unless a wait gave up
+        combine_segment<GT, HD, C::ML_CAP>(p, ck.first, ck.nch, row, head0,
+                                           reinterpret_cast<float2*>(smem),
+                                           reinterpret_cast<float4*>(smem + C::OFF_ACC), sm_red,
+                                           tid, lane, warp);
     if (tid == 0) p.counters[cidx] = 0u;
 }
 
