@@ -12,7 +12,7 @@ import pytest
 ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
 PKG = os.path.join(ROOT, "tgai-go_b200")
 GOLDEN = os.path.join(ROOT, "tests", "golden")
-for p in (PKG, os.path.join(ROOT, "oracle")):
+for p in (PKG, os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")):
     if p not in sys.path:
         sys.path.insert(0, p)
 

@@ -18,6 +18,11 @@ this, it only reads the committed .npz files.
                      double-precision cpu_attention output.
   attntest.npz       tests/test_vk_attn_moe.c's attention scenario (srand(777),
                      MAXSEQ=256, NKV=40, POS=39 and POS=10).
+  forward.npz        whole-model logits of tg_forward (CPU engine) over the
+                     seeded synthetic models of tests/fwd_model.py (a MoE and a
+                     dense GQA model, written as .TG files), one row per step
+                     of their scripts: prefill, decode, a second sequence,
+                     LCP truncate + re-append.
 
 Usage: python tests/golden/gen_golden.py
 """
@@ -239,6 +244,46 @@ def attntest(ref, libc):
                         q=q, kv_rows=kvc[:, :NKV].copy(), out_pos39=outs[39], out_pos10=outs[10])
 
 
+def forward_golden(eng):
+    sys.path.insert(0, os.path.dirname(HERE))
+    import fwd_model as FM
+    eng.tg_load.restype = C.c_void_p
+    eng.tg_load.argtypes = [C.c_char_p, C.c_int, C.POINTER(C.c_int)]
+    eng.tg_kvcache_new.restype = C.c_void_p
+    eng.tg_kvcache_new.argtypes = [C.c_void_p, C.c_int]
+    eng.tg_kvcache_free.argtypes = [C.c_void_p]
+    eng.tg_forward.restype = P
+    eng.tg_forward.argtypes = [C.c_void_p, C.POINTER(C.c_int32), C.c_int, C.c_void_p, C.c_int]
+    eng.tg_free.argtypes = [C.c_void_p]
+    out = {}
+    for name, cfg in FM.CONFIGS.items():
+        seed = FM.SEEDS[name]
+        w = FM.weights(cfg, seed)
+        with tempfile.TemporaryDirectory() as td:
+            path = os.path.join(td, f"{name}.TG")
+            FM.write_tg(path, cfg, w)
+            err = C.c_int(0)
+            m = eng.tg_load(path.encode(), 0, C.byref(err))
+            if not m:
+                raise RuntimeError(f"tg_load({name}) failed: {err.value}")
+            caches = {}
+            logits = []
+            for seq_name, ids, pos in FM.script(cfg, seed):
+                if seq_name not in caches:
+                    caches[seq_name] = eng.tg_kvcache_new(m, cfg["max_seq"])
+                arr = (C.c_int32 * len(ids))(*ids.tolist())
+                lp = eng.tg_forward(m, arr, len(ids), caches[seq_name], int(pos))
+                if not lp:
+                    raise RuntimeError("tg_forward failed")
+                logits.append(np.ctypeslib.as_array(lp, shape=(cfg["vocab"],)).copy())
+            for c in caches.values():
+                eng.tg_kvcache_free(c)
+            eng.tg_free(m)
+        out[f"{name}_logits"] = np.array(logits, np.float32)
+        out[f"{name}_seed"] = np.int32(seed)
+    np.savez_compressed(os.path.join(HERE, "forward.npz"), **out)
+
+
 def main():
     if not os.path.isdir(REF) or not os.path.exists(os.path.join(REF_LIB, "libtgkv_ref.so")):
         sys.exit("reference checkout or oracle/_ref missing: run `make -C oracle ref` first")
@@ -249,6 +294,7 @@ def main():
     engine_fixture(eng)
     kvtest(ref, libc)
     attntest(ref, libc)
+    forward_golden(eng)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")

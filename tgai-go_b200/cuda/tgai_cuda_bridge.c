@@ -234,7 +234,10 @@ void* tg_cuda_kv_malloc(size_t bytes) {
     pthread_mutex_unlock(&g_mu);
     void* p = NULL;
     if (!cuda_ok(cudaMalloc(&p, bytes ? bytes : 1), "cudaMalloc")) return NULL;
-    if (!cuda_ok(cudaMemset(p, 0, bytes), "cudaMemset")) {
+    /* the zero fill completes before the pointer is returned: work queued on
+     * non-blocking streams is not ordered after the legacy stream's memset */
+    if (!cuda_ok(cudaMemset(p, 0, bytes), "cudaMemset") ||
+        !cuda_ok(cudaStreamSynchronize(0), "cudaMemset sync")) {
         cudaFree(p);
         return NULL;
     }

@@ -1,0 +1,61 @@
+/* tgkv_forward.h -- launchers of the whole-forward kernels (tgkv_forward.cu),
+ * internal to libtgkv.so.  Every launcher queues on `stream` and returns a
+ * cudaError_t value (0 = launched). */
+#ifndef TGKV_FORWARD_H
+#define TGKV_FORWARD_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* x[t] = emb[ids[t]] (ids outside [0, rows) read row unk). */
+int tgkv_fwd_embed(float* x, const float* emb, const int32_t* ids, uint32_t seq, uint32_t d,
+                   uint32_t rows, int32_t unk, void* stream);
+
+/* out[r] = x[r] * (1 / sqrt(mean(x[r]^2) + eps)) * w, for rows r < n_rows
+ * (row strides in elements).  out may equal x. */
+int tgkv_fwd_rmsnorm(float* out, const float* x, const float* w, uint32_t n_rows, uint32_t d,
+                     uint64_t out_stride, uint64_t x_stride, float eps, void* stream);
+
+/* y[r][c] += b[c]. */
+int tgkv_fwd_bias(float* y, const float* b, uint32_t rows, uint32_t cols, void* stream);
+
+/* h[r][j] = silu(a) * b with a = ab[r][j], b = ab[r][dff + j]; a is first
+ * clamped to [-88, 88] when clamp != 0 (the dense FFN does, the experts do not). */
+int tgkv_fwd_silu_mul(float* h, const float* ab, uint32_t rows, uint32_t dff, int clamp,
+                      void* stream);
+
+/* Router: logits [seq][ne] (+ bias [ne] when not NULL), top-na experts by
+ * value, softmax over them.  top_ids/top_w [seq][na]; counts[ne] must be
+ * zero on entry and receive, per expert, how many (token, k) pairs chose it;
+ * lists[e * seq * na + i] holds those pairs (t * na + k), in no fixed order. */
+int tgkv_fwd_route(const float* logits, const float* bias, int32_t* top_ids, float* top_w,
+                   uint32_t* counts, uint32_t* lists, uint32_t seq, uint32_t ne, uint32_t na,
+                   void* stream);
+
+/* Expert FFN, grouped by expert.  Phase 1: for every pair p of expert e,
+ * h[p][j] = silu(W1[e][j] . x[p / na]) * (W2[e][j] . x[p / na]) with
+ * w12 = [ne][2 * dff][d] (W1 rows, then W2 rows).  Phase 2:
+ * y[p][i] = W3[e][i] . h[p] with w3 = [ne][d][dff].  d and dff multiples of 4. */
+int tgkv_fwd_expert_w12(const float* w12, const float* x, float* h, const uint32_t* counts,
+                        const uint32_t* lists, uint32_t seq, uint32_t ne, uint32_t na,
+                        uint32_t d, uint32_t dff, void* stream);
+int tgkv_fwd_expert_w3(const float* w3, const float* h, float* y, const uint32_t* counts,
+                       const uint32_t* lists, uint32_t seq, uint32_t ne, uint32_t na,
+                       uint32_t d, uint32_t dff, void* stream);
+
+/* x[t] += sum over k of top_w[t][k] * y[t * na + k] (k in order, invalid
+ * experts skipped). */
+int tgkv_fwd_moe_combine(float* x, const float* y, const int32_t* top_ids, const float* top_w,
+                         uint32_t seq, uint32_t d, uint32_t ne, uint32_t na, void* stream);
+
+/* Page-locked host memory (NULL on failure). */
+void* tgkv_fwd_host_alloc(size_t bytes);
+void  tgkv_fwd_host_free(void* p);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TGKV_FORWARD_H */

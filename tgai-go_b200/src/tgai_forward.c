@@ -1,0 +1,728 @@
+/* tgai_forward.c -- whole-model forward on a B200 around the KV path.
+ *
+ * Host C.  The block structure and its order follow the engine's CPU forward
+ * (src/tgai_engine.c:3821-4358 transformer_block, :4361-4507 tg_forward):
+ *
+ *   x = emb[ids]                                       (ids out of range -> unk)
+ *   per layer:  ln = rmsnorm(x, ln1);  qkv = ln . [Wq; Wk; Wv]^T (+ biases)
+ *               RoPE(q, k) at positions pos.., K/V appended to the layer cache
+ *               attn = causal GQA attention over the cache
+ *               x += attn . Wo^T
+ *               ln = rmsnorm(x, ln2)
+ *               dense: x += (silu(clamp(ln.W1^T)) * ln.W2^T) . W3^T
+ *               MoE:   top-k of ln.Wr^T (+ bias), softmax over the k,
+ *                      x += sum_k w_k * W3_e (silu(W1_e ln) * W2_e ln)
+ *   logits = rmsnorm(x_last, final_norm) . emb^T
+ *
+ * The device side is one stream per sequence ("slot", keyed by the caller's
+ * pointer as cuda/tgai_cuda.cu:1656-1672 keys them): our kernels
+ * (tgkv_forward.cu), the KV path's RoPE+append and attention kernels, and
+ * fp32 cuBLAS GEMMs for the projections, the router and the LM head (opened
+ * with dlopen on first use, so the KV path alone never needs cuBLAS).  The
+ * only host synchronisation per forward is the final logits copy; the MoE
+ * routing stays on the device (the reference bridge copies the top-k ids to
+ * the host once per layer, cuda/tgai_cuda.cu:1532-1590).
+ *
+ * Slot rules of the reference bridge: at most TGAI_CUDA_KV_SLOTS slots
+ * (default 16, 1..64; cuda/tgai_cuda.cu:790-800), a request beyond them is
+ * rejected and counted; a forward whose cache_pos is past the slot's last
+ * written position clears the slot's KV first (:1674-1711); otherwise the
+ * rows [0, cache_pos) are kept and the new tokens overwrite from cache_pos on
+ * (LCP truncate + re-append).  Each slot's KV holds max_seq_len positions
+ * from its first use (the reference grows by relayout from 2048; 180 GB of
+ * HBM makes the fixed capacity the simpler choice).
+ */
+#include "tgai_engine_bridge.h"
+#include "tgai_cuda_bridge.h"
+#include "tgai_gpu_dispatch.h"
+#include "tgai_kv_cache.h"
+#include "tgkv_forward.h"
+
+#include <cublas_v2.h>
+#include <dlfcn.h>
+#include <math.h>
+#include <pthread.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define HIDDEN __attribute__((visibility("hidden")))
+
+static _Thread_local char t_err[256] = "fwd: no error";
+static _Thread_local uint32_t t_launches;
+
+static void set_err(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_err, sizeof(t_err), fmt, ap);
+    va_end(ap);
+}
+
+const char* tg_fwd_last_error(void) { return t_err; }
+uint32_t tg_fwd_last_launches(void) { return t_launches; }
+
+/* ---- cuBLAS, opened on first use ----------------------------------------- */
+typedef cublasStatus_t (*blas_create_fn)(cublasHandle_t*);
+typedef cublasStatus_t (*blas_destroy_fn)(cublasHandle_t);
+typedef cublasStatus_t (*blas_stream_fn)(cublasHandle_t, cudaStream_t);
+typedef cublasStatus_t (*blas_sgemm_fn)(cublasHandle_t, cublasOperation_t, cublasOperation_t,
+                                        int, int, int, const float*, const float*, int,
+                                        const float*, int, const float*, float*, int);
+static struct {
+    int ok;
+    char why[200];
+    blas_create_fn create;
+    blas_destroy_fn destroy;
+    blas_stream_fn set_stream;
+    blas_sgemm_fn sgemm;
+} g_blas;
+static pthread_once_t g_blas_once = PTHREAD_ONCE_INIT;
+
+static void blas_open(void) {
+    static const char* names[] = {"libcublas.so.12", "libcublas.so"};
+    void* h = NULL;
+    for (size_t i = 0; i < sizeof(names) / sizeof(names[0]) && !h; i++)
+        h = dlopen(names[i], RTLD_NOW | RTLD_LOCAL);
+    if (!h) {
+        snprintf(g_blas.why, sizeof(g_blas.why), "cuBLAS not loadable: %s", dlerror());
+        return;
+    }
+    g_blas.create = (blas_create_fn)dlsym(h, "cublasCreate_v2");
+    g_blas.destroy = (blas_destroy_fn)dlsym(h, "cublasDestroy_v2");
+    g_blas.set_stream = (blas_stream_fn)dlsym(h, "cublasSetStream_v2");
+    g_blas.sgemm = (blas_sgemm_fn)dlsym(h, "cublasSgemm_v2");
+    if (!g_blas.create || !g_blas.destroy || !g_blas.set_stream || !g_blas.sgemm) {
+        snprintf(g_blas.why, sizeof(g_blas.why), "cuBLAS lacks the v2 GEMM entry points");
+        return;
+    }
+    g_blas.ok = 1;
+}
+
+static int blas_ready(void) {
+    pthread_once(&g_blas_once, blas_open);
+    if (!g_blas.ok) set_err("%s", g_blas.why);
+    return g_blas.ok;
+}
+
+/* ---- model and slots ------------------------------------------------------ */
+typedef struct {
+    float* ln1;        /* [d] */
+    float* ln2;        /* [d] */
+    float* wqkv;       /* [q_dim + 2 kv_dim][d]: Wq rows, Wk rows, Wv rows */
+    float* bqkv;       /* [q_dim + 2 kv_dim] or NULL */
+    float* wo;         /* [d][q_dim] */
+    float* w12;        /* dense [2 dff][d]; MoE [ne][2 dff][d]: W1 rows then W2 rows */
+    float* w3;         /* dense [d][dff];   MoE [ne][d][dff] */
+    float* router;     /* [ne][d] */
+    float* qb;         /* [ne] or NULL */
+} Layer;
+
+typedef struct Slot {
+    const void* key;
+    int used;
+    int id;
+    TGKvCache** kv;          /* one per layer */
+    int last_pos;            /* positions [0, last_pos) written by this slot; -1 none */
+    int kv_hi;
+    void* stream;
+    cublasHandle_t blas;
+    uint32_t cap;            /* token rows the workspaces hold */
+    float *x, *ln, *qkv, *q, *attn, *ab, *h, *router, *top_w, *y, *logits;
+    int32_t *top_ids, *ids;
+    uint32_t *counts, *lists;
+    int32_t* h_ids;          /* page-locked */
+    float* h_logits;         /* page-locked [vocab] */
+} Slot;
+
+struct TGFwdModel {
+    TGFwdConfig c;
+    uint32_t hd, nkv, q_dim, kv_dim, qkv_dim, rows;
+    Layer* L;
+    float *emb, *fnorm, *cs, *sn;
+    uint64_t wbytes;
+    pthread_mutex_t mu;
+    Slot* slots;
+    uint32_t max_slots, live;
+    long long rejects;
+};
+
+/* Device copy of n floats from host (blocking). */
+static float* upload(TGFwdModel* m, const float* src, uint64_t n) {
+    float* d = (float*)tg_cuda_kv_malloc(n * sizeof(float));
+    if (!d) { set_err("device allocation of %llu bytes failed", (unsigned long long)(n * 4)); return NULL; }
+    if (!tg_cuda_kv_h2d(d, src, n * sizeof(float), NULL)) {
+        set_err("weight upload failed: %s", tg_cuda_kv_last_error());
+        tg_cuda_kv_free(d);
+        return NULL;
+    }
+    m->wbytes += n * sizeof(float);
+    return d;
+}
+
+/* A tensor of exactly rows x cols elements (cols 1 for 1-D), or NULL. */
+static const float* tensor(TGFwdWeightFn get, void* ctx, const char* name, uint32_t rows,
+                           uint32_t cols, int required) {
+    uint32_t shape[2] = {0, 0};
+    const float* p = get(ctx, name, shape);
+    if (!p) {
+        if (required) set_err("missing weight %s", name);
+        return NULL;
+    }
+    if ((uint64_t)shape[0] * shape[1] != (uint64_t)rows * cols) {
+        set_err("weight %s has shape [%u, %u], expected [%u, %u]", name, shape[0], shape[1],
+                rows, cols);
+        return NULL;
+    }
+    return p;
+}
+
+/* An optional tensor: NULL and *bad = 0 when absent, NULL and *bad = 1 when
+ * present with the wrong size. */
+static const float* optional(TGFwdWeightFn get, void* ctx, const char* name, uint32_t rows,
+                             uint32_t cols, int* bad) {
+    uint32_t shape[2] = {0, 0};
+    *bad = 0;
+    if (!get(ctx, name, shape)) return NULL;
+    const float* p = tensor(get, ctx, name, rows, cols, 1);
+    if (!p) *bad = 1;
+    return p;
+}
+
+static void free_layer(Layer* l) {
+    tg_cuda_kv_free(l->ln1);
+    tg_cuda_kv_free(l->ln2);
+    tg_cuda_kv_free(l->wqkv);
+    tg_cuda_kv_free(l->bqkv);
+    tg_cuda_kv_free(l->wo);
+    tg_cuda_kv_free(l->w12);
+    tg_cuda_kv_free(l->w3);
+    tg_cuda_kv_free(l->router);
+    tg_cuda_kv_free(l->qb);
+}
+
+static void slot_release_mem(TGFwdModel* m, Slot* s);
+
+void tg_fwd_destroy(TGFwdModel* m) {
+    if (!m) return;
+    if (m->slots)
+        for (uint32_t i = 0; i < m->max_slots; i++) slot_release_mem(m, &m->slots[i]);
+    free(m->slots);
+    if (m->L) {
+        for (uint32_t l = 0; l < m->c.n_layers; l++) free_layer(&m->L[l]);
+        free(m->L);
+    }
+    tg_cuda_kv_free(m->emb);
+    tg_cuda_kv_free(m->fnorm);
+    tg_cuda_kv_free(m->cs);
+    tg_cuda_kv_free(m->sn);
+    pthread_mutex_destroy(&m->mu);
+    free(m);
+}
+
+/* Concatenate row blocks into one host buffer and upload it. */
+static float* upload_cat(TGFwdModel* m, const float* const* parts, const uint64_t* n, int k) {
+    uint64_t tot = 0;
+    for (int i = 0; i < k; i++) tot += n[i];
+    float* h = (float*)malloc(tot * sizeof(float));
+    if (!h) { set_err("host allocation failed"); return NULL; }
+    uint64_t o = 0;
+    for (int i = 0; i < k; i++) {
+        if (parts[i]) memcpy(h + o, parts[i], n[i] * sizeof(float));
+        else memset(h + o, 0, n[i] * sizeof(float));
+        o += n[i];
+    }
+    float* d = upload(m, h, tot);
+    free(h);
+    return d;
+}
+
+static int load_layer(TGFwdModel* m, uint32_t l, TGFwdWeightFn get, void* ctx) {
+    const uint32_t d = m->c.d_model, dff = m->c.d_ff, ne = m->c.n_experts;
+    Layer* L = &m->L[l];
+    char name[160];
+    int bad = 0;
+#define NAME(...) (snprintf(name, sizeof(name), __VA_ARGS__), name)
+    const float* p;
+    if (!(p = tensor(get, ctx, NAME("blocks.%u.ln1.weight", l), d, 1, 1)) || !(L->ln1 = upload(m, p, d)))
+        return 0;
+    if (!(p = tensor(get, ctx, NAME("blocks.%u.ln2.weight", l), d, 1, 1)) || !(L->ln2 = upload(m, p, d)))
+        return 0;
+    {
+        const float* w[3];
+        const float* b[3];
+        uint64_t nw[3] = {(uint64_t)m->q_dim * d, (uint64_t)m->kv_dim * d, (uint64_t)m->kv_dim * d};
+        uint64_t nb[3] = {m->q_dim, m->kv_dim, m->kv_dim};
+        static const char* pn[3] = {"q_proj", "k_proj", "v_proj"};
+        int any_bias = 0;
+        for (int i = 0; i < 3; i++) {
+            if (!(w[i] = tensor(get, ctx, NAME("blocks.%u.attn.%s.weight", l, pn[i]),
+                                (uint32_t)(nb[i]), d, 1)))
+                return 0;
+            b[i] = optional(get, ctx, NAME("blocks.%u.attn.%s.bias", l, pn[i]), (uint32_t)nb[i], 1, &bad);
+            if (bad) return 0;
+            any_bias |= b[i] != NULL;
+        }
+        if (!(L->wqkv = upload_cat(m, w, nw, 3))) return 0;
+        if (any_bias && !(L->bqkv = upload_cat(m, b, nb, 3))) return 0;
+    }
+    if (!(p = tensor(get, ctx, NAME("blocks.%u.attn.out_proj.weight", l), d, m->q_dim, 1)) ||
+        !(L->wo = upload(m, p, (uint64_t)d * m->q_dim)))
+        return 0;
+    if (ne == 0) {
+        const float* w[2];
+        uint64_t nw[2] = {(uint64_t)dff * d, (uint64_t)dff * d};
+        if (!(w[0] = tensor(get, ctx, NAME("blocks.%u.ffn.w1.weight", l), dff, d, 1))) return 0;
+        if (!(w[1] = tensor(get, ctx, NAME("blocks.%u.ffn.w2.weight", l), dff, d, 1))) return 0;
+        if (!(L->w12 = upload_cat(m, w, nw, 2))) return 0;
+        if (!(p = tensor(get, ctx, NAME("blocks.%u.ffn.w3.weight", l), d, dff, 1)) ||
+            !(L->w3 = upload(m, p, (uint64_t)d * dff)))
+            return 0;
+        return 1;
+    }
+    if (!(p = tensor(get, ctx, NAME("blocks.%u.moe.router.weight", l), ne, d, 1)) ||
+        !(L->router = upload(m, p, (uint64_t)ne * d)))
+        return 0;
+    p = optional(get, ctx, NAME("blocks.%u.moe._qb_bias", l), ne, 1, &bad);
+    if (bad || (p && !(L->qb = upload(m, p, ne)))) return 0;
+    const uint64_t per = (uint64_t)dff * d;
+    const float** w12 = (const float**)calloc(2 * ne, sizeof(float*));
+    const float** w3 = (const float**)calloc(ne, sizeof(float*));
+    uint64_t* n12 = (uint64_t*)calloc(2 * ne, sizeof(uint64_t));
+    int ok = w12 && w3 && n12;
+    if (!ok) set_err("host allocation failed");
+    for (uint32_t e = 0; ok && e < ne; e++) {
+        n12[2 * e] = n12[2 * e + 1] = per;
+        ok = (w12[2 * e] = tensor(get, ctx, NAME("blocks.%u.moe.experts.%u.w1.weight", l, e), dff, d, 1)) &&
+             (w12[2 * e + 1] = tensor(get, ctx, NAME("blocks.%u.moe.experts.%u.w2.weight", l, e), dff, d, 1)) &&
+             (w3[e] = tensor(get, ctx, NAME("blocks.%u.moe.experts.%u.w3.weight", l, e), d, dff, 1));
+    }
+    if (ok) ok = (L->w12 = upload_cat(m, w12, n12, (int)(2 * ne))) != NULL;
+    if (ok) {
+        for (uint32_t e = 0; e < ne; e++) n12[e] = per;
+        ok = (L->w3 = upload_cat(m, w3, n12, (int)ne)) != NULL;
+    }
+    free(w12);
+    free(w3);
+    free(n12);
+#undef NAME
+    return ok;
+}
+
+TGFwdModel* tg_fwd_create(const TGFwdConfig* cfg, TGFwdWeightFn get, void* ctx) {
+    if (!cfg || !get) { set_err("null argument"); return NULL; }
+    TGFwdConfig c = *cfg;
+    if (!c.n_kv_heads) c.n_kv_heads = c.n_heads;
+    if (!c.n_layers || !c.d_model || !c.n_heads || !c.vocab_size || !c.max_seq_len) {
+        set_err("n_layers, d_model, n_heads, vocab_size and max_seq_len must be positive");
+        return NULL;
+    }
+    if (!c.head_dim) c.head_dim = c.d_model / c.n_heads;
+    if (c.n_kv_heads > c.n_heads || c.n_heads % c.n_kv_heads) {
+        set_err("n_heads %u is not a multiple of n_kv_heads %u", c.n_heads, c.n_kv_heads);
+        return NULL;
+    }
+    if (!tg_cuda_kv_attn_supported(0, c.head_dim)) {
+        set_err("head_dim %u has no fp32 attention kernel (32, 64 or 128)", c.head_dim);
+        return NULL;
+    }
+    if (c.d_model % 4 || !c.d_ff || c.d_ff % 4) {
+        set_err("d_model and d_ff must be positive multiples of 4");
+        return NULL;
+    }
+    if (c.n_experts > 16 || (c.n_experts && (!c.n_activated || c.n_activated > 8 ||
+                                             c.n_activated > c.n_experts))) {
+        set_err("MoE needs 1..16 experts and top-1..8 (got %u, %u)", c.n_experts, c.n_activated);
+        return NULL;
+    }
+    if (!(c.rope_theta > 0.f)) { set_err("rope_theta must be positive"); return NULL; }
+    if (!tg_gpu_backend_init() || !tg_cuda_kv_init()) {
+        set_err("no CUDA device: %s", tg_gpu_backend_reason());
+        return NULL;
+    }
+    if (!blas_ready()) return NULL;
+
+    TGFwdModel* m = (TGFwdModel*)calloc(1, sizeof(TGFwdModel));
+    if (!m) { set_err("host allocation failed"); return NULL; }
+    pthread_mutex_init(&m->mu, NULL);
+    m->c = c;
+    m->hd = c.head_dim;
+    m->nkv = c.n_kv_heads;
+    m->q_dim = c.n_heads * c.head_dim;
+    m->kv_dim = c.n_kv_heads * c.head_dim;
+    m->qkv_dim = m->q_dim + 2 * m->kv_dim;
+    m->max_slots = 16;
+    {
+        const char* e = getenv("TGAI_CUDA_KV_SLOTS");
+        if (e && e[0]) { int v = atoi(e); if (v >= 1 && v <= 64) m->max_slots = (uint32_t)v; }
+    }
+    m->slots = (Slot*)calloc(m->max_slots, sizeof(Slot));
+    m->L = (Layer*)calloc(c.n_layers, sizeof(Layer));
+    if (!m->slots || !m->L) { set_err("host allocation failed"); goto fail; }
+
+    {   /* embedding: rows beyond vocab_size are never read (tgai_engine.c:4397-4412) */
+        uint32_t shape[2] = {0, 0};
+        const float* e = get(ctx, "token_embedding.weight", shape);
+        if (!e) { set_err("missing weight token_embedding.weight"); goto fail; }
+        if (shape[1] != c.d_model || !shape[0]) {
+            set_err("token_embedding.weight has shape [%u, %u], expected [*, %u]", shape[0],
+                    shape[1], c.d_model);
+            goto fail;
+        }
+        m->rows = shape[0] < c.vocab_size ? shape[0] : c.vocab_size;
+        if (c.unk_id < 0 || (uint32_t)c.unk_id >= m->rows) {
+            set_err("unk_id %d is outside the %u embedding rows", c.unk_id, m->rows);
+            goto fail;
+        }
+        if (!(m->emb = upload(m, e, (uint64_t)m->rows * c.d_model))) goto fail;
+        const float* f = tensor(get, ctx, "final_norm.weight", c.d_model, 1, 1);
+        if (!f || !(m->fnorm = upload(m, f, c.d_model))) goto fail;
+    }
+    for (uint32_t l = 0; l < c.n_layers; l++)
+        if (!load_layer(m, l, get, ctx)) goto fail;
+    {   /* RoPE tables of every position, the engine's formula (no context extension) */
+        const uint64_t n = (uint64_t)c.max_seq_len * (c.head_dim / 2);
+        float* cs = (float*)malloc(n * sizeof(float));
+        float* sn = (float*)malloc(n * sizeof(float));
+        int ok = cs && sn &&
+                 tg_kv_rope_tables(c.rope_theta, c.head_dim, 0, c.max_seq_len, 0, c.max_seq_len,
+                                   cs, sn, NULL);
+        if (ok) ok = (m->cs = upload(m, cs, n)) && (m->sn = upload(m, sn, n));
+        else set_err("RoPE tables: %s", tg_kv_last_error());
+        free(cs);
+        free(sn);
+        if (!ok) goto fail;
+    }
+    return m;
+fail:
+    tg_fwd_destroy(m);
+    return NULL;
+}
+
+uint64_t tg_fwd_weight_bytes(const TGFwdModel* m) { return m ? m->wbytes : 0; }
+
+/* ---- slots ---------------------------------------------------------------- */
+static void slot_free_ws(Slot* s) {
+    float** f[] = {&s->x, &s->ln, &s->qkv, &s->q, &s->attn, &s->ab, &s->h, &s->router,
+                   &s->top_w, &s->y};
+    for (size_t i = 0; i < sizeof(f) / sizeof(f[0]); i++) { tg_cuda_kv_free(*f[i]); *f[i] = NULL; }
+    tg_cuda_kv_free(s->top_ids);
+    tg_cuda_kv_free(s->ids);
+    tg_cuda_kv_free(s->counts);
+    tg_cuda_kv_free(s->lists);
+    s->top_ids = s->ids = NULL;
+    s->counts = s->lists = NULL;
+    tgkv_fwd_host_free(s->h_ids);
+    s->h_ids = NULL;
+    s->cap = 0;
+}
+
+static void slot_release_mem(TGFwdModel* m, Slot* s) {
+    if (s->stream) tg_cuda_kv_sync(s->stream);
+    slot_free_ws(s);
+    if (s->kv) {
+        for (uint32_t l = 0; l < m->c.n_layers; l++) tg_kv_destroy(s->kv[l]);
+        free(s->kv);
+        s->kv = NULL;
+    }
+    tg_cuda_kv_free(s->logits);
+    s->logits = NULL;
+    tgkv_fwd_host_free(s->h_logits);
+    s->h_logits = NULL;
+    if (s->blas) g_blas.destroy(s->blas);
+    s->blas = NULL;
+    if (s->stream) tg_cuda_kv_stream_destroy(s->stream);
+    s->stream = NULL;
+    s->used = 0;
+    s->key = NULL;
+}
+
+/* Workspaces for `need` token rows (grown by doubling, never shrunk). */
+static int slot_reserve(TGFwdModel* m, Slot* s, uint32_t need) {
+    if (need <= s->cap) return 1;
+    uint32_t cap = s->cap ? s->cap : 16;
+    while (cap < need) cap *= 2;
+    if (s->stream) tg_cuda_kv_sync(s->stream);
+    slot_free_ws(s);
+    const uint64_t d = m->c.d_model, dff = m->c.d_ff, ne = m->c.n_experts, na = m->c.n_activated;
+    const uint64_t pairs = (uint64_t)cap * (ne ? na : 1);
+    s->x = (float*)tg_cuda_kv_malloc(cap * d * 4);
+    s->ln = (float*)tg_cuda_kv_malloc(cap * d * 4);
+    s->qkv = (float*)tg_cuda_kv_malloc((uint64_t)cap * m->qkv_dim * 4);
+    s->q = (float*)tg_cuda_kv_malloc((uint64_t)cap * m->q_dim * 4);
+    s->attn = (float*)tg_cuda_kv_malloc((uint64_t)cap * m->q_dim * 4);
+    s->h = (float*)tg_cuda_kv_malloc(pairs * dff * 4);
+    s->ids = (int32_t*)tg_cuda_kv_malloc((uint64_t)cap * 4);
+    s->h_ids = (int32_t*)tgkv_fwd_host_alloc((uint64_t)cap * 4);
+    int ok = s->x && s->ln && s->qkv && s->q && s->attn && s->h && s->ids && s->h_ids;
+    if (ne == 0) {
+        s->ab = (float*)tg_cuda_kv_malloc(cap * 2 * dff * 4);
+        ok = ok && s->ab;
+    } else {
+        s->router = (float*)tg_cuda_kv_malloc(cap * ne * 4);
+        s->top_w = (float*)tg_cuda_kv_malloc(pairs * 4);
+        s->top_ids = (int32_t*)tg_cuda_kv_malloc(pairs * 4);
+        s->y = (float*)tg_cuda_kv_malloc(pairs * d * 4);
+        s->counts = (uint32_t*)tg_cuda_kv_malloc(ne * 4);
+        s->lists = (uint32_t*)tg_cuda_kv_malloc(ne * pairs * 4);
+        ok = ok && s->router && s->top_w && s->top_ids && s->y && s->counts && s->lists;
+    }
+    if (!ok) {
+        slot_free_ws(s);
+        set_err("workspace for %u tokens: allocation failed", cap);
+        return 0;
+    }
+    s->cap = cap;
+    return 1;
+}
+
+static int slot_init(TGFwdModel* m, Slot* s) {
+    s->stream = tg_cuda_kv_stream_create();
+    if (!s->stream) { set_err("stream: %s", tg_cuda_kv_last_error()); return 0; }
+    if (g_blas.create(&s->blas) != CUBLAS_STATUS_SUCCESS) {
+        s->blas = NULL;
+        set_err("cublasCreate failed");
+        return 0;
+    }
+    if (g_blas.set_stream(s->blas, (cudaStream_t)s->stream) != CUBLAS_STATUS_SUCCESS) {
+        set_err("cublasSetStream failed");
+        return 0;
+    }
+    s->kv = (TGKvCache**)calloc(m->c.n_layers, sizeof(TGKvCache*));
+    if (!s->kv) { set_err("host allocation failed"); return 0; }
+    for (uint32_t l = 0; l < m->c.n_layers; l++) {
+        s->kv[l] = tg_kv_create_ex(m->c.max_seq_len, m->nkv, m->hd, TG_KV_F32);
+        if (!s->kv[l]) { set_err("KV cache of layer %u: %s", l, tg_kv_last_error()); return 0; }
+    }
+    s->logits = (float*)tg_cuda_kv_malloc((uint64_t)m->c.vocab_size * 4);
+    s->h_logits = (float*)tgkv_fwd_host_alloc((uint64_t)m->c.vocab_size * 4);
+    if (!s->logits || !s->h_logits) { set_err("logits buffers: allocation failed"); return 0; }
+    memset(s->h_logits, 0, (size_t)m->c.vocab_size * 4);
+    s->last_pos = -1;
+    s->kv_hi = 0;
+    return slot_reserve(m, s, 16);
+}
+
+static Slot* find_slot(const TGFwdModel* m, const void* key) {
+    for (uint32_t i = 0; i < m->max_slots; i++)
+        if (m->slots[i].used && m->slots[i].key == key) return &m->slots[i];
+    return NULL;
+}
+
+static Slot* slot_get(TGFwdModel* m, const void* key) {
+    pthread_mutex_lock(&m->mu);
+    Slot* s = find_slot(m, key);
+    if (!s) {
+        int had_room = 0;
+        for (uint32_t i = 0; i < m->max_slots; i++) {
+            if (m->slots[i].used) continue;
+            had_room = 1;
+            s = &m->slots[i];
+            memset(s, 0, sizeof(*s));
+            s->used = 1;
+            s->key = key;
+            s->id = (int)i;
+            if (slot_init(m, s)) {
+                m->live++;
+            } else {
+                slot_release_mem(m, s);         /* slot_init's message stands */
+                s = NULL;
+            }
+            break;
+        }
+        if (!s) {
+            if (!had_room) set_err("no free slot (%u live of %u)", m->live, m->max_slots);
+            m->rejects++;
+        }
+    }
+    pthread_mutex_unlock(&m->mu);
+    return s;
+}
+
+/* Zero the slot's KV and forget its positions. */
+static int slot_clear(TGFwdModel* m, Slot* s) {
+    for (uint32_t l = 0; l < m->c.n_layers; l++) {
+        if (!tg_cuda_kv_memset(tg_kv_device_handle(s->kv[l]), 0, (size_t)tg_kv_bytes(s->kv[l]),
+                               s->stream)) {
+            set_err("KV clear: %s", tg_cuda_kv_last_error());
+            return 0;
+        }
+        tg_kv_reset(s->kv[l]);
+    }
+    s->last_pos = -1;
+    s->kv_hi = 0;
+    return 1;
+}
+
+int tg_fwd_reset_slot(TGFwdModel* m, const void* key) {
+    if (!m) return 0;
+    pthread_mutex_lock(&m->mu);
+    Slot* s = find_slot(m, key);
+    int ok = s && slot_clear(m, s) && tg_cuda_kv_sync(s->stream);
+    pthread_mutex_unlock(&m->mu);
+    return ok;
+}
+
+int tg_fwd_free_slot(TGFwdModel* m, const void* key) {
+    if (!m) return 0;
+    pthread_mutex_lock(&m->mu);
+    Slot* s = find_slot(m, key);
+    if (s) {
+        slot_release_mem(m, s);
+        m->live--;
+    }
+    pthread_mutex_unlock(&m->mu);
+    return s != NULL;
+}
+
+void tg_fwd_reset_all(TGFwdModel* m) {
+    if (!m) return;
+    pthread_mutex_lock(&m->mu);
+    for (uint32_t i = 0; i < m->max_slots; i++)
+        if (m->slots[i].used && slot_clear(m, &m->slots[i])) tg_cuda_kv_sync(m->slots[i].stream);
+    pthread_mutex_unlock(&m->mu);
+}
+
+uint32_t tg_fwd_slot_count(const TGFwdModel* m) { return m ? m->live : 0; }
+
+int tg_fwd_slot_last_pos(const TGFwdModel* m, const void* key) {
+    if (!m) return -1;
+    pthread_mutex_lock((pthread_mutex_t*)&m->mu);
+    const Slot* s = find_slot(m, key);
+    const int r = s ? s->last_pos : -1;
+    pthread_mutex_unlock((pthread_mutex_t*)&m->mu);
+    return r;
+}
+
+/* Slot index of key, or -1; and the rejected-request count (the reference
+ * bridge's tg_gpu_kv_slot_of / _rejects). */
+HIDDEN int tgkv_fwd_slot_index(TGFwdModel* m, const void* key) {
+    if (!m) return -1;
+    pthread_mutex_lock(&m->mu);
+    const Slot* s = find_slot(m, key);
+    const int r = s ? s->id : -1;
+    pthread_mutex_unlock(&m->mu);
+    return r;
+}
+HIDDEN long long tgkv_fwd_rejects(const TGFwdModel* m) { return m ? m->rejects : 0; }
+HIDDEN uint32_t tgkv_fwd_max_slots(const TGFwdModel* m) { return m ? m->max_slots : 0; }
+
+/* ---- forward -------------------------------------------------------------- */
+#define CHECK_LAUNCH(expr)                                                      \
+    do {                                                                        \
+        const int _e = (expr);                                                  \
+        t_launches++;                                                           \
+        if (_e) { set_err("%s failed (CUDA error %d)", #expr, _e); return 0; }  \
+    } while (0)
+
+/* out[M][N] (row stride ldo) = x[M][K] (row stride ldx) . W[N][K]^T, or += */
+static int gemm(Slot* s, uint32_t M, uint32_t N, uint32_t K, const float* x, uint32_t ldx,
+                const float* w, float* out, uint32_t ldo, int accumulate) {
+    const float one = 1.f, zero = 0.f;
+    t_launches++;
+    const cublasStatus_t st = g_blas.sgemm(s->blas, CUBLAS_OP_T, CUBLAS_OP_N, (int)N, (int)M,
+                                           (int)K, &one, w, (int)K, x, (int)ldx,
+                                           accumulate ? &one : &zero, out, (int)ldo);
+    if (st != CUBLAS_STATUS_SUCCESS) {
+        set_err("cublasSgemm(%u x %u x %u) failed with status %d", M, N, K, (int)st);
+        return 0;
+    }
+    return 1;
+}
+
+static int run_layer(TGFwdModel* m, Slot* s, uint32_t l, uint32_t seq, uint32_t pos) {
+    const Layer* L = &m->L[l];
+    const TGFwdConfig* c = &m->c;
+    const uint32_t d = c->d_model, dff = c->d_ff, ne = c->n_experts, na = c->n_activated;
+    void* st = s->stream;
+    TGKvCache* kv = s->kv[l];
+
+    CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, s->x, L->ln1, seq, d, d, d, 1e-6f, st));
+    if (!gemm(s, seq, m->qkv_dim, d, s->ln, d, L->wqkv, s->qkv, m->qkv_dim, 0)) return 0;
+    if (L->bqkv) CHECK_LAUNCH(tgkv_fwd_bias(s->qkv, L->bqkv, seq, m->qkv_dim, st));
+    t_launches++;
+    if (!tg_cuda_kv_rope_append(TG_KV_F32, s->qkv, m->cs, m->sn, tg_kv_device_handle(kv), s->q,
+                                seq, c->n_heads, m->nkv, m->hd, pos, c->max_seq_len, st)) {
+        set_err("RoPE + append: %s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    tg_kv_advance(kv, seq);
+    if (!tg_kv_attention(kv, s->q, s->attn, c->n_heads, seq, st)) {
+        set_err("attention: %s", tg_kv_last_error());
+        return 0;
+    }
+    t_launches += tg_cuda_kv_attn_last_launches();
+    if (!gemm(s, seq, d, m->q_dim, s->attn, m->q_dim, L->wo, s->x, d, 1)) return 0;
+    CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, s->x, L->ln2, seq, d, d, d, 1e-6f, st));
+    if (ne == 0) {
+        if (!gemm(s, seq, 2 * dff, d, s->ln, d, L->w12, s->ab, 2 * dff, 0)) return 0;
+        CHECK_LAUNCH(tgkv_fwd_silu_mul(s->h, s->ab, seq, dff, 1, st));
+        return gemm(s, seq, d, dff, s->h, dff, L->w3, s->x, d, 1);
+    }
+    if (!gemm(s, seq, ne, d, s->ln, d, L->router, s->router, ne, 0)) return 0;
+    t_launches++;
+    if (!tg_cuda_kv_memset(s->counts, 0, (size_t)ne * 4, st)) {
+        set_err("memset: %s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    CHECK_LAUNCH(tgkv_fwd_route(s->router, L->qb, s->top_ids, s->top_w, s->counts, s->lists,
+                                seq, ne, na, st));
+    CHECK_LAUNCH(tgkv_fwd_expert_w12(L->w12, s->ln, s->h, s->counts, s->lists, seq, ne, na, d,
+                                     dff, st));
+    CHECK_LAUNCH(tgkv_fwd_expert_w3(L->w3, s->h, s->y, s->counts, s->lists, seq, ne, na, d, dff,
+                                    st));
+    CHECK_LAUNCH(tgkv_fwd_moe_combine(s->x, s->y, s->top_ids, s->top_w, seq, d, ne, na, st));
+    return 1;
+}
+
+static int run_forward(TGFwdModel* m, Slot* s, const int32_t* ids, uint32_t seq, uint32_t pos) {
+    const TGFwdConfig* c = &m->c;
+    const uint32_t d = c->d_model;
+    void* st = s->stream;
+    if (!slot_reserve(m, s, seq)) return 0;
+    /* a gap (positions the slot never wrote) clears it: cuda/tgai_cuda.cu:1703-1711 */
+    if (s->kv_hi > 0 && (int)pos > s->last_pos && !slot_clear(m, s)) return 0;
+    for (uint32_t l = 0; l < c->n_layers; l++) {   /* keep [0, pos): the LCP of the caller */
+        tg_kv_reset(s->kv[l]);
+        tg_kv_advance(s->kv[l], pos);
+    }
+    memcpy(s->h_ids, ids, (size_t)seq * 4);
+    t_launches++;
+    if (!tg_cuda_kv_h2d(s->ids, s->h_ids, (size_t)seq * 4, st)) {
+        set_err("ids upload: %s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    CHECK_LAUNCH(tgkv_fwd_embed(s->x, m->emb, s->ids, seq, d, m->rows, c->unk_id, st));
+    for (uint32_t l = 0; l < c->n_layers; l++)
+        if (!run_layer(m, s, l, seq, pos)) return 0;
+    /* final norm of the last row, then the tied-embedding LM head */
+    const float* xl = s->x + (uint64_t)(seq - 1) * d;
+    CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, xl, m->fnorm, 1, d, d, d, 1e-6f, st));
+    if (!gemm(s, 1, m->rows, d, s->ln, d, m->emb, s->logits, m->rows, 0)) return 0;
+    t_launches++;
+    if (!tg_cuda_kv_d2h(s->h_logits, s->logits, (size_t)m->rows * 4, st) || !tg_cuda_kv_sync(st)) {
+        set_err("forward: %s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    s->last_pos = (int)(pos + seq);
+    if (s->last_pos > s->kv_hi) s->kv_hi = s->last_pos;
+    return 1;
+}
+
+const float* tg_fwd_forward(TGFwdModel* m, const void* key, const int32_t* ids,
+                            uint32_t seq_len, uint32_t cache_pos) {
+    t_launches = 0;
+    if (!m || !ids || !seq_len) { set_err("null argument or empty sequence"); return NULL; }
+    if ((uint64_t)cache_pos + seq_len > m->c.max_seq_len) {
+        set_err("positions %u..%u exceed max_seq_len %u", cache_pos, cache_pos + seq_len - 1,
+                m->c.max_seq_len);
+        return NULL;
+    }
+    Slot* s = slot_get(m, key);
+    if (!s) return NULL;
+    if (!run_forward(m, s, ids, seq_len, cache_pos)) {
+        tg_cuda_kv_sync(s->stream);
+        return NULL;
+    }
+    return s->h_logits;
+}

@@ -3,8 +3,8 @@
 This mirrors how the reference's Python layer binds its engine
 (python/tgai_go/_engine.py:344-347 declares tg_kvcache_new/free/reset and
 tg_forward with ctypes): every entry point of include/tgai_kv_cache.h,
-include/tgai_backend.h, include/tgai_gpu_dispatch.h and
-include/tgai_cuda_bridge.h gets argtypes/restype here.  Loading fails loudly if
+include/tgai_backend.h, include/tgai_gpu_dispatch.h, include/tgai_cuda_bridge.h
+and include/tgai_engine_bridge.h gets argtypes/restype here.  Loading fails loudly if
 the library is missing -- there is no Python or CPU fallback.
 """
 import ctypes as C
@@ -45,6 +45,18 @@ class TGBackend(C.Structure):
                 ("map", vp),
                 ("rmsnorm", vp), ("silu_mul", vp), ("softmax", vp), ("rope", ROPE_FN),
                 ("mm_bf16", vp), ("attention", ATTN_FN), ("moe_router", vp), ("priv", vp)]
+
+
+class TGFwdConfig(C.Structure):
+    """TGFwdConfig of include/tgai_engine_bridge.h."""
+    _fields_ = [("n_layers", u32), ("d_model", u32), ("n_heads", u32), ("n_kv_heads", u32),
+                ("head_dim", u32), ("d_ff", u32), ("vocab_size", u32), ("max_seq_len", u32),
+                ("n_experts", u32), ("n_activated", u32), ("rope_theta", C.c_float),
+                ("unk_id", C.c_int32)]
+
+
+# TGFwdWeightFn: const float* (*)(void* ctx, const char* name, uint32_t shape[2])
+WEIGHT_FN = C.CFUNCTYPE(vp, vp, cp, PU32)
 
 
 def current_backend(lib):
@@ -158,6 +170,37 @@ PROTOS = {
     "tg_cuda_kv_attention": (i32, [vp, vp]),
     "tg_cuda_kv_rope_append": (i32, [i32, vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32,
                                      vp]),
+    # tgai_engine_bridge.h -- the engine's CUDA seam (cuda/tgai_cuda_bridge.h:31-60)
+    "tg_engine_cuda_init": (i32, [vp]),
+    "tg_engine_cuda_forward": (i32, [vp, C.POINTER(C.c_int32), i32, vp, i32,
+                                     C.POINTER(PF)]),
+    "tg_engine_cuda_reset": (None, []),
+    "tg_engine_cuda_reset_slot": (None, [vp]),
+    "tg_engine_cuda_free_slot": (None, [vp]),
+    "tg_engine_cuda_shutdown": (None, []),
+    "tg_engine_cuda_ready": (i32, []),
+    "tg_engine_cuda_reason": (cp, []),
+    "tg_engine_cuda_calls": (C.c_longlong, []),
+    "tg_engine_cuda_fallbacks": (C.c_longlong, []),
+    "tg_gpu_kv_slot_of": (i32, [vp]),
+    "tg_gpu_kv_slot_seq": (i32, [vp]),
+    "tg_gpu_kv_slot_live": (i32, []),
+    "tg_gpu_kv_slot_max": (i32, []),
+    "tg_gpu_kv_slot_rejects": (C.c_longlong, []),
+    "tg_gpu_cuda_calls": (C.c_longlong, []),
+    "tg_gpu_cuda_fallbacks": (C.c_longlong, []),
+    # tgai_engine_bridge.h -- neutral whole-forward API
+    "tg_fwd_create": (vp, [C.POINTER(TGFwdConfig), WEIGHT_FN, vp]),
+    "tg_fwd_destroy": (None, [vp]),
+    "tg_fwd_forward": (PF, [vp, vp, C.POINTER(C.c_int32), u32, u32]),
+    "tg_fwd_reset_slot": (i32, [vp, vp]),
+    "tg_fwd_free_slot": (i32, [vp, vp]),
+    "tg_fwd_reset_all": (None, [vp]),
+    "tg_fwd_slot_count": (u32, [vp]),
+    "tg_fwd_slot_last_pos": (i32, [vp, vp]),
+    "tg_fwd_weight_bytes": (u64, [vp]),
+    "tg_fwd_last_launches": (u32, []),
+    "tg_fwd_last_error": (cp, []),
 }
 
 _lib = None
@@ -181,6 +224,54 @@ def load(path=LIB_PATH):
 
 class KvError(RuntimeError):
     pass
+
+
+class Forward:
+    """A whole-model forward (tg_fwd_*) over fp32 host weights.
+
+    weights: dict name -> float32 array (the engine's tensor names; Linear
+    weights [out, in]).  forward(key, ids, pos) returns the logits row as a
+    numpy copy; key is any hashable naming the sequence.
+    """
+
+    def __init__(self, lib, cfg, weights):
+        import numpy as np
+        self.lib = lib
+        self._w = {k: np.ascontiguousarray(v, np.float32) for k, v in weights.items()}
+        self._names = {}
+
+        def get(ctx, name, shape):
+            a = self._w.get(name.decode())
+            if a is None:
+                return None
+            shape[0] = a.shape[0]
+            shape[1] = int(a.size // a.shape[0]) if a.ndim > 1 else 1
+            return a.ctypes.data
+
+        self._cb = WEIGHT_FN(get)
+        self.cfg = cfg
+        self.m = lib.tg_fwd_create(C.byref(cfg), self._cb, None)
+        if not self.m:
+            raise KvError(f"tg_fwd_create: {lib.tg_fwd_last_error().decode(errors='replace')}")
+        self._w = None                      # read during create only
+        self._keys = {}
+
+    def key(self, k):
+        return self._keys.setdefault(k, len(self._keys) + 1)
+
+    def forward(self, k, ids, pos):
+        import numpy as np
+        ids = np.ascontiguousarray(ids, np.int32)
+        arr = ids.ctypes.data_as(C.POINTER(C.c_int32))
+        p = self.lib.tg_fwd_forward(self.m, C.c_void_p(self.key(k)), arr, len(ids), pos)
+        if not p:
+            raise KvError(f"tg_fwd_forward: {self.lib.tg_fwd_last_error().decode(errors='replace')}")
+        return np.ctypeslib.as_array(p, shape=(self.cfg.vocab_size,)).copy()
+
+    def close(self):
+        if self.m:
+            self.lib.tg_fwd_destroy(self.m)
+            self.m = None
 
 
 def check(ok, lib=None, what="tg_kv"):
