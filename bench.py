@@ -527,13 +527,249 @@ def run_cfg3(args):
     print(json.dumps(line), flush=True)
 
 
+# ---- whole-model decode through the engine seam's forward (tg_fwd_*) ----
+# A synthetic model shaped like the reference's headline whole-model number
+# (README.md:279: "V2.7 3B BF16, 28-layer MoE", 11.2 tok/s on 8 CPU threads):
+# 28 layers, d_model 1536, 12 query / 4 KV heads of 128, 8 experts top-2 with
+# d_ff 2560 and a router bias, vocab 32000 (2.9 B parameters, fp32 here).
+FWD = dict(arch=0, n_layers=28, d_model=1536, n_heads=12, n_kv_heads=4, d_ff=2560, vocab=32000,
+           max_seq=4096, n_experts=8, n_activated=2, rope_theta=10000, unk=1, qkv_bias=False,
+           qb_bias=True)
+FWD_METRIC = "whole-model decode tokens/s (tg_engine_cuda_forward / tg_fwd_forward)"
+
+
+def fwd_shapes(cfg):
+    """name -> (rows, cols) of every tensor of the model."""
+    d, dff, ne = cfg["d_model"], cfg["d_ff"], cfg["n_experts"]
+    hd = d // cfg["n_heads"]
+    qd, kvd = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+    sh = {"token_embedding.weight": (cfg["vocab"], d), "final_norm.weight": (d, 1)}
+    for l in range(cfg["n_layers"]):
+        p = f"blocks.{l}."
+        sh.update({p + "ln1.weight": (d, 1), p + "ln2.weight": (d, 1),
+                   p + "attn.q_proj.weight": (qd, d), p + "attn.k_proj.weight": (kvd, d),
+                   p + "attn.v_proj.weight": (kvd, d), p + "attn.out_proj.weight": (d, qd),
+                   p + "moe.router.weight": (ne, d), p + "moe._qb_bias": (ne, 1)})
+        for e in range(ne):
+            sh[p + f"moe.experts.{e}.w1.weight"] = (dff, d)
+            sh[p + f"moe.experts.{e}.w2.weight"] = (dff, d)
+            sh[p + f"moe.experts.{e}.w3.weight"] = (d, dff)
+    return sh
+
+
+def fwd_tensor(seed, name, rows, cols):
+    """Seeded uniform values of unit variance / sqrt(fan-in); norms near 1."""
+    import zlib
+    rng = np.random.default_rng([seed, zlib.crc32(name.encode())])
+    a = rng.random((rows, cols) if cols > 1 else rows, dtype=np.float32) - np.float32(0.5)
+    if name.endswith("norm.weight") or ".ln" in name:
+        return np.float32(1.0) + np.float32(0.2) * a
+    if name == "token_embedding.weight":
+        return np.float32(np.sqrt(12.0)) * a
+    return a * np.float32(np.sqrt(12.0 / max(cols, 1)))
+
+
+def fwd_bytes_per_token(cfg, ctx):
+    """Algorithmic HBM bytes of one decode token (fp32): every weight the token
+    touches once (attention, router, the top-k experts, the LM head), the K/V
+    of ctx positions read once per KV head and the new row written."""
+    d, dff, ne, na = cfg["d_model"], cfg["d_ff"], cfg["n_experts"], cfg["n_activated"]
+    hd = d // cfg["n_heads"]
+    qd, kvd = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+    per_layer = (2 * d + (qd + 2 * kvd) * d + d * qd + ne * d + ne + na * 3 * dff * d
+                 + 2 * ctx * kvd + 2 * kvd)
+    return 4.0 * (cfg["n_layers"] * per_layer + cfg["vocab"] * d + 2 * d)
+
+
+def fwd_cpu_sample(cfg, seed, prefill, steps, threads):
+    """The reference engine's own CPU forward (oracle/_ref build of
+    src/tgai_engine.c) on the same model cut to 2 and 4 layers: decode
+    seconds per token at each, extrapolated linearly in layers.  None when
+    the reference build is absent."""
+    so = os.path.join(ROOT, "oracle", "_ref", "libtgai_engine_ref.so")
+    if not os.path.exists(so):
+        return None
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import tempfile
+    import fwd_model as FM
+    eng = C.CDLL(so, mode=os.RTLD_LAZY)
+    eng.tg_load.restype = C.c_void_p
+    eng.tg_load.argtypes = [C.c_char_p, C.c_int, C.POINTER(C.c_int)]
+    eng.tg_kvcache_new.restype = C.c_void_p
+    eng.tg_kvcache_new.argtypes = [C.c_void_p, C.c_int]
+    eng.tg_kvcache_free.argtypes = [C.c_void_p]
+    eng.tg_forward.restype = C.POINTER(C.c_float)
+    eng.tg_forward.argtypes = [C.c_void_p, C.POINTER(C.c_int32), C.c_int, C.c_void_p, C.c_int]
+    eng.tg_free.argtypes = [C.c_void_p]
+    eng.tg_set_nthreads.argtypes = [C.c_int]
+    eng.tg_set_nthreads(threads)
+    ids = np.random.default_rng(seed).integers(0, cfg["vocab"], prefill + steps).astype(np.int32)
+    per = {}
+    for nl in (2, 4):
+        c = dict(cfg, n_layers=nl)
+        w = {n: fwd_tensor(seed, n, *rc) for n, rc in fwd_shapes(c).items()}
+        with tempfile.TemporaryDirectory() as td:
+            path = os.path.join(td, "m.TG")
+            FM.write_tg(path, c, w)
+            del w
+            err = C.c_int(0)
+            m = eng.tg_load(path.encode(), 1, C.byref(err))
+            if not m:
+                return None
+            kv = eng.tg_kvcache_new(m, prefill + steps + 1)
+            arr = (C.c_int32 * prefill)(*ids[:prefill].tolist())
+            eng.tg_forward(m, arr, prefill, kv, 0)
+            t0 = time.perf_counter()
+            for i in range(steps):
+                one = (C.c_int32 * 1)(int(ids[prefill + i]))
+                eng.tg_forward(m, one, 1, kv, prefill + i)
+            per[nl] = (time.perf_counter() - t0) / steps
+            eng.tg_kvcache_free(kv)
+            eng.tg_free(m)
+    slope = (per[4] - per[2]) / 2.0
+    t_tok = per[2] + slope * (cfg["n_layers"] - 2)
+    desc = (f"reference engine tg_forward (oracle/_ref), fp32, {threads} threads: {steps} decode "
+            f"tokens after a {prefill}-token prefill on the model cut to 2 and 4 layers "
+            f"({per[2] * 1e3:.1f} / {per[4] * 1e3:.1f} ms per token), extrapolated linearly to "
+            f"{cfg['n_layers']} layers")
+    return 1.0 / t_tok, desc
+
+
+def run_fwd(args):
+    """One step = one decode token of one sequence through tg_fwd_forward
+    (host token id in, host logits out, synchronous as a sampling loop
+    needs), after a 512-token prefill."""
+    world, rank, _ = dist_setup(args)
+    cfg = dict(FWD)
+    prefill = 512
+    threads = os.cpu_count() or 1
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        r = fwd_cpu_sample(cfg, args.seed, prefill, max(args.steps, 3), threads)
+        if r is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref engine not built"}))
+            return
+        v, desc = r
+        print(json.dumps({
+            "impl": "reference", "metric": FWD_METRIC, "value": v, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "fwd", "model": "V2.7-shaped 28-layer MoE (synthetic)"},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads,
+                             "kind": "reference", "sample": desc},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    import tgkv
+    lib = tgkv.load()
+    if world > 1:
+        tgkv.check(lib.tg_cuda_kv_set_device(int(os.environ.get("LOCAL_RANK", "0"))), lib)
+    tgkv.check(lib.tg_be_select(b"cuda"), lib, "tg_be_select")
+    shapes = fwd_shapes(cfg)
+    held = {}
+
+    def get(ctx, name, shape):
+        # tg_fwd_create reads a layer's tensors while it assembles that layer:
+        # every array of the current layer stays alive until the next begins
+        n = name.decode()
+        rc = shapes.get(n)
+        if rc is None:
+            return None
+        layer = n.split(".")[1] if n.startswith("blocks.") else None
+        if layer is not None and held.get("_layer") != layer:
+            held.clear()
+            held["_layer"] = layer
+        a = held[n] = fwd_tensor(args.seed, n, *rc)
+        shape[0], shape[1] = rc
+        return a.ctypes.data
+
+    cb = tgkv.WEIGHT_FN(get)
+    fc = tgkv.TGFwdConfig(n_layers=cfg["n_layers"], d_model=cfg["d_model"],
+                          n_heads=cfg["n_heads"], n_kv_heads=cfg["n_kv_heads"], d_ff=cfg["d_ff"],
+                          vocab_size=cfg["vocab"], max_seq_len=cfg["max_seq"],
+                          n_experts=cfg["n_experts"], n_activated=cfg["n_activated"],
+                          rope_theta=cfg["rope_theta"], unk_id=cfg["unk"])
+    m = lib.tg_fwd_create(C.byref(fc), cb, None)
+    held.clear()
+    if not m:
+        raise SystemExit("tg_fwd_create: " + lib.tg_fwd_last_error().decode())
+    ids = np.random.default_rng([args.seed, rank]).integers(
+        0, cfg["vocab"], prefill + args.warmup + args.steps).astype(np.int32)
+    key = C.c_void_p(1)
+
+    def fwd(tok, pos):
+        p = lib.tg_fwd_forward(m, key, tok.ctypes.data_as(C.POINTER(C.c_int32)), len(tok), pos)
+        if not p:
+            raise SystemExit("tg_fwd_forward: " + lib.tg_fwd_last_error().decode())
+        return p
+
+    fwd(ids[:prefill], 0)
+    for i in range(args.warmup):
+        fwd(ids[prefill + i:prefill + i + 1], prefill + i)
+    launches = lib.tg_fwd_last_launches()
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo")
+        dist.barrier()
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    clocks.start()
+    t0 = time.perf_counter()
+    pos0 = prefill + args.warmup
+    for i in range(args.steps):
+        fwd(ids[pos0 + i:pos0 + i + 1], pos0 + i)
+    dt = time.perf_counter() - t0
+    clk = clocks.stop()
+    if world > 1:
+        t = np.array([dt])
+        import torch
+        tt = torch.tensor(t)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        dt = float(tt[0])
+        dist.destroy_process_group()
+    lib.tg_fwd_destroy(m)
+    if rank != 0:
+        return
+    tok_s = world * args.steps / dt
+    ctx = pos0 + args.steps / 2.0
+    bpt = fwd_bytes_per_token(cfg, ctx)
+    peak, src = measured_peak()
+    achieved = bpt * args.steps / dt / 1e9
+    line = {"metric": FWD_METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dt / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "fwd", "model": "V2.7-shaped 28-layer MoE (synthetic)",
+                       "layers": cfg["n_layers"], "d_model": cfg["d_model"],
+                       "heads": f"{cfg['n_heads']}q/{cfg['n_kv_heads']}kv x 128",
+                       "experts": f"{cfg['n_experts']} top-{cfg['n_activated']}, d_ff {cfg['d_ff']}",
+                       "vocab": cfg["vocab"], "context": f"{pos0}..{pos0 + args.steps}",
+                       "parallelism": f"replicas x{world}",
+                       "l2": "weights read per token (3.4 GB) >> 126 MB L2"},
+            "roofline": {"bound": "hbm", "kernel": "whole decode step", "achieved": achieved,
+                         "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": src, "traffic": None,
+                         "bytes_per_token": bpt},
+            "gpu_launches": launches * args.steps,
+            "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 4 * cfg["vocab"]},
+            "clocks": clk}
+    if not args.no_cpu:
+        r = fwd_cpu_sample(cfg, args.seed, prefill, 3, threads)
+        if r:
+            line["cpu_baseline"] = {"value": r[0], "unit": "tokens/s", "cores": threads,
+                                    "kind": "reference", "sample": r[1]}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["fwd"], default="cfg4")
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--seqs", type=int, default=0,
                     help="sequences per GPU (default: the workload's); for small profiling cases")
@@ -552,7 +788,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if args.impl == "reference":
+    if args.workload == "fwd":
+        run_fwd(args)
+    elif args.impl == "reference":
         run_reference(args)
     elif args.workload == "cfg3":
         run_cfg3(args)
