@@ -14,6 +14,7 @@
 // multiply-add of the expert outputs (:4304).
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "tgkv_forward.h"
 
@@ -33,6 +34,21 @@ __device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
 }
 
 __device__ __forceinline__ float silu_mul(float a, float b) { return (a / (1.0f + expf(-a))) * b; }
+
+// Programmatic dependent launch: the decode kernels are launched so that they
+// may start while their predecessor on the stream finishes.  Before
+// pdl_wait() they touch only weights (constant during a forward), which they
+// prefetch into L2; pdl_wait() returns once the predecessor has completed and
+// its writes are visible (at once for a launch without the attribute).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// One warp prefetches a weight row of n floats into L2, one 128-byte line per lane step.
+__device__ __forceinline__ void prefetch_row(const float* w, uint32_t n) {
+    for (uint32_t i = (threadIdx.x & 31) * 32; i < n; i += 32 * 32)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(w + i));
+}
 
 __global__ void __launch_bounds__(256) embed_kernel(float* x, const float* emb, const int32_t* ids,
                                                    uint32_t d, uint32_t rows, int32_t unk) {
@@ -154,10 +170,11 @@ __global__ void __launch_bounds__(256) expert_kernel(const float* __restrict__ w
         float acc_a[kPairs], acc_b[kPairs];
 #pragma unroll
         for (int u = 0; u < kPairs; ++u) acc_a[u] = acc_b[u] = 0.f;
+#pragma unroll 4
         for (uint32_t i = lane * 4; i < k_dim; i += 128) {
-            const float4 a4 = *reinterpret_cast<const float4*>(wa + i);
+            const float4 a4 = __ldg(reinterpret_cast<const float4*>(wa + i));
             float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (kW12) b4 = *reinterpret_cast<const float4*>(wb + i);
+            if (kW12) b4 = __ldg(reinterpret_cast<const float4*>(wb + i));
 #pragma unroll
             for (int u = 0; u < kPairs; ++u) {
                 const float4 x4 = *reinterpret_cast<const float4*>(src[u] + i);
@@ -195,6 +212,241 @@ __global__ void __launch_bounds__(256) combine_kernel(float* x, const float* y,
         }
         x[(uint64_t)t * d + i] += ot;
     }
+}
+
+// ---------------------------------------------------------------- decode
+// Kernels for steps of at most kDecRows tokens (decode).  Each CTA stages the
+// token rows (RMS-normalised when a norm weight is given) in shared memory
+// and every warp streams whole weight rows with 16-byte loads, so a weight
+// byte is read once per step and the norm, bias, residual and SwiGLU ride in
+// the same launch.  Several warps per SM keep many loads in flight: the step
+// is bound by how fast the weights stream from HBM.
+constexpr int kDecRows = 4;
+
+// Rows [0, R) of x (row stride ldx, K columns) into sx [R][K]; with g, each
+// row becomes x * (1/sqrt(mean(x^2) + eps)) * g.  Ends with __syncthreads.
+__device__ __forceinline__ void stage_rows(float* sx, float* s_scale, const float* x,
+                                           uint64_t ldx, uint32_t R, uint32_t K,
+                                           const float* g, float eps) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (uint32_t r = 0; r < R; ++r)
+        for (uint32_t i = threadIdx.x * 4; i < K; i += blockDim.x * 4)
+            *reinterpret_cast<float4*>(sx + r * K + i) =
+                *reinterpret_cast<const float4*>(x + r * ldx + i);
+    __syncthreads();
+    if (!g) return;
+    if (warp < R) {
+        float ss = 0.f;
+        for (uint32_t i = lane; i < K; i += 32) ss = fmaf(sx[warp * K + i], sx[warp * K + i], ss);
+        ss = warp_sum(ss);
+        if (lane == 0) s_scale[warp] = 1.0f / sqrtf(ss / (float)K + eps);
+    }
+    __syncthreads();
+    for (uint32_t r = 0; r < R; ++r) {
+        const float sc = s_scale[r];
+        for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) sx[r * K + i] = sx[r * K + i] * sc * g[i];
+    }
+    __syncthreads();
+}
+
+// acc[r] = W[n] . sx[r] for the rows of this warp's output n (all lanes hold
+// the sums on return).  Eight 16-byte weight loads per lane are issued before
+// their products are formed.
+__device__ __forceinline__ void row_dots(const float* __restrict__ w, const float* sx, uint32_t R,
+                                         uint32_t K, float* acc) {
+    const uint32_t lane = threadIdx.x & 31;
+#pragma unroll
+    for (int r = 0; r < kDecRows; ++r) acc[r] = 0.f;
+    constexpr int kU = 8;
+    uint32_t i = lane * 4;
+    for (; i + (kU - 1) * 128 < K; i += kU * 128) {
+        float4 a4[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) a4[u] = __ldg(reinterpret_cast<const float4*>(w + i + u * 128));
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+#pragma unroll
+            for (int r = 0; r < kDecRows; ++r)
+                if ((uint32_t)r < R)
+                    acc[r] = dot4(a4[u], *reinterpret_cast<const float4*>(sx + r * K + i + u * 128),
+                                  acc[r]);
+    }
+    for (; i < K; i += 128) {
+        const float4 a4 = __ldg(reinterpret_cast<const float4*>(w + i));
+#pragma unroll
+        for (int r = 0; r < kDecRows; ++r)
+            if ((uint32_t)r < R) acc[r] = dot4(a4, *reinterpret_cast<const float4*>(sx + r * K + i), acc[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < kDecRows; ++r) acc[r] = warp_sum(acc[r]);
+}
+
+enum { kStore = 0, kAdd = 1, kSwiglu = 2 };
+
+template <int MODE>
+__global__ void __launch_bounds__(256) dec_gemv_kernel(const float* __restrict__ w, const float* x,
+                                                       uint64_t ldx, const float* g,
+                                                       const float* bias, float* out,
+                                                       uint64_t ldo, uint32_t R, uint32_t N,
+                                                       uint32_t K, int clamp) {
+    extern __shared__ __align__(16) float dsm[];
+    float* sx = dsm + kDecRows;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (uint32_t n = blockIdx.x * 8 + warp; n < N; n += gridDim.x * 8) {
+        prefetch_row(w + (uint64_t)n * K, K);
+        if (MODE == kSwiglu) prefetch_row(w + (uint64_t)(N + n) * K, K);
+    }
+    pdl_wait();
+    pdl_trigger();
+    stage_rows(sx, dsm, x, ldx, R, K, g, 1e-6f);
+    for (uint32_t n = blockIdx.x * 8 + warp; n < N; n += gridDim.x * 8) {
+        float a[kDecRows], b[kDecRows] = {};
+        row_dots(w + (uint64_t)n * K, sx, R, K, a);
+        if (MODE == kSwiglu) row_dots(w + (uint64_t)(N + n) * K, sx, R, K, b);
+        if (lane < R) {                      // lane r writes row r's output
+            float v = a[0], vb = b[0];
+#pragma unroll
+            for (int r = 1; r < kDecRows; ++r)
+                if ((uint32_t)r == lane) { v = a[r]; vb = b[r]; }
+            float* o = out + lane * ldo + n;
+            if (MODE == kStore) {
+                *o = bias ? v + bias[n] : v;
+            } else if (MODE == kAdd) {
+                *o += v;
+            } else {
+                if (clamp) v = fminf(fmaxf(v, -88.0f), 88.0f);
+                *o = silu_mul(v, vb);
+            }
+        }
+    }
+}
+
+// Expert W3, the k-ordered weighted sum and the residual of a decode step:
+// x[r][i] += sum_k top_w[r][k] * (W3[e_k][i] . h[r * na + k]).  One warp per
+// row i; the dot products of two k at a time share one load loop so that 16
+// weight loads per lane are in flight.
+__global__ void __launch_bounds__(256) dec_w3_combine_kernel(const float* __restrict__ w3,
+                                                             const float* __restrict__ h,
+                                                             const int32_t* top_ids,
+                                                             const float* top_w, float* x,
+                                                             uint32_t R, uint32_t d, uint32_t dff,
+                                                             uint32_t ne, uint32_t na) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t i = blockIdx.x * 8 + warp;
+    pdl_wait();
+    pdl_trigger();
+    if (i >= d) return;
+    for (uint32_t r = 0; r < R; ++r) {
+        float ot = 0.f;
+        for (uint32_t k = 0; k < na; k += 2) {
+            const int e0 = top_ids[r * na + k];
+            const int e1 = k + 1 < na ? top_ids[r * na + k + 1] : -1;
+            const bool v0 = e0 >= 0 && (uint32_t)e0 < ne, v1 = e1 >= 0 && (uint32_t)e1 < ne;
+            const float* w0 = w3 + ((uint64_t)(v0 ? e0 : 0) * d + i) * dff;
+            const float* w1 = w3 + ((uint64_t)(v1 ? e1 : 0) * d + i) * dff;
+            const float* h0 = h + (uint64_t)(r * na + k) * dff;
+            const float* h1 = h0 + dff;
+            float a0 = 0.f, a1 = 0.f;
+            constexpr int kU = 8;
+            uint32_t j = lane * 4;
+            for (; j + (kU - 1) * 128 < dff; j += kU * 128) {
+                float4 p0[kU], p1[kU];
+#pragma unroll
+                for (int u = 0; u < kU; ++u) {
+                    p0[u] = v0 ? __ldg(reinterpret_cast<const float4*>(w0 + j + u * 128))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                    p1[u] = v1 ? __ldg(reinterpret_cast<const float4*>(w1 + j + u * 128))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < kU; ++u) {
+                    a0 = dot4(p0[u], *reinterpret_cast<const float4*>(h0 + j + u * 128), a0);
+                    if (v1) a1 = dot4(p1[u], *reinterpret_cast<const float4*>(h1 + j + u * 128), a1);
+                }
+            }
+            for (; j < dff; j += 128) {
+                if (v0) a0 = dot4(__ldg(reinterpret_cast<const float4*>(w0 + j)),
+                                  *reinterpret_cast<const float4*>(h0 + j), a0);
+                if (v1) a1 = dot4(__ldg(reinterpret_cast<const float4*>(w1 + j)),
+                                  *reinterpret_cast<const float4*>(h1 + j), a1);
+            }
+            a0 = warp_sum(a0);
+            a1 = warp_sum(a1);
+            if (v0) ot = fmaf(top_w[r * na + k], a0, ot);
+            if (v1) ot = fmaf(top_w[r * na + k + 1], a1, ot);
+        }
+        if (lane == 0) x[(uint64_t)r * d + i] += ot;
+    }
+}
+
+// MoE front and expert W1/W2 + SiLU of a decode step in one launch: grid row
+// p = (token r, choice k).  Every CTA normalises token r's row, computes its
+// router logits (+ bias) and the engine's top-k and softmax -- the same
+// arithmetic in every CTA, so all agree -- then streams W1/W2 rows of its
+// expert e_k: h[p][j] = silu(W1[e][j] . ln) * (W2[e][j] . ln), one warp per j.
+// The CTAs of column 0 publish top_ids / top_w for the W3 launch.
+__global__ void __launch_bounds__(256) dec_moe_w12_kernel(const float* x, const float* g,
+                                                          const float* __restrict__ router,
+                                                          const float* bias,
+                                                          const float* __restrict__ w12,
+                                                          int32_t* top_ids, float* top_w, float* h,
+                                                          uint32_t d, uint32_t dff, uint32_t ne,
+                                                          uint32_t na) {
+    extern __shared__ __align__(16) float dsm[];
+    __shared__ float slog[16];
+    __shared__ int s_ids[8];
+    __shared__ float s_w[8];
+    const uint32_t p = blockIdx.y, r = p / na, kk = p % na;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (uint32_t e = warp; e < ne; e += 8) prefetch_row(router + (uint64_t)e * d, d);
+    pdl_wait();
+    pdl_trigger();
+    float* sx = dsm + kDecRows;
+    stage_rows(sx, dsm, x + (uint64_t)r * d, d, 1, d, g, 1e-6f);
+    for (uint32_t e = warp; e < ne; e += 8) {
+        float a[kDecRows];
+        row_dots(router + (uint64_t)e * d, sx, 1, d, a);
+        if (lane == 0) slog[e] = bias ? a[0] + bias[e] : a[0];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int ids[8];
+        float vals[8];
+        for (uint32_t k = 0; k < na; ++k) {
+            int best = -1;
+            float best_v = -1e30f;
+            for (uint32_t e = 0; e < ne; ++e) {
+                bool used = false;
+                for (uint32_t q = 0; q < k; ++q) used |= ids[q] == (int)e;
+                if (used) continue;
+                if (slog[e] > best_v) { best_v = slog[e]; best = (int)e; }
+            }
+            ids[k] = best;
+            vals[k] = best_v;
+        }
+        float mx = vals[0];
+        for (uint32_t k = 1; k < na; ++k) if (vals[k] > mx) mx = vals[k];
+        float ss = 0.f;
+        for (uint32_t k = 0; k < na; ++k) { vals[k] = expf(vals[k] - mx); ss += vals[k]; }
+        for (uint32_t k = 0; k < na; ++k) {
+            s_ids[k] = ids[k];
+            s_w[k] = vals[k] / ss;
+        }
+        if (blockIdx.x == 0 && kk == 0)
+            for (uint32_t k = 0; k < na; ++k) {
+                top_ids[r * na + k] = s_ids[k];
+                top_w[r * na + k] = s_w[k];
+            }
+    }
+    __syncthreads();
+    const int e = s_ids[kk];
+    const uint32_t j = blockIdx.x * 8 + warp;
+    if (e < 0 || (uint32_t)e >= ne || j >= dff) return;
+    const float* wa = w12 + ((uint64_t)e * 2 * dff + j) * d;
+    float a[kDecRows], b[kDecRows];
+    row_dots(wa, sx, 1, d, a);
+    row_dots(wa + (uint64_t)dff * d, sx, 1, d, b);
+    if (lane == 0) h[(uint64_t)p * dff + j] = silu_mul(a[0], b[0]);
 }
 
 inline uint32_t blocks_for(uint64_t n, uint32_t per) { return (uint32_t)((n + per - 1) / per); }
@@ -267,6 +519,89 @@ extern "C" int tgkv_fwd_moe_combine(float* x, const float* y, const int32_t* top
                                     uint32_t na, void* stream) {
     combine_kernel<<<seq, 256, 0, (cudaStream_t)stream>>>(x, y, top_ids, top_w, d, ne, na);
     return (int)cudaGetLastError();
+}
+
+
+// ---- decode launchers
+static size_t dec_smem(uint32_t R, uint32_t K) { return (size_t)(kDecRows + kDecRows * 16 + R * K) * 4; }
+
+static bool pdl_on() {
+    static const bool on = [] {
+        const char* e = getenv("TGKV_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// Launch as a programmatic dependent of the previous work on the stream.
+template <typename... KArgs, typename... Args>
+static int launch_pdl(void (*k)(KArgs...), dim3 grid, size_t smem, void* stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_on() ? 1 : 0;
+    return (int)cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
+template <typename F>
+static int set_smem(F* f, size_t bytes) {
+    if (bytes <= 48 * 1024) return 0;
+    return (int)cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+extern "C" uint32_t tgkv_fwd_decode_rows(void) { return kDecRows; }
+
+extern "C" int tgkv_fwd_dec_gemv(int mode, const float* w, const float* x, uint64_t ldx,
+                                 const float* g, const float* bias, float* out, uint64_t ldo,
+                                 uint32_t R, uint32_t N, uint32_t K, int clamp, void* stream) {
+    if (R == 0 || R > kDecRows || K % 4 || ldx % 4) return (int)cudaErrorInvalidValue;
+    const size_t sm = dec_smem(R, K);
+    if (sm > 200 * 1024) return (int)cudaErrorInvalidValue;
+    const dim3 grid(blocks_for(N, 8));
+    int e;
+    switch (mode) {
+    case kStore:
+        if ((e = set_smem(dec_gemv_kernel<kStore>, sm))) return e;
+        return launch_pdl(dec_gemv_kernel<kStore>, grid, sm, stream, w, x, ldx, g, bias, out, ldo,
+                          R, N, K, clamp);
+    case kAdd:
+        if ((e = set_smem(dec_gemv_kernel<kAdd>, sm))) return e;
+        return launch_pdl(dec_gemv_kernel<kAdd>, grid, sm, stream, w, x, ldx, g, bias, out, ldo,
+                          R, N, K, clamp);
+    case kSwiglu:
+        if ((e = set_smem(dec_gemv_kernel<kSwiglu>, sm))) return e;
+        return launch_pdl(dec_gemv_kernel<kSwiglu>, grid, sm, stream, w, x, ldx, g, bias, out,
+                          ldo, R, N, K, clamp);
+    default:
+        return (int)cudaErrorInvalidValue;
+    }
+}
+
+extern "C" int tgkv_fwd_dec_w3_combine(const float* w3, const float* h, const int32_t* top_ids,
+                                       const float* top_w, float* x, uint32_t R, uint32_t d,
+                                       uint32_t dff, uint32_t ne, uint32_t na, void* stream) {
+    if (R == 0 || R > kDecRows || dff % 4) return (int)cudaErrorInvalidValue;
+    return launch_pdl(dec_w3_combine_kernel, dim3(blocks_for(d, 8)), 0, stream, w3, h, top_ids,
+                      top_w, x, R, d, dff, ne, na);
+}
+
+extern "C" int tgkv_fwd_dec_moe_w12(const float* x, const float* g, const float* router,
+                                    const float* bias, const float* w12, int32_t* top_ids,
+                                    float* top_w, float* h, uint32_t R, uint32_t d, uint32_t dff,
+                                    uint32_t ne, uint32_t na, void* stream) {
+    if (R == 0 || R > kDecRows || d % 4 || ne == 0 || ne > 16 || na == 0 || na > 8 || na > ne)
+        return (int)cudaErrorInvalidValue;
+    const size_t sm = dec_smem(1, d);
+    int e;
+    if ((e = set_smem(dec_moe_w12_kernel, sm))) return e;
+    return launch_pdl(dec_moe_w12_kernel, dim3(blocks_for(dff, 8), R * na), sm, stream, x, g,
+                      router, bias, w12, top_ids, top_w, h, d, dff, ne, na);
 }
 
 extern "C" void* tgkv_fwd_host_alloc(size_t bytes) {

@@ -51,6 +51,28 @@ int tgkv_fwd_expert_w3(const float* w3, const float* h, float* y, const uint32_t
 int tgkv_fwd_moe_combine(float* x, const float* y, const int32_t* top_ids, const float* top_w,
                          uint32_t seq, uint32_t d, uint32_t ne, uint32_t na, void* stream);
 
+/* Decode steps (at most tgkv_fwd_decode_rows() token rows), fused kernels,
+ * launched as programmatic dependents (TGKV_PDL=0: plain launches).
+ * dec_gemv: out[r][n] for r < R, n < N from W [N][K] (mode 1: += ; mode 2:
+ * SwiGLU over W = [W1; W2] of 2N rows, a clamped to +-88 when clamp != 0),
+ * the input rows RMS-normalised with g first when g is not NULL, bias [N]
+ * added in mode 0 when not NULL.  K and ldx multiples of 4. */
+uint32_t tgkv_fwd_decode_rows(void);
+int tgkv_fwd_dec_gemv(int mode, const float* w, const float* x, uint64_t ldx, const float* g,
+                      const float* bias, float* out, uint64_t ldo, uint32_t R, uint32_t N,
+                      uint32_t K, int clamp, void* stream);
+/* Router and experts W1/W2 in one launch: for every pair p = (r, k),
+ * ln = rmsnorm(x[r], g), the router's top-na of ln . router^T (+ bias) with
+ * softmax weights, and h[p] = silu(W1[e_k] ln) * (W2[e_k] ln); top_ids /
+ * top_w [R][na] written for tgkv_fwd_dec_w3_combine. */
+int tgkv_fwd_dec_moe_w12(const float* x, const float* g, const float* router, const float* bias,
+                         const float* w12, int32_t* top_ids, float* top_w, float* h, uint32_t R,
+                         uint32_t d, uint32_t dff, uint32_t ne, uint32_t na, void* stream);
+/* x[r] += sum_k top_w[r][k] * W3[e_k] . h[r * na + k]  (w3 = [ne][d][dff]). */
+int tgkv_fwd_dec_w3_combine(const float* w3, const float* h, const int32_t* top_ids,
+                            const float* top_w, float* x, uint32_t R, uint32_t d, uint32_t dff,
+                            uint32_t ne, uint32_t na, void* stream);
+
 /* Page-locked host memory (NULL on failure). */
 void* tgkv_fwd_host_alloc(size_t bytes);
 void  tgkv_fwd_host_free(void* p);

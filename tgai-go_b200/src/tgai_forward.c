@@ -630,16 +630,26 @@ static int gemm(Slot* s, uint32_t M, uint32_t N, uint32_t K, const float* x, uin
     return 1;
 }
 
-static int run_layer(TGFwdModel* m, Slot* s, uint32_t l, uint32_t seq, uint32_t pos) {
-    const Layer* L = &m->L[l];
-    const TGFwdConfig* c = &m->c;
-    const uint32_t d = c->d_model, dff = c->d_ff, ne = c->n_experts, na = c->n_activated;
-    void* st = s->stream;
-    TGKvCache* kv = s->kv[l];
+/* The fused decode kernels stage R token rows of K floats in shared memory. */
+static int decode_fits(uint32_t R, uint32_t K) {
+    return R <= tgkv_fwd_decode_rows() && (uint64_t)R * K * 4 + 1024 <= 200 * 1024;
+}
 
-    CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, s->x, L->ln1, seq, d, d, d, 1e-6f, st));
-    if (!gemm(s, seq, m->qkv_dim, d, s->ln, d, L->wqkv, s->qkv, m->qkv_dim, 0)) return 0;
-    if (L->bqkv) CHECK_LAUNCH(tgkv_fwd_bias(s->qkv, L->bqkv, seq, m->qkv_dim, st));
+/* Attention half of a layer: q/k/v, RoPE + KV append, attention.  Leaves the
+ * attention output in s->attn. */
+static int attn_half(TGFwdModel* m, Slot* s, const Layer* L, TGKvCache* kv, uint32_t seq,
+                     uint32_t pos, int decode) {
+    const TGFwdConfig* c = &m->c;
+    const uint32_t d = c->d_model;
+    void* st = s->stream;
+    if (decode) {
+        CHECK_LAUNCH(tgkv_fwd_dec_gemv(0, L->wqkv, s->x, d, L->ln1, L->bqkv, s->qkv, m->qkv_dim,
+                                       seq, m->qkv_dim, d, 0, st));
+    } else {
+        CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, s->x, L->ln1, seq, d, d, d, 1e-6f, st));
+        if (!gemm(s, seq, m->qkv_dim, d, s->ln, d, L->wqkv, s->qkv, m->qkv_dim, 0)) return 0;
+        if (L->bqkv) CHECK_LAUNCH(tgkv_fwd_bias(s->qkv, L->bqkv, seq, m->qkv_dim, st));
+    }
     t_launches++;
     if (!tg_cuda_kv_rope_append(TG_KV_F32, s->qkv, m->cs, m->sn, tg_kv_device_handle(kv), s->q,
                                 seq, c->n_heads, m->nkv, m->hd, pos, c->max_seq_len, st)) {
@@ -652,6 +662,33 @@ static int run_layer(TGFwdModel* m, Slot* s, uint32_t l, uint32_t seq, uint32_t 
         return 0;
     }
     t_launches += tg_cuda_kv_attn_last_launches();
+    return 1;
+}
+
+static int run_layer(TGFwdModel* m, Slot* s, uint32_t l, uint32_t seq, uint32_t pos) {
+    const Layer* L = &m->L[l];
+    const TGFwdConfig* c = &m->c;
+    const uint32_t d = c->d_model, dff = c->d_ff, ne = c->n_experts, na = c->n_activated;
+    void* st = s->stream;
+    const int decode = decode_fits(seq, d) && decode_fits(seq, m->q_dim) && decode_fits(seq, dff);
+    if (!attn_half(m, s, L, s->kv[l], seq, pos, decode)) return 0;
+    if (decode) {
+        /* out projection + residual, then the FFN, each with its norm fused */
+        CHECK_LAUNCH(tgkv_fwd_dec_gemv(1, L->wo, s->attn, m->q_dim, NULL, NULL, s->x, d, seq, d,
+                                       m->q_dim, 0, st));
+        if (ne == 0) {
+            CHECK_LAUNCH(tgkv_fwd_dec_gemv(2, L->w12, s->x, d, L->ln2, NULL, s->h, dff, seq, dff,
+                                           d, 1, st));
+            CHECK_LAUNCH(tgkv_fwd_dec_gemv(1, L->w3, s->h, dff, NULL, NULL, s->x, d, seq, d, dff,
+                                           0, st));
+            return 1;
+        }
+        CHECK_LAUNCH(tgkv_fwd_dec_moe_w12(s->x, L->ln2, L->router, L->qb, L->w12, s->top_ids,
+                                          s->top_w, s->h, seq, d, dff, ne, na, st));
+        CHECK_LAUNCH(tgkv_fwd_dec_w3_combine(L->w3, s->h, s->top_ids, s->top_w, s->x, seq, d, dff,
+                                             ne, na, st));
+        return 1;
+    }
     if (!gemm(s, seq, d, m->q_dim, s->attn, m->q_dim, L->wo, s->x, d, 1)) return 0;
     CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, s->x, L->ln2, seq, d, d, d, 1e-6f, st));
     if (ne == 0) {
@@ -697,8 +734,13 @@ static int run_forward(TGFwdModel* m, Slot* s, const int32_t* ids, uint32_t seq,
         if (!run_layer(m, s, l, seq, pos)) return 0;
     /* final norm of the last row, then the tied-embedding LM head */
     const float* xl = s->x + (uint64_t)(seq - 1) * d;
-    CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, xl, m->fnorm, 1, d, d, d, 1e-6f, st));
-    if (!gemm(s, 1, m->rows, d, s->ln, d, m->emb, s->logits, m->rows, 0)) return 0;
+    if (decode_fits(1, d)) {
+        CHECK_LAUNCH(tgkv_fwd_dec_gemv(0, m->emb, xl, d, m->fnorm, NULL, s->logits, m->rows, 1,
+                                       m->rows, d, 0, st));
+    } else {
+        CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, xl, m->fnorm, 1, d, d, d, 1e-6f, st));
+        if (!gemm(s, 1, m->rows, d, s->ln, d, m->emb, s->logits, m->rows, 0)) return 0;
+    }
     t_launches++;
     if (!tg_cuda_kv_d2h(s->h_logits, s->logits, (size_t)m->rows * 4, st) || !tg_cuda_kv_sync(st)) {
         set_err("forward: %s", tg_cuda_kv_last_error());
