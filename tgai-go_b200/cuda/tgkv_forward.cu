@@ -321,6 +321,60 @@ __global__ void __launch_bounds__(256) dec_gemv_kernel(const float* __restrict__
     }
 }
 
+// Q/K/V projection of a decode step with its norm, bias, RoPE and the KV
+// append fused: one warp per pair of adjacent output rows (2m, 2m+1), which
+// RoPE rotates together.  Query rows go to q_out [R][q_dim]; key and value
+// rows of token r go to position pos0 + r of the fp32 cache [2][max_seq]
+// [kv_dim].  The rotation is the KV path's (tgkv_kernels.cu rope_append), so
+// the bits equal a separate RoPE launch's.
+__global__ void __launch_bounds__(256) dec_qkv_rope_kernel(const float* __restrict__ w,
+                                                           const float* x, const float* g,
+                                                           const float* bias, const float* cs,
+                                                           const float* sn, float* q_out,
+                                                           float* kvc, uint32_t R, uint32_t d,
+                                                           uint32_t q_dim, uint32_t kv_dim,
+                                                           uint32_t hd, uint32_t pos0,
+                                                           uint32_t max_seq) {
+    extern __shared__ __align__(16) float dsm[];
+    float* sx = dsm + kDecRows;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t npair = (q_dim + 2 * kv_dim) / 2;
+    for (uint32_t m = blockIdx.x * 8 + warp; m < npair; m += gridDim.x * 8)
+        prefetch_row(w + (uint64_t)(2 * m) * d, 2 * d);
+    pdl_wait();
+    pdl_trigger();
+    stage_rows(sx, dsm, x, d, R, d, g, 1e-6f);
+    for (uint32_t m = blockIdx.x * 8 + warp; m < npair; m += gridDim.x * 8) {
+        const uint32_t n0 = 2 * m;
+        float a[kDecRows], b[kDecRows];
+        row_dots(w + (uint64_t)n0 * d, sx, R, d, a);
+        row_dots(w + (uint64_t)(n0 + 1) * d, sx, R, d, b);
+        if (lane < R) {
+            float v0 = a[0], v1 = b[0];
+#pragma unroll
+            for (int r = 1; r < kDecRows; ++r)
+                if ((uint32_t)r == lane) { v0 = a[r]; v1 = b[r]; }
+            if (bias) { v0 += bias[n0]; v1 += bias[n0 + 1]; }
+            const uint64_t pos = pos0 + lane;
+            if (n0 < q_dim + kv_dim) {
+                const uint32_t col = n0 < q_dim ? n0 : n0 - q_dim;
+                const uint32_t half = hd >> 1;
+                const float c = cs[pos * half + (col % hd) / 2], sn_ = sn[pos * half + (col % hd) / 2];
+                const float r0 = __fmaf_rn(v0, c, -__fmul_rn(v1, sn_));
+                const float r1 = __fmaf_rn(v0, sn_, __fmul_rn(v1, c));
+                float* dst = n0 < q_dim ? q_out + (uint64_t)lane * q_dim + col
+                                        : kvc + pos * kv_dim + col;
+                dst[0] = r0;
+                dst[1] = r1;
+            } else {
+                float* dst = kvc + ((uint64_t)max_seq + pos) * kv_dim + (n0 - q_dim - kv_dim);
+                dst[0] = v0;
+                dst[1] = v1;
+            }
+        }
+    }
+}
+
 // Expert W3, the k-ordered weighted sum and the residual of a decode step:
 // x[r][i] += sum_k top_w[r][k] * (W3[e_k][i] . h[r * na + k]).  One warp per
 // row i; the dot products of two k at a time share one load loop so that 16
@@ -581,6 +635,23 @@ extern "C" int tgkv_fwd_dec_gemv(int mode, const float* w, const float* x, uint6
     default:
         return (int)cudaErrorInvalidValue;
     }
+}
+
+extern "C" int tgkv_fwd_dec_qkv_rope(const float* w, const float* x, const float* g,
+                                     const float* bias, const float* cs, const float* sn,
+                                     float* q_out, float* kvc, uint32_t R, uint32_t d,
+                                     uint32_t q_dim, uint32_t kv_dim, uint32_t hd, uint32_t pos0,
+                                     uint32_t max_seq, void* stream) {
+    if (R == 0 || R > kDecRows || d % 4 || hd % 2 || q_dim % hd || kv_dim % hd ||
+        (uint64_t)pos0 + R > max_seq)
+        return (int)cudaErrorInvalidValue;
+    const size_t sm = dec_smem(R, d);
+    if (sm > 200 * 1024) return (int)cudaErrorInvalidValue;
+    int e;
+    if ((e = set_smem(dec_qkv_rope_kernel, sm))) return e;
+    const uint32_t npair = (q_dim + 2 * kv_dim) / 2;
+    return launch_pdl(dec_qkv_rope_kernel, dim3(blocks_for(npair, 8)), sm, stream, w, x, g, bias,
+                      cs, sn, q_out, kvc, R, d, q_dim, kv_dim, hd, pos0, max_seq);
 }
 
 extern "C" int tgkv_fwd_dec_w3_combine(const float* w3, const float* h, const int32_t* top_ids,

@@ -61,6 +61,13 @@ uint32_t tgkv_fwd_decode_rows(void);
 int tgkv_fwd_dec_gemv(int mode, const float* w, const float* x, uint64_t ldx, const float* g,
                       const float* bias, float* out, uint64_t ldo, uint32_t R, uint32_t N,
                       uint32_t K, int clamp, void* stream);
+/* Q/K/V rows of R tokens from rmsnorm(x, g) . W^T (+ bias), RoPE with the
+ * cs/sn tables [max_seq][hd/2] at positions pos0 + r, queries to q_out
+ * [R][q_dim], keys/values into the fp32 cache kvc [2][max_seq][kv_dim]. */
+int tgkv_fwd_dec_qkv_rope(const float* w, const float* x, const float* g, const float* bias,
+                          const float* cs, const float* sn, float* q_out, float* kvc, uint32_t R,
+                          uint32_t d, uint32_t q_dim, uint32_t kv_dim, uint32_t hd, uint32_t pos0,
+                          uint32_t max_seq, void* stream);
 /* Router and experts W1/W2 in one launch: for every pair p = (r, k),
  * ln = rmsnorm(x[r], g), the router's top-na of ln . router^T (+ bias) with
  * softmax weights, and h[p] = silu(W1[e_k] ln) * (W2[e_k] ln); top_ids /

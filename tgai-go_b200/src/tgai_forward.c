@@ -643,18 +643,21 @@ static int attn_half(TGFwdModel* m, Slot* s, const Layer* L, TGKvCache* kv, uint
     const uint32_t d = c->d_model;
     void* st = s->stream;
     if (decode) {
-        CHECK_LAUNCH(tgkv_fwd_dec_gemv(0, L->wqkv, s->x, d, L->ln1, L->bqkv, s->qkv, m->qkv_dim,
-                                       seq, m->qkv_dim, d, 0, st));
+        /* norm + projection + bias + RoPE + KV append in one launch */
+        CHECK_LAUNCH(tgkv_fwd_dec_qkv_rope(L->wqkv, s->x, L->ln1, L->bqkv, m->cs, m->sn, s->q,
+                                           (float*)tg_kv_device_handle(kv), seq, d, m->q_dim,
+                                           m->kv_dim, m->hd, pos, c->max_seq_len, st));
     } else {
         CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, s->x, L->ln1, seq, d, d, d, 1e-6f, st));
         if (!gemm(s, seq, m->qkv_dim, d, s->ln, d, L->wqkv, s->qkv, m->qkv_dim, 0)) return 0;
         if (L->bqkv) CHECK_LAUNCH(tgkv_fwd_bias(s->qkv, L->bqkv, seq, m->qkv_dim, st));
-    }
-    t_launches++;
-    if (!tg_cuda_kv_rope_append(TG_KV_F32, s->qkv, m->cs, m->sn, tg_kv_device_handle(kv), s->q,
-                                seq, c->n_heads, m->nkv, m->hd, pos, c->max_seq_len, st)) {
-        set_err("RoPE + append: %s", tg_cuda_kv_last_error());
-        return 0;
+        t_launches++;
+        if (!tg_cuda_kv_rope_append(TG_KV_F32, s->qkv, m->cs, m->sn, tg_kv_device_handle(kv),
+                                    s->q, seq, c->n_heads, m->nkv, m->hd, pos, c->max_seq_len,
+                                    st)) {
+            set_err("RoPE + append: %s", tg_cuda_kv_last_error());
+            return 0;
+        }
     }
     tg_kv_advance(kv, seq);
     if (!tg_kv_attention(kv, s->q, s->attn, c->n_heads, seq, st)) {
