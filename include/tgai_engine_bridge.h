@@ -6,7 +6,7 @@
  *  1. The engine-facing entry points, with the signatures and contract of the
  *     reference's cuda/tgai_cuda_bridge.h:31-60.  tgai_engine.c built with
  *     TG_ENGINE_HAS_CUDA_BRIDGE calls tg_engine_cuda_forward first in
- *     tg_forward (src/tgai_engine.c:4361-4372) and runs its CPU path only when
+ *     tg_forward (src/tgai_engine.c:4373-4378) and runs its CPU path only when
  *     it returns 0.  tg_engine_cuda_init reads the model through the engine's
  *     own exported accessors (tg_config, find_weight, get_cached_weight;
  *     src/tgai_engine.h:70-76), looked up in the running process, so this

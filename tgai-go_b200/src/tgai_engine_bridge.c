@@ -8,9 +8,11 @@
  * ready or the model is not the one it took, and counts a fallback when the
  * GPU forward itself fails.  The reference reads the model through the
  * engine's exported accessors; so does this file, resolving tg_config,
- * find_weight, get_cached_weight and tg_preload_all in the running process
- * (src/tgai_engine.h:60-117), so that the library links without the engine.
+ * find_weight, get_cached_weight and tg_preload_all in the engine object that
+ * called tg_engine_cuda_init (else anywhere in the process;
+ * src/tgai_engine.h:60-117), so that the library links without the engine.
  */
+#define _GNU_SOURCE
 #include "tgai_engine_bridge.h"
 
 #include <dlfcn.h>
@@ -102,10 +104,22 @@ int tg_engine_cuda_init(TGModel* m) {
         snprintf(g_reason, sizeof(g_reason),
                  "TGAI_USE_GPU not enabled (set to 1 to enable GPU forward)");
     } else {
-        p_config = (config_fn)dlsym(RTLD_DEFAULT, "tg_config");
-        p_find = (find_fn)dlsym(RTLD_DEFAULT, "find_weight");
-        p_get = (get_fn)dlsym(RTLD_DEFAULT, "get_cached_weight");
-        preload_fn preload = (preload_fn)dlsym(RTLD_DEFAULT, "tg_preload_all");
+        /* the accessors of the engine that called us (tg_load), else any in the process */
+        void* eng = NULL;
+        Dl_info di;
+        if (dladdr(__builtin_return_address(0), &di) && di.dli_fname)
+            eng = dlopen(di.dli_fname, RTLD_LAZY | RTLD_NOLOAD);
+        if (eng && !dlsym(eng, "tg_config")) {
+            dlclose(eng);
+            eng = NULL;
+        }
+        void* const held = eng;            /* the engine stays loaded: it called us */
+        if (!eng) eng = RTLD_DEFAULT;
+        p_config = (config_fn)dlsym(eng, "tg_config");
+        p_find = (find_fn)dlsym(eng, "find_weight");
+        p_get = (get_fn)dlsym(eng, "get_cached_weight");
+        preload_fn preload = (preload_fn)dlsym(eng, "tg_preload_all");
+        if (held) dlclose(held);
         const EngineHeader* h = p_config && p_find && p_get ? p_config(m) : NULL;
         if (!p_config || !p_find || !p_get) {
             snprintf(g_reason, sizeof(g_reason),
