@@ -148,8 +148,10 @@ uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c);
 /* Launches made by the last tg_cuda_kv_attention on this thread. */
 uint32_t tg_cuda_kv_attn_last_launches(void);
 /* Kernel family of this thread's last tg_cuda_kv_attention call:
- * 0 none, 1 split-sequence (tgkv_kernels.cu), 2 tensor-core suffix
- * (tgkv_prefill.cu). */
+ * 0 none, 1 split-sequence on CUDA cores (tgkv_kernels.cu), 2 tensor-core
+ * suffix (tgkv_prefill.cu), 3 tensor-core split-sequence decode
+ * (tgkv_decode_tc.cuh; bf16 head_dim-128 caches, TGKV_DECODE_TC=0 turns it
+ * off). */
 int tg_cuda_kv_attn_last_kernel(void);
 /* CTAs per row block (KV split) of the last tensor-core suffix launch. */
 uint32_t tg_cuda_kv_attn_last_split(void);

@@ -21,6 +21,17 @@ TOL_F32 = 1e-5
 TOL_BF16 = 1e-2
 
 
+@pytest.fixture(autouse=True, params=["auto", "tc"])
+def decode_kernel(request, monkeypatch):
+    """Every test twice: with the library's own choice of decode kernel, and
+    with every bf16 head_dim-128 call forced onto the tensor-core decode
+    kernel (which the library otherwise keeps for launches of >= 4
+    sequences), so that both split-sequence kernels meet every case."""
+    if request.param == "tc":
+        monkeypatch.setenv("TGKV_DECODE_TC", "1")
+    return request.param
+
+
 def golden(name):
     return np.load(os.path.join(GOLDEN, name))
 
@@ -421,9 +432,12 @@ def test_cfg5_long_context_131072(cuda, devbuf):
     assert rel_head_err(got, eng) < TOL_BF16
     # At 131072 positions the engine order's sequential float sums carry
     # ~1e-5 of rounding themselves; the double-accumulation oracle is the
-    # sharper reference and the split-sequence kernel stays within 1e-5 of it.
+    # sharper reference: the CUDA-core kernel stays within 1e-5 of it, the
+    # tensor-core one (fp32 accumulation inside the MMAs over ~1000 tiles)
+    # within TC_TOL (measured 1.5e-5).
+    tol = attn_tol(lib)
     f64 = O.attention_f64(q[-1:], kvc, nh, nkv, hd, 1, L - 1, L, L)
-    assert rel_head_err(got, f64) < 1e-5
+    assert rel_head_err(got, f64) < tol
     assert rel_head_err(eng, f64) < 1e-4
     lib.tg_kv_destroy(c)
 

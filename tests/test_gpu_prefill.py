@@ -19,7 +19,7 @@ from test_gpu_parity import attend, host_cache, make_cache, synth_qkv
 
 pytestmark = pytest.mark.gpu
 
-SPLIT, TENSOR = 1, 2       # tg_cuda_kv_attn_last_kernel() families
+SPLIT, TENSOR, DECODE_TC = 1, 2, 3    # tg_cuda_kv_attn_last_kernel() families
 BF16_TOL = 1e-2            # the bf16-cache tolerance of the path
 # TC_TOL: emulating the hi + lo split exactly on the CPU gives 6.5e-6 on the
 # cfg3 shape; the tensor cores' fp32 accumulation adds about as much again.
@@ -60,6 +60,7 @@ def test_prefill_equals_split_sequence_kernel(cuda, devbuf, monkeypatch):
     tc = attend(lib, devbuf, c, q[-nq:], nh, nq)
     assert lib.tg_cuda_kv_attn_last_kernel() == TENSOR
     monkeypatch.setenv("TGKV_PREFILL", "0")
+    monkeypatch.setenv("TGKV_DECODE_TC", "0")
     cc = attend(lib, devbuf, c, q[-nq:], nh, nq)
     assert lib.tg_cuda_kv_attn_last_kernel() == SPLIT
     assert rel_head_err(tc, cc) < TC_TOL
@@ -87,12 +88,15 @@ def test_prefill_with_temperature(cuda, devbuf):
     (1, 128, 12, 4, 64),     # group of 3
 ])
 def test_ineligible_calls_stay_on_split_kernel(cuda, devbuf, dtype, hd, nh, nkv, nq):
+    """Not for the suffix kernel: the split-sequence kernels take them (the
+    tensor-core one for bf16 head_dim 128, the CUDA-core one otherwise)."""
     lib = cuda
     L = 300
     q, k, v = synth_qkv(99 + nh + hd, L, nh, nkv, hd)
     c = make_cache(lib, devbuf, L, nkv, hd, dtype, k, v)
     got = attend(lib, devbuf, c, q[-nq:], nh, nq)
-    assert lib.tg_cuda_kv_attn_last_kernel() == SPLIT
+    want = DECODE_TC if (dtype, hd) == (1, 128) else SPLIT
+    assert lib.tg_cuda_kv_attn_last_kernel() == want
     kvc = host_cache(lib, c, dtype, L, nkv * hd)
     eng = O.attention_engine(q[-nq:], kvc, nh, nkv, hd, nq, L - nq, L, L)
     assert rel_head_err(got, eng) < 1e-5

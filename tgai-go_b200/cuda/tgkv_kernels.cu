@@ -713,6 +713,48 @@ int launch_attn(const TGKvAttnParams* p, uint32_t grid, cudaStream_t st) {
 
 }  // namespace tgkv
 
+#include "tgkv_decode_tc.cuh"
+
+namespace tgkv {
+template <int GT>
+int launch_attn_tc(const TGKvAttnParams* p, uint32_t grid, cudaStream_t st) {
+    static bool configured = false;                 // benign race: same value
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<GT>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)tc::SMEM_BYTES);
+        if (e != cudaSuccess) return (int)e;
+        configured = true;
+    }
+    static const bool pdl = [] {
+        const char* e = getenv("TGKV_PDL");
+        return !(e && e[0] == '0');
+    }();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(tc::kThreads);
+    cfg.dynamicSmemBytes = tc::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return (int)cudaLaunchKernelEx(&cfg, attention_tc_kernel<GT>, *p);
+}
+}  // namespace tgkv
+
+extern "C" int tgkv_launch_attention_tc(const TGKvAttnParams* p, uint32_t g_tile, uint32_t grid,
+                                        void* stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    switch (g_tile) {
+    case 1: return tgkv::launch_attn_tc<1>(p, grid, st);
+    case 2: return tgkv::launch_attn_tc<2>(p, grid, st);
+    case 4: return tgkv::launch_attn_tc<4>(p, grid, st);
+    default: return (int)cudaErrorInvalidValue;
+    }
+}
+
 extern "C" uint32_t tgkv_attention_g_tile(uint32_t head_dim, uint32_t group) {
     // Largest of 4, 2, 1 that divides the group and fits the register budget
     // (query and output slices of GT heads per lane).

@@ -127,6 +127,11 @@ int tgkv_launch_prefill(const TGKvPrefillParams* p, void* stream);
 uint32_t tgkv_prefill_max_clusters(uint32_t n_split);
 int tgkv_launch_attention(const TGKvAttnParams* p, int dtype, uint32_t head_dim,
                           uint32_t g_tile, uint32_t grid, void* stream);
+/* The tensor-core decode kernel (tgkv_decode_tc.cuh): bf16 caches of
+ * head_dim 128 with a swizzled tensor map, g_tile 1, 2 or 4, chunks planned
+ * with tiles of 128 positions and one CTA per SM. */
+int tgkv_launch_attention_tc(const TGKvAttnParams* p, uint32_t g_tile, uint32_t grid,
+                             void* stream);
 int tgkv_launch_append(const TGKvAppendParams* p, int dtype, void* stream);
 /* One thread waits (acquire, system scope; bounded, error word on expiry)
  * until *flag has reached target (wrap-safe). */
@@ -134,6 +139,9 @@ int tgkv_launch_gather_wait(const uint32_t* flag, uint32_t target, int32_t* err,
 int tgkv_launch_rope_append(const TGKvRopeParams* p, void* stream);
 /* Chunk length the planner uses for a launch of total_positions (bridge). */
 uint32_t tgkv_pick_chunk(const uint32_t* n_pos, uint32_t n_items, uint32_t mult, uint32_t sm_count);
+/* The same with `slots` resident CTAs per wave and chunks a multiple of tile. */
+uint32_t tgkv_pick_chunk_tiled(const uint32_t* n_pos, uint32_t n_items, uint32_t mult,
+                               uint32_t slots, uint32_t tile);
 /* Heads per CTA the attention kernel supports for this head_dim (<= G). */
 uint32_t tgkv_attention_g_tile(uint32_t head_dim, uint32_t group);
 /* 1 if (dtype, head_dim) has an attention kernel. */

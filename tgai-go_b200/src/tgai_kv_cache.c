@@ -390,6 +390,7 @@ TGKvBatch* tg_kv_batch_create(TGKvCache* const* caches, uint32_t n, uint32_t n_h
         table[i].base = (uint64_t)(uintptr_t)caches[i]->dev;
         table[i].max_seq = caches[i]->max_seq;
         table[i].tmap = (uint64_t)(uintptr_t)caches[i]->tmap;
+        table[i].tmap_sw = (uint64_t)(uintptr_t)caches[i]->tmap_sw;
     }
     b->table_dev = (TGCudaCacheDesc*)b->be->alloc(n * sizeof(TGCudaCacheDesc));
     if (!b->table_dev || !tg_cuda_kv_h2d(b->table_dev, table, n * sizeof(TGCudaCacheDesc), NULL)) {
