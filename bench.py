@@ -334,6 +334,8 @@ def run_ours(args):
     barrier()
     clock = clocks.stop()
     timed_launches = launches[0]
+    kfam = {1: "attention_kernel (CUDA cores)", 3: "attention_tc_kernel (tcgen05)"}.get(
+        lib.tg_cuda_kv_attn_last_kernel(), "?")
     ms = t0.elapsed_time(t1) / args.steps
     ms_max = max_over_ranks(ms)
     call_ms = [a.elapsed_time(b) for a, b in ev]
@@ -430,6 +432,7 @@ def run_ours(args):
                                        + ("in-kernel NVLink gather" if fused else "NCCL all-gather")
                                        if heads_sharded else
                                        f"sequences x{world} ({'LPT split' if args.shard_seqs else 'own set per GPU'}), no collective"),
+                       "attention_kernel": kfam,
                        "fill_s": round(t_fill, 1)},
             "hbm_gbs": algo / (ms * args.steps / 1000.0) / 1e9,
             "roofline": {"bound": "hbm", "achieved": kernel_gbs, "peak": peak, "unit": "GB/s",
