@@ -21,14 +21,17 @@ TOL_F32 = 1e-5
 TOL_BF16 = 1e-2
 
 
-@pytest.fixture(autouse=True, params=["auto", "tc"])
+@pytest.fixture(autouse=True, params=["auto", "tc", "tc-steal"])
 def decode_kernel(request, monkeypatch):
-    """Every test twice: with the library's own choice of decode kernel, and
-    with every bf16 head_dim-128 call forced onto the tensor-core decode
-    kernel (which the library otherwise keeps for launches of >= 4
-    sequences), so that both split-sequence kernels meet every case."""
-    if request.param == "tc":
+    """Every test three times: with the library's own choice of decode
+    kernel; with every bf16 head_dim-128 call forced onto the tensor-core
+    decode kernel (which the library otherwise keeps for launches of >= 4
+    sequences); and the same with its opt-in tile stealing.  Both
+    split-sequence kernels and both tensor-core schedules meet every case."""
+    if request.param.startswith("tc"):
         monkeypatch.setenv("TGKV_DECODE_TC", "1")
+    if request.param == "tc-steal":
+        monkeypatch.setenv("TGKV_STEAL", "1")
     return request.param
 
 

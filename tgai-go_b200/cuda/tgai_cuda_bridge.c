@@ -583,12 +583,24 @@ uint64_t tg_cuda_kv_attn_scratch_bytes(const TGCudaAttnCall* c) {
     return part_o_bytes(&pl, c->head_dim) + pl.max_chunks * pl.gt * 2 * 4;
 }
 
-/* One arrival counter per segment. */
+/* One arrival counter per segment; the tensor-core decode kernel also keeps
+ * one tile queue per segment after them. */
 uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c) {
     if (use_prefill(c)) return 1;
     AttnPlan pl;
     if (!plan_attention(c, &pl)) return 0;
-    return (uint64_t)c->n_items * c->n_kv_heads * pl.n_sub;
+    return (uint64_t)c->n_items * c->n_kv_heads * pl.n_sub * (pl.tc ? 2u : 1u);
+}
+
+/* Tile stealing inside a segment (tensor-core decode), opt-in with
+ * TGKV_STEAL=1: the segment's CTAs take 128-position tiles from a shared
+ * queue instead of streaming fixed chunks.  Measured on B200 it did not pay:
+ * cfg4 0.961 against 0.977 of HBM with fixed chunks on the same box, one
+ * 131072-position sequence 0.76-0.80 against 0.82 -- one atomic per tile on
+ * the producer's path costs more than the imbalance it removes. */
+static int steal_on(void) {
+    const char* e = getenv("TGKV_STEAL");
+    return e && e[0] == '1';
 }
 
 uint32_t tg_cuda_kv_attn_last_launches(void) { return t_last_launches; }
@@ -671,6 +683,9 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         p.part_o = (float*)c->scratch;
         p.part_ml = (float*)((char*)c->scratch + po);
         p.counters = c->counters;
+        p.tile_ctr = (pl.tc && steal_on())
+                         ? c->counters + (uint64_t)c->n_items * c->n_kv_heads * pl.n_sub
+                         : NULL;
         p.err = g_err_word;
         p.cache_stride = c->table_dev ? 1u : 0u;
         p.n_items = n;

@@ -50,7 +50,8 @@ constexpr uint32_t OFF_TSLOT = OFF_BAR + 32 * 8;
 constexpr uint32_t OFF_RED = OFF_TSLOT + 16;            // [4 warps][16] tile maxima / sums
 constexpr uint32_t OFF_CRED = OFF_RED + 4 * kN * 4;     // [4][GT][2] for the merge
 constexpr uint32_t OFF_FLAG = OFF_CRED + 4 * 4 * 2 * 4;
-constexpr uint32_t SMEM_USED = OFF_FLAG + 16;
+constexpr uint32_t OFF_TPOS = OFF_FLAG + 16;            // [3] first position of each stage's tile
+constexpr uint32_t SMEM_USED = OFF_TPOS + 16;
 constexpr uint32_t SMEM_BYTES = SMEM_USED + 1024;       // slack to align the base
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 // the merge reuses the idle ring: (m, l) pairs, then 128 float4 sums
@@ -70,6 +71,7 @@ constexpr int B_QREADY = 14;   // Q in shared memory (128 arrivals)
 constexpr uint32_t TM_S = 0, TM_O = 32, TM_COLS = 64;
 
 constexpr int kErrTcTimeout = 5;
+constexpr uint32_t kEnd = 0xffffffffu;          // a stage's tile position: no more tiles
 
 // Byte offset of element (row r, column c) of a 16-row, 128-column bf16
 // operand stored as two 64-column blocks in the canonical 128-byte swizzle
@@ -142,11 +144,20 @@ attention_tc_kernel(const __grid_constant__ TGKvAttnParams p) {
     uint32_t* tslot = reinterpret_cast<uint32_t*>(base + OFF_TSLOT);
     float* red = reinterpret_cast<float*>(base + OFF_RED);
     int* flag = reinterpret_cast<int*>(base + OFF_FLAG);      // [0] abort, [1] last
+    volatile uint32_t* tpos = reinterpret_cast<volatile uint32_t*>(base + OFF_TPOS);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t u = blockIdx.x;
     const Chunk ck = decode_chunk(p, u);
-    const int nt = (int)((ck.pos1 - ck.pos0 + kPos - 1) / kPos);
+    const uint32_t n_item = p.n_pos[ck.item];
+    const uint64_t cidx = (uint64_t)(p.item_base + ck.item) * (p.n_sub * p.n_kv_heads) + ck.seg;
+    // Tile stealing (tile_ctr set, opt-in): the segment's CTAs take tiles of
+    // [0, n_item) from its queue, so a CTA on a slower SM takes fewer;
+    // otherwise each CTA streams the tiles of its own chunk.  Either way the
+    // producer ends the stream with a stage marked kEnd and the other warps
+    // stop there.
+    const bool steal = p.tile_ctr != nullptr;
+    const uint32_t lim = steal ? n_item : ck.pos1;          // positions past lim are masked
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -177,12 +188,14 @@ attention_tc_kernel(const __grid_constant__ TGKvAttnParams p) {
 
     if (warp == kTmaWarp) {
         const TGKvCacheDesc cd = p.caches ? p.caches[ck.item * p.cache_stride] : p.cache0;
-        if (p.k_new && ck.pos1 == p.n_pos[ck.item]) {
+        if (p.k_new && (steal || ck.pos1 == n_item)) {
             // fused append, as in attention_kernel: this KV head's slice of the
-            // new row, then visible to the TMA reads below
+            // new row, then visible to this CTA's TMA reads below (with
+            // stealing any CTA of the segment may load the last tile, so each
+            // writes the same bytes first)
             const uint64_t kv_dim = (uint64_t)p.n_kv_heads * HD;
             const uint64_t src = (uint64_t)(p.item_base + ck.item) * kv_dim + ck.kvh * HD;
-            const uint64_t dst = (uint64_t)(ck.pos1 - 1) * kv_dim + ck.kvh * HD;
+            const uint64_t dst = (uint64_t)(n_item - 1) * kv_dim + ck.kvh * HD;   // the new row
             const uint64_t vofs = (uint64_t)cd.max_seq * kv_dim;
             uint16_t* c = reinterpret_cast<uint16_t*>(cd.base);
             for (int e = lane; e < HD; e += 32) {
@@ -195,14 +208,30 @@ attention_tc_kernel(const __grid_constant__ TGKvAttnParams p) {
         if (lane == 0) {
             prefetch_tmap(cd.tmap_sw);
             const int x = (int)(ck.kvh * HD);
-            for (int t = 0; t < nt; ++t) {
+            const uint32_t seg_tiles = (n_item + kPos - 1) / kPos;
+            for (int t = 0;; ++t) {
+                uint32_t yy;
+                bool done;
+                if (steal) {
+                    const uint32_t g = atomicAdd(p.tile_ctr + cidx, 1u);
+                    done = g >= seg_tiles;
+                    yy = g * kPos;
+                } else {
+                    yy = ck.pos0 + (uint32_t)t * kPos;
+                    done = yy >= ck.pos1;
+                }
                 const int s = t % kStages;
                 if (t >= kStages && !mbar_wait(&bar[B_EMPTY + s], (uint32_t)((t / kStages) - 1) & 1u)) {
                     atomicExch(p.err, kErrTcTimeout);
                     flag[0] = 1;
                     break;
                 }
-                const int y = (int)(ck.pos0 + (uint32_t)t * kPos);
+                tpos[s] = done ? kEnd : yy;
+                if (done) {                     // the end marker: the phase completes without data
+                    mbar_arrive(&bar[B_FULL + s]);
+                    break;
+                }
+                const int y = (int)yy;
                 unsigned char* st = base + OFF_RING + s * kStage;
                 mbar_arrive_expect_tx(&bar[B_FULL + s], kStage);
                 tma_load_3d(st, cd.tmap_sw, x, y, 0, &bar[B_FULL + s]);
@@ -220,10 +249,16 @@ attention_tc_kernel(const __grid_constant__ TGKvAttnParams p) {
             constexpr uint32_t id_s = umma_idesc_bf16(kPos, kN, 0, 0);
             constexpr uint32_t id_pv = umma_idesc_bf16(HD, kN, 1, 0);
             ok = mbar_wait(&bar[B_QREADY], 0);
-            // S^T(j) into buffer j % 2: A = the K tile (K-major), B = the stacked Q
+            int nt = -1;                        // tiles of this CTA, once the end marker is seen
+            // S^T(j) into buffer j % 2: A = the K tile (K-major), B = the stacked Q.
+            // Returns false on a timeout; at the end marker sets nt = j instead.
             auto issue_s = [&](int j) -> bool {
                 const int s = j % kStages, b = j & 1;
                 if (!mbar_wait(&bar[B_FULL + s], (uint32_t)(j / kStages) & 1u)) return false;
+                if (tpos[s] == kEnd) {
+                    nt = j;
+                    return true;
+                }
                 if (j >= 2 && !mbar_wait(&bar[B_SFREE + b], (uint32_t)((j >> 1) - 1) & 1u))
                     return false;
                 tc_fence_after();
@@ -238,8 +273,9 @@ attention_tc_kernel(const __grid_constant__ TGKvAttnParams p) {
                 umma_commit(&bar[B_SFULL + b]);
                 return true;
             };
-            for (int j = 0; ok && j < nt && j < 2; ++j) ok = issue_s(j);
-            for (int j = 0; ok && j < nt; ++j) {
+            if (ok) ok = issue_s(0);
+            if (ok && nt < 0) ok = issue_s(1);
+            for (int j = 0; ok && (nt < 0 || j < nt); ++j) {
                 const int s = j % kStages, b = j & 1;
                 if (!mbar_wait(&bar[B_PFULL + b], (uint32_t)(j >> 1) & 1u)) { ok = false; break; }
                 tc_fence_after();
@@ -257,7 +293,7 @@ attention_tc_kernel(const __grid_constant__ TGKvAttnParams p) {
                 }
                 umma_commit(&bar[B_EMPTY + s]);
                 umma_commit(&bar[B_PEMPTY + b]);
-                if (j + 2 < nt) ok = issue_s(j + 2);
+                if (nt < 0) ok = issue_s(j + 2);
             }
             if (!ok) {
                 atomicExch(p.err, kErrTcTimeout);
@@ -276,7 +312,6 @@ attention_tc_kernel(const __grid_constant__ TGKvAttnParams p) {
     const uint32_t group = p.n_heads / p.n_kv_heads;
     const uint32_t head0 = ck.kvh * group + ck.sub * GT;
     const uint64_t row = (uint64_t)(p.item_base + ck.item) * p.n_heads * HD;
-    const uint32_t n_item = p.n_pos[ck.item];
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     // rows >= 3 GT of the Q and P operands stay zero; row t * GT + h of Q:
     // term t of q * scale (log2 domain) for head h
@@ -310,14 +345,24 @@ attention_tc_kernel(const __grid_constant__ TGKvAttnParams p) {
     auto pv_done = [&](int j) -> bool {
         return mbar_wait(&bar[B_PEMPTY + (j & 1)], (uint32_t)(j >> 1) & 1u);
     };
-    for (int j = 0; j < nt; ++j) {
-        const int b = j & 1;
+    int nt = 0;                                          // tiles this CTA attended
+    for (int j = 0;; ++j) {
+        const int b = j & 1, s = j % kStages;
         uint32_t sv[16];
+        // the stage's tile position, or the end marker, once its FULL phase is
+        // complete; every thread reads the same word, and the barrier makes
+        // the exit (end or timeout) common to the four warps
+        bool mine = mbar_wait(&bar[B_FULL + s], (uint32_t)(j / kStages) & 1u);
+        uint32_t tp = kEnd;
+        if (mine) tp = tpos[s];
+        if (!softmax_bar_all(ok && mine)) { ok = false; break; }
+        if (tp == kEnd) break;
+        nt = j + 1;
         // tcgen05.ld / st are warp-collective: every guard around them is made
         // warp-uniform
-        bool mine = __all_sync(0xffffffffu, mbar_wait(&bar[B_SFULL + b], (uint32_t)(j >> 1) & 1u));
-        const uint32_t pos = ck.pos0 + (uint32_t)j * kPos + pp;
-        const bool valid = pos < ck.pos1;
+        mine = __all_sync(0xffffffffu, mbar_wait(&bar[B_SFULL + b], (uint32_t)(j >> 1) & 1u));
+        const uint32_t pos = tp + pp;
+        const bool valid = pos < lim;
         float sc[GT], tmx[GT];
         if (mine) {
             tc_fence_after();
@@ -393,17 +438,13 @@ attention_tc_kernel(const __grid_constant__ TGKvAttnParams p) {
         }
         if (pos >= n_item) {
             // rows past the item's length may hold anything (a truncated turn):
-            // P = 0 there, but 0 x Inf/NaN is NaN, so clear this V row
-            const int s = j % kStages;
-            if (mbar_wait(&bar[B_FULL + s], (uint32_t)(j / kStages) & 1u)) {
-                const uint32_t vr = sbase + OFF_RING + s * kStage + 2 * kBlk + pp * 128u;
+            // P = 0 there, but 0 x Inf/NaN is NaN, so clear this V row (its
+            // stage has landed: FULL was waited for above)
+            const uint32_t vr = sbase + OFF_RING + s * kStage + 2 * kBlk + pp * 128u;
 #pragma unroll
-                for (uint32_t c = 0; c < 128; c += 16) {
-                    st_shared_zero16(vr + c);
-                    st_shared_zero16(vr + kBlk + c);
-                }
-            } else {
-                ok = false;
+            for (uint32_t c = 0; c < 128; c += 16) {
+                st_shared_zero16(vr + c);
+                st_shared_zero16(vr + kBlk + c);
             }
         }
         fence_proxy_async_smem();
@@ -425,7 +466,9 @@ attention_tc_kernel(const __grid_constant__ TGKvAttnParams p) {
         flag[0] = 1;
     }
     tc_fence_after();
-    {
+#pragma unroll
+    for (int h = 0; h < GT; ++h) ov_f[h] = 0.f;          // a CTA left without tiles
+    if (nt > 0) {
         uint32_t ov[16];
         tmem_ld16(tmem + lane_off + TM_O, ov);
         tmem_wait_ld16(ov);
@@ -468,13 +511,13 @@ attention_tc_kernel(const __grid_constant__ TGKvAttnParams p) {
         }
     }
     if (whole) {
+        if (steal && tid == 0) p.tile_ctr[cidx] = 0u;      // this CTA was the segment
         if (p.gather_world) gather_signal(p, tid);
         return;
     }
     // ---- the last chunk of the segment to finish merges them all
     __threadfence();
     softmax_bar();
-    const uint64_t cidx = (uint64_t)(p.item_base + ck.item) * (p.n_sub * p.n_kv_heads) + ck.seg;
     if (tid == 0) {
         const uint32_t prev = atomicAdd(&p.counters[cidx], 1u);
         flag[1] = (prev == ck.nch - 1) ? 1 : 0;
@@ -488,7 +531,12 @@ attention_tc_kernel(const __grid_constant__ TGKvAttnParams p) {
                                       reinterpret_cast<float2*>(base + OFF_RING),
                                       reinterpret_cast<float4*>(base + OFF_ACC),
                                       reinterpret_cast<float*>(base + OFF_CRED), tid, lane, warp);
-    if (tid == 0) p.counters[cidx] = 0u;
+    if (tid == 0) {
+        p.counters[cidx] = 0u;
+        // every CTA of the segment has arrived, so every producer is past its
+        // last take from the queue
+        if (steal) p.tile_ctr[cidx] = 0u;
+    }
 }
 
 }  // namespace tgkv

@@ -52,6 +52,10 @@ typedef struct {
     float*       part_o;         /* [n_chunks][GT][head_dim]  scratch */
     float*       part_ml;        /* [n_chunks][GT][2]         scratch */
     uint32_t*    counters;       /* [items][n_sub*n_kv_heads], zero, self-resetting */
+    uint32_t*    tile_ctr;       /* tensor-core decode only: NULL (each CTA streams its
+                                  * chunk), or per-segment tile queues laid out as
+                                  * counters (zero, reset by the merging CTA): the
+                                  * segment's CTAs take 128-position tiles from it */
     int32_t*     err;            /* device error word (0 = fine) */
     uint32_t cache_stride;       /* cache index = item * cache_stride */
     uint32_t n_items;
