@@ -37,8 +37,11 @@ def _plan(lib, devbuf, n_seq, L, nkv, hd, nh, seed):
     return caches, b, rows
 
 
-def test_single_rank_gather_equals_plain_decode(cuda, devbuf):
+@pytest.mark.parametrize("kernel", ["auto", "tc"])
+def test_single_rank_gather_equals_plain_decode(cuda, devbuf, monkeypatch, kernel):
     lib = cuda
+    if kernel == "tc":                       # the tensor-core decode kernel's gather stores
+        monkeypatch.setenv("TGKV_DECODE_TC", "1")
     n_seq, L, nkv, hd, nh = 3, 2500, 4, 128, 16
     caches, b, rows = _plan(lib, devbuf, n_seq, L, nkv, hd, nh, 6100)
     elems = n_seq * nh * hd
@@ -149,10 +152,13 @@ def _rank_main(rank, world, port, result_dir):
         f.write(f"{e} {err}\n")
 
 
-def test_two_rank_gather_over_nvlink(tmp_path):
+@pytest.mark.parametrize("kernel", ["auto", "tc"])
+def test_two_rank_gather_over_nvlink(tmp_path, monkeypatch, kernel):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
+    if kernel == "tc":                       # inherited by the spawned ranks
+        monkeypatch.setenv("TGKV_DECODE_TC", "1")
     import socket
     import torch.multiprocessing as mp
     with socket.socket() as s:

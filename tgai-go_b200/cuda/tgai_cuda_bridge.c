@@ -427,14 +427,17 @@ typedef struct {
 
 
 /* Chunk length (one CTA per chunk of one item's positions for one KV head
- * and head subset).  CTAs run in waves of two per SM, and every wave costs a
- * fixed start-up, tail and merge time besides its streaming, measured on B200
- * at about the time of 768 positions per CTA (cfg5: 103 / 124 / 139 us per
- * layer at 1 / 2 / 3 waves against 83 us of pure streaming).  So the planner
- * takes, over targets of 1 to 16 waves, the chunk whose exact CTA count
- * minimises waves x (chunk + 768); never below 128 positions, a multiple of
- * the TMA tile.  TGKV_CHUNK overrides (tests use it to force split
- * boundaries); TGKV_WAVES fixes the wave target. */
+ * and head subset).  CTAs run in waves (two per SM on the CUDA-core kernel,
+ * one on the tensor-core one), and every wave costs a fixed start-up, tail
+ * and merge time besides its streaming, measured on B200 at about the time
+ * of 768 positions per CTA (cfg5: 103 / 124 / 139 us per layer at 1 / 2 / 3
+ * waves against 83 us of pure streaming).  So the planner takes, over 1 to 16
+ * waves, the smallest chunk whose CTAs fill exactly that many waves, and of
+ * those the one minimising waves x (chunk + 768); never below 128 positions,
+ * a multiple of the kernel's tile.  (Rounding the chunk up from total / slots
+ * can spill a few CTAs into one more wave: one 131072-position sequence with
+ * 8 KV heads made 152 CTAs for 148 slots.)  TGKV_CHUNK overrides (tests use it
+ * to force split boundaries); TGKV_WAVES fixes the wave count. */
 enum { kWaveOverheadPositions = 768 };
 
 static uint64_t count_chunks(const uint32_t* n_pos, uint32_t n_items, uint32_t chunk, uint32_t mult) {
@@ -457,17 +460,26 @@ __attribute__((visibility("hidden"))) uint32_t tgkv_pick_chunk_tiled(const uint3
     const char* e = getenv("TGKV_CHUNK");
     if (e && e[0] && atol(e) >= 1) return round_up((uint64_t)atol(e), tile);
     const uint64_t slots = slots_in ? slots_in : 296;
-    uint64_t total = 0;
-    for (uint32_t i = 0; i < n_items; i++) total += n_pos[i];
-    total *= mult;
+    uint32_t longest = 1;
+    for (uint32_t i = 0; i < n_items; i++)
+        if (n_pos[i] > longest) longest = n_pos[i];
+    const uint32_t cmax = round_up(longest < 128 ? 128 : longest, tile);
     const char* w = getenv("TGKV_WAVES");
     const uint64_t forced = (w && w[0] && atol(w) >= 1) ? (uint64_t)atol(w) : 0;
-    uint64_t best_cost = ~0ull, best = 128;
+    uint64_t best_cost = ~0ull, best = cmax;
     for (uint64_t waves = forced ? forced : 1; waves <= (forced ? forced : 16); waves++) {
-        uint64_t c = (total + slots * waves - 1) / (slots * waves);
-        if (c < 128) c = 128;
-        if (c > (1u << 30)) c = 1u << 30;
-        c = round_up(c, tile);
+        /* the smallest chunk (a multiple of tile, >= 128) whose CTAs fit in
+         * `waves` full waves: the CTA count only falls as the chunk grows */
+        const uint64_t cap = slots * waves;
+        if (count_chunks(n_pos, n_items, cmax, mult) > cap) continue;
+        uint32_t lo = 128 / tile, hi = cmax / tile;      /* in tiles; hi always fits */
+        if (lo == 0) lo = 1;
+        while (lo < hi) {
+            const uint32_t mid = lo + (hi - lo) / 2;
+            if (count_chunks(n_pos, n_items, mid * tile, mult) <= cap) hi = mid;
+            else lo = mid + 1;
+        }
+        const uint64_t c = (uint64_t)lo * tile;
         const uint64_t n = count_chunks(n_pos, n_items, (uint32_t)c, mult);
         const uint64_t cost = (n + slots - 1) / slots * (c + kWaveOverheadPositions);
         if (cost < best_cost) {
@@ -480,20 +492,26 @@ __attribute__((visibility("hidden"))) uint32_t tgkv_pick_chunk_tiled(const uint3
 
 /* Decode calls over bf16 head_dim-128 caches with a swizzled tensor map (a
  * batch's caches all have one when they are bf16 / 128) run on the
- * tensor-core decode kernel when the launch holds at least 4 sequences.
- * Measured on B200 (one CTA per SM, so each CTA's pipeline fill and drain are
- * exposed unless many chunks share the GPU): 64 ragged sequences (cfg4)
- * 0.997 of HBM against 0.86 on the CUDA-core kernel; one 131072-position
- * sequence 0.82 against 0.87; one 4096-position sequence 1739 against 2072
- * tok/s.  TGKV_DECODE_TC=1 takes every eligible call to the tensor-core
- * kernel, TGKV_DECODE_TC=0 none. */
+ * tensor-core decode kernel when the launch streams at least 262144
+ * (position, KV head, head subset) rows -- about one wave of 16-tile CTAs.
+ * That kernel keeps one CTA per SM and pays more per CTA (TMEM, the q terms,
+ * the pipeline fill) but streams HBM at full speed; small launches are
+ * latency-bound and stay on the CUDA-core kernel.  Measured on B200: 64
+ * ragged sequences (cfg4) 0.99-1.02 of HBM against 0.86; one 131072-position
+ * sequence 0.888 against 0.866; one 4096-position sequence (16384 rows)
+ * 1739 against 2072 tok/s.  TGKV_DECODE_TC=1 takes every eligible call to
+ * the tensor-core kernel, TGKV_DECODE_TC=0 none. */
 static int use_decode_tc(const TGCudaAttnCall* c, uint32_t gt) {
     const char* e = getenv("TGKV_DECODE_TC");
     const int mode = (e && e[0] == '0') ? 0 : (e && e[0] == '1') ? 1 : -1;
     if (mode == 0 || c->dtype != 1 || c->head_dim != 128 || gt > 4 ||
         !(c->table_dev != NULL || c->cache.tmap_sw != 0))
         return 0;
-    return mode == 1 || c->n_items >= 4;
+    if (mode == 1) return 1;
+    uint64_t rows = 0;
+    for (uint32_t i = 0; i < c->n_items; i++) rows += c->n_pos[i];
+    rows *= (uint64_t)c->n_heads / gt;                 /* KV heads x head subsets */
+    return rows >= 262144;
 }
 
 static int plan_attention(const TGCudaAttnCall* c, AttnPlan* pl) {
@@ -594,10 +612,9 @@ uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c) {
 
 /* Tile stealing inside a segment (tensor-core decode), opt-in with
  * TGKV_STEAL=1: the segment's CTAs take 128-position tiles from a shared
- * queue instead of streaming fixed chunks.  Measured on B200 it did not pay:
- * cfg4 0.961 against 0.977 of HBM with fixed chunks on the same box, one
- * 131072-position sequence 0.76-0.80 against 0.82 -- one atomic per tile on
- * the producer's path costs more than the imbalance it removes. */
+ * queue instead of streaming fixed chunks.  Measured on B200 it did not pay
+ * overall: cfg4 0.961 against 0.977 of HBM with fixed chunks on the same
+ * box, one 131072-position sequence in one wave 0.894 against 0.888. */
 static int steal_on(void) {
     const char* e = getenv("TGKV_STEAL");
     return e && e[0] == '1';
