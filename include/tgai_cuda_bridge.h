@@ -145,6 +145,9 @@ typedef struct {
 int      tg_cuda_kv_attn_supported(int dtype, uint32_t head_dim);
 uint64_t tg_cuda_kv_attn_scratch_bytes(const TGCudaAttnCall* c);
 uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c);
+/* (item, KV head, head subset) segments of a split-sequence call: each is
+ * finished once, so a gather receives this many arrivals per rank. */
+uint64_t tg_cuda_kv_attn_segments(const TGCudaAttnCall* c);
 /* Launches made by the last tg_cuda_kv_attention on this thread. */
 uint32_t tg_cuda_kv_attn_last_launches(void);
 /* Kernel family of this thread's last tg_cuda_kv_attention call:

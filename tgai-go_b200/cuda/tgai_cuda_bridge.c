@@ -610,6 +610,15 @@ uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c) {
     return (uint64_t)c->n_items * c->n_kv_heads * pl.n_sub * (pl.tc ? 2u : 1u);
 }
 
+/* Segments of the call: (item, KV head, head subset) triples, each finished
+ * (and, with a gather, signalled) once. */
+uint64_t tg_cuda_kv_attn_segments(const TGCudaAttnCall* c) {
+    if (use_prefill(c)) return 0;
+    AttnPlan pl;
+    if (!plan_attention(c, &pl)) return 0;
+    return (uint64_t)c->n_items * c->n_kv_heads * pl.n_sub;
+}
+
 /* Tile stealing inside a segment (tensor-core decode), opt-in with
  * TGKV_STEAL=1: the segment's CTAs take 128-position tiles from a shared
  * queue instead of streaming fixed chunks.  Measured on B200 it did not pay

@@ -548,7 +548,7 @@ static int batch_decode(TGKvBatch* b, const float* q, const float* k_new, const 
     if (g) {
         /* every rank finishes the same number of segments and signals each
          * rank once per segment */
-        g->target += g->world * (uint32_t)tg_cuda_kv_attn_counters(&call);
+        g->target += g->world * (uint32_t)tg_cuda_kv_attn_segments(&call);
         if (!tg_cuda_kv_gather_wait((const uint32_t*)(g->mem + g->flag_off), g->target, stream)) {
             set_err("%s", tg_cuda_kv_last_error());
             return 0;

@@ -153,6 +153,7 @@ PROTOS = {
     "tg_cuda_kv_attn_supported": (i32, [i32, u32]),
     "tg_cuda_kv_attn_scratch_bytes": (u64, [vp]),
     "tg_cuda_kv_attn_counters": (u64, [vp]),
+    "tg_cuda_kv_attn_segments": (u64, [vp]),
     "tg_cuda_kv_attn_last_launches": (u32, []),
     "tg_cuda_kv_attn_last_kernel": (i32, []),
     "tg_cuda_kv_attn_last_split": (u32, []),
