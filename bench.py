@@ -327,9 +327,14 @@ def run_ours(args):
     barrier()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    # Per-call events only where NCCL collectives share the step: otherwise the
+    # step is nothing but the per-layer attention launches, back to back, and
+    # events between them would break their programmatic-dependent overlap
+    # (a 13 us cfg2 call measured 21 us with them).
+    per_call_events = heads_sharded and not fused
     t0.record(stream)
     for s_ in range(args.steps):
-        step(ev[s_ * layers:(s_ + 1) * layers])
+        step(ev[s_ * layers:(s_ + 1) * layers] if per_call_events else None)
     t1.record(stream)
     barrier()
     clock = clocks.stop()
@@ -338,9 +343,12 @@ def run_ours(args):
         lib.tg_cuda_kv_attn_last_kernel(), "?")
     ms = t0.elapsed_time(t1) / args.steps
     ms_max = max_over_ranks(ms)
-    call_ms = [a.elapsed_time(b) for a, b in ev]
     algo = sum(attn_bytes(lens_step[0] + s_, nh, nkv, hd) for s_ in range(args.steps)) * layers
-    kernel_gbs = algo / (sum(call_ms) / 1000.0) / 1e9
+    if per_call_events:
+        call_ms = sum(a.elapsed_time(b) for a, b in ev)
+    else:
+        call_ms = ms * args.steps                      # the timed region is the calls
+    kernel_gbs = algo / (call_ms / 1000.0) / 1e9
     per_launch_bytes = algo / (args.steps * layers)
 
     # ---- end to end: host buffers, copies inside the timed region
@@ -438,8 +446,11 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": kernel_gbs, "peak": peak, "unit": "GB/s",
                          "frac": kernel_gbs / peak, "traffic": traffic,
                          "peak_source": peak_kind,
-                         "kernel": "tg_kv_batch_decode per layer (append + split-sequence "
-                                   "attention launches), CUDA events on the launch stream",
+                         "kernel": ("tg_kv_batch_decode per layer (append fused into the "
+                                    "split-sequence attention launch): CUDA events on the launch "
+                                    "stream, " + ("around every call" if per_call_events else
+                                                  "around the timed region, which holds only "
+                                                  "these calls")),
                          "algorithmic_bytes_per_launch": per_launch_bytes},
             "gpu_launches": timed_launches,
             "clocks": clock,

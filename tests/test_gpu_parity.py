@@ -348,27 +348,31 @@ def test_batched_decode_fused_append_geometries(cuda, devbuf, dtype, nh, nkv, hd
         lib.tg_kv_destroy(c)
 
 
-def test_batch_decode_pinned_host_buffers_on_a_stream(cuda, devbuf):
+@pytest.mark.parametrize("n_seq", [3, 24])
+def test_batch_decode_pinned_host_buffers_on_a_stream(cuda, devbuf, n_seq):
     """tg_kv_batch_decode_host with page-locked buffers on a non-default
-    stream, several steps back to back: uploads go through the plan's two
-    staging slots on its copy stream, outputs straight from the kernel into
-    the pinned out buffers."""
+    stream, several steps back to back.  3 sequences (36 KB of inputs): the
+    kernel reads the pinned inputs in place and writes the pinned outputs;
+    24 sequences (288 KB): uploads through the plan's two staging slots on its
+    copy stream, outputs still straight into the pinned out buffers."""
     import torch
     lib = cuda
     nh, nkv, hd, steps = 16, 4, 128, 5
     kvd = nkv * hd
     caches = []
-    for i, L in enumerate([33, 1500, 4000]):
+    lens = [[33, 1500, 4000][i % 3] + 7 * i for i in range(n_seq)]
+    for i, L in enumerate(lens):
         _, k, v = synth_qkv(520 + i, L, nh, nkv, hd)
-        caches.append(make_cache(lib, devbuf, 4100, nkv, hd, 1, k, v))
-    b = lib.tg_kv_batch_create((C.c_void_p * 3)(*caches), 3, nh)
-    qs = [torch.from_numpy(O.normal(3 * nh * hd, 30 + s).reshape(3, nh, hd)).pin_memory()
+        caches.append(make_cache(lib, devbuf, 4400, nkv, hd, 1, k, v))
+    n = n_seq
+    b = lib.tg_kv_batch_create((C.c_void_p * n)(*caches), n, nh)
+    qs = [torch.from_numpy(O.normal(n * nh * hd, 30 + s).reshape(n, nh, hd)).pin_memory()
           for s in range(steps)]
-    ks = [torch.from_numpy(O.normal(3 * kvd, 40 + s).reshape(3, kvd)).pin_memory()
+    ks = [torch.from_numpy(O.normal(n * kvd, 40 + s).reshape(n, kvd)).pin_memory()
           for s in range(steps)]
-    vs = [torch.from_numpy(O.normal(3 * kvd, 50 + s).reshape(3, kvd)).pin_memory()
+    vs = [torch.from_numpy(O.normal(n * kvd, 50 + s).reshape(n, kvd)).pin_memory()
           for s in range(steps)]
-    outs = [torch.zeros(3, nh, hd).pin_memory() for _ in range(steps)]
+    outs = [torch.zeros(n, nh, hd).pin_memory() for _ in range(steps)]
     assert lib.tg_cuda_kv_host_device_ptr(outs[0].data_ptr())
     assert not lib.tg_cuda_kv_host_device_ptr(np.zeros(4, np.float32).ctypes.data)
     stream = lib.tg_cuda_kv_stream_create()
@@ -380,12 +384,12 @@ def test_batch_decode_pinned_host_buffers_on_a_stream(cuda, devbuf):
     assert lib.tg_cuda_kv_device_error() == 0
     for i, c in enumerate(caches):
         L = lib.tg_kv_len(c)
-        kvc = O.bf16_to_f32(cache_rows(lib, c, 1, 4100, kvd))
+        rows = cache_rows(lib, c, 1, 4400, kvd)
+        kvc = O.bf16_to_f32(rows)
         for s in range(steps):
-            n = L - steps + s + 1           # positions step s attended
-            assert np.array_equal(cache_rows(lib, c, 1, 4100, kvd)[0, n - 1],
-                                  O.f32_to_bf16(ks[s][i].numpy()))
-            eng = O.attention_engine(qs[s][i].numpy(), kvc, nh, nkv, hd, 1, n - 1, n, 4100)
+            m = L - steps + s + 1           # positions step s attended
+            assert np.array_equal(rows[0, m - 1], O.f32_to_bf16(ks[s][i].numpy()))
+            eng = O.attention_engine(qs[s][i].numpy(), kvc, nh, nkv, hd, 1, m - 1, m, 4400)
             assert rel_head_err(outs[s][i].numpy(), eng[0]) < 1e-5, (i, s)
     lib.tg_cuda_kv_stream_destroy(stream)
     lib.tg_kv_batch_destroy(b)
