@@ -351,10 +351,9 @@ def test_batched_decode_fused_append_geometries(cuda, devbuf, dtype, nh, nkv, hd
 @pytest.mark.parametrize("n_seq", [3, 24])
 def test_batch_decode_pinned_host_buffers_on_a_stream(cuda, devbuf, n_seq):
     """tg_kv_batch_decode_host with page-locked buffers on a non-default
-    stream, several steps back to back.  3 sequences (36 KB of inputs): the
-    kernel reads the pinned inputs in place and writes the pinned outputs;
-    24 sequences (288 KB): uploads through the plan's two staging slots on its
-    copy stream, outputs still straight into the pinned out buffers."""
+    stream, several steps back to back: uploads go through the plan's two
+    staging slots on its copy stream, outputs straight from the kernel into
+    the pinned out buffers (3 and 24 sequences)."""
     import torch
     lib = cuda
     nh, nkv, hd, steps = 16, 4, 128, 5

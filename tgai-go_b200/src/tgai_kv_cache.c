@@ -576,27 +576,11 @@ int tg_kv_batch_decode_gather(TGKvBatch* b, const float* q, const float* k_new,
  * them straight from the kernel (no copy; the stores overlap the streaming),
  * else they are copied back on `stream` -- with g, the whole gathered buffer
  * is copied.  Synchronising `stream` covers the results either way. */
-/* Inputs of at most this many bytes, in page-locked memory, are read by the
- * attention launch in place. */
-enum { kDirectInputBytes = 64 * 1024 };
-
 static int batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_host,
                              const float* v_host, float* out_host, TGKvGather* g, void* stream) {
     if (!b || !q_host || !k_host || !v_host || !out_host) { set_err("null argument"); return 0; }
     const uint64_t qb = (uint64_t)b->n * b->n_heads * b->head_dim * 4;
     const uint64_t kb = (uint64_t)b->n * b->kv_dim * 4;
-    if (!g && qb + 2 * kb <= kDirectInputBytes) {
-        /* Small page-locked inputs, no gather: the kernel reads q and the new
-         * K/V rows in place and stores the outputs into out_host, so the call
-         * is one launch with no copy and no cross-stream event, and
-         * consecutive calls keep their programmatic-dependent overlap.  (Large
-         * inputs are staged: every chunk of a row re-reads its q.) */
-        const float* qd = (const float*)tg_cuda_kv_host_device_ptr(q_host);
-        const float* kd = (const float*)tg_cuda_kv_host_device_ptr(k_host);
-        const float* vd = (const float*)tg_cuda_kv_host_device_ptr(v_host);
-        float* od = (float*)tg_cuda_kv_host_device_ptr(out_host);
-        if (qd && kd && vd && od) return batch_decode(b, qd, kd, vd, od, NULL, stream);
-    }
     const uint64_t need = 2 * qb + 2 * kb + 64;
     if (!b->copy_stream) {
         b->copy_stream = tg_cuda_kv_stream_create();
