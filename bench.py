@@ -11,7 +11,8 @@ sequence per step, all layers) and achieved HBM GB/s of the attention launches.
                   [--workload cfg4|cfg5|cfg2]
 
 N > 1 runs under torchrun, one rank per GPU.  cfg4 shards by sequences (each
-rank owns its own 64; weak scaling, no collective on the data path).  cfg5
+rank owns its own 64 with the length profile of the 1-GPU run; weak scaling,
+no collective on the data path).  cfg5
 (one 131072-token sequence) shards KV-head groups and all-gathers the per-head
 outputs with NCCL after every layer (strong scaling).
 
@@ -234,7 +235,9 @@ def run_ours(args):
         mine = shard.lpt_partition(all_lens, world)[rank]
         lens0 = all_lens[mine]
     else:
-        lens0 = lengths_for(wl, args.seed, 0 if heads_sharded else rank)
+        # weak scaling: every rank serves its own 64 sequences (values seeded
+        # per rank) with the same length profile, so per-GPU work is fixed as N grows
+        lens0 = lengths_for(wl, args.seed, 0)
     n_seq = len(lens0)
     kvd = nkv * hd
     e2e_steps = 0 if args.no_e2e else args.steps
