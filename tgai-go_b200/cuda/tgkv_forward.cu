@@ -49,6 +49,24 @@ __device__ __forceinline__ void prefetch_row(const float* w, uint32_t n) {
     for (uint32_t i = (threadIdx.x & 31) * 32; i < n; i += 32 * 32)
         asm volatile("prefetch.global.L2 [%0];" ::"l"(w + i));
 }
+// Share `part` of `parts` of [pf, pf + n floats) prefetched into L2 by this
+// CTA's threads: the weights of a LATER launch on the stream.  A decode
+// step's kernels are short and latency-bound, with HBM bandwidth to spare;
+// pulling the next kernel's weights into L2 meanwhile leaves that kernel
+// L2 latency instead of HBM latency.  Every line prefetched lies inside
+// [pf, pf + n).
+__device__ __forceinline__ void prefetch_share(const float* pf, uint64_t n, uint32_t part,
+                                               uint32_t parts) {
+    if (!pf || n == 0) return;
+    const uint64_t lines = (n + 31) / 32;
+    const uint64_t per = (lines + parts - 1) / parts;
+    const uint64_t l0 = (uint64_t)part * per;
+    const uint64_t l1 = l0 + per < lines ? l0 + per : lines;
+    for (uint64_t l = l0 + threadIdx.x; l < l1; l += blockDim.x)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(pf + l * 32));
+}
+__device__ __forceinline__ uint32_t cta_rank() { return blockIdx.x + gridDim.x * blockIdx.y; }
+__device__ __forceinline__ uint32_t cta_count() { return gridDim.x * gridDim.y; }
 
 __global__ void __launch_bounds__(256) embed_kernel(float* x, const float* emb, const int32_t* ids,
                                                    uint32_t d, uint32_t rows, int32_t unk) {
@@ -223,91 +241,160 @@ __global__ void __launch_bounds__(256) combine_kernel(float* x, const float* y,
 // is bound by how fast the weights stream from HBM.
 constexpr int kDecRows = 4;
 
-// Rows [0, R) of x (row stride ldx, K columns) into sx [R][K]; with g, each
-// row becomes x * (1/sqrt(mean(x^2) + eps)) * g.  Ends with __syncthreads.
-__device__ __forceinline__ void stage_rows(float* sx, float* s_scale, const float* x,
-                                           uint64_t ldx, uint32_t R, uint32_t K,
-                                           const float* g, float eps) {
+// Shared-memory layout of a decode CTA: the per-warp partial sums of squares
+// [32][kDecRows], the norm weight g [K], then the staged rows sx [R][K].
+__host__ __device__ constexpr uint32_t dec_red_floats() { return 32 * kDecRows; }
+
+// Rows [0, R) of x (row stride ldx, K columns) staged in shared memory and
+// returned as sx [R][K]; with g, each row becomes x * (1/sqrt(mean(x^2) +
+// eps)) * g.  One pass brings x and g in (all loads of a thread in flight
+// together) and sums each thread's squares in registers; the block then
+// reduces the sums (warp shuffles, one barrier) and every thread rescales the
+// elements it staged.  Ends with __syncthreads.
+__device__ __forceinline__ float* stage_rows(float* dsm, const float* x, uint64_t ldx, uint32_t R,
+                                             uint32_t K, const float* g, float eps) {
+    float* red = dsm;
+    float* sg = dsm + dec_red_floats();
+    float* sx = sg + K;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (uint32_t r = 0; r < R; ++r)
-        for (uint32_t i = threadIdx.x * 4; i < K; i += blockDim.x * 4)
-            *reinterpret_cast<float4*>(sx + r * K + i) =
-                *reinterpret_cast<const float4*>(x + r * ldx + i);
-    __syncthreads();
-    if (!g) return;
-    if (warp < R) {
-        float ss = 0.f;
-        for (uint32_t i = lane; i < K; i += 32) ss = fmaf(sx[warp * K + i], sx[warp * K + i], ss);
-        ss = warp_sum(ss);
-        if (lane == 0) s_scale[warp] = 1.0f / sqrtf(ss / (float)K + eps);
+    float ss[kDecRows];
+#pragma unroll
+    for (int r = 0; r < kDecRows; ++r) ss[r] = 0.f;
+    for (uint32_t i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
+        if (g) *reinterpret_cast<float4*>(sg + i) = *reinterpret_cast<const float4*>(g + i);
+#pragma unroll
+        for (int r = 0; r < kDecRows; ++r) {
+            if ((uint32_t)r >= R) break;
+            const float4 v = *reinterpret_cast<const float4*>(x + r * ldx + i);
+            *reinterpret_cast<float4*>(sx + r * K + i) = v;
+            ss[r] = fmaf(v.x, v.x, ss[r]);
+            ss[r] = fmaf(v.y, v.y, ss[r]);
+            ss[r] = fmaf(v.z, v.z, ss[r]);
+            ss[r] = fmaf(v.w, v.w, ss[r]);
+        }
+    }
+    if (g) {
+#pragma unroll
+        for (int r = 0; r < kDecRows; ++r) {
+            const float t = warp_sum(ss[r]);
+            if (lane == 0) red[warp * kDecRows + r] = t;
+        }
     }
     __syncthreads();
-    for (uint32_t r = 0; r < R; ++r) {
-        const float sc = s_scale[r];
-        for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) sx[r * K + i] = sx[r * K + i] * sc * g[i];
+    if (!g) return sx;
+    float sc[kDecRows];
+#pragma unroll
+    for (int r = 0; r < kDecRows; ++r) {
+        float t = 0.f;
+        for (uint32_t w = 0; w < (blockDim.x >> 5); ++w) t += red[w * kDecRows + r];
+        sc[r] = 1.0f / sqrtf(t / (float)K + eps);
+    }
+    for (uint32_t i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
+        const float4 g4 = *reinterpret_cast<const float4*>(sg + i);
+#pragma unroll
+        for (int r = 0; r < kDecRows; ++r) {
+            if ((uint32_t)r >= R) break;
+            float4 v = *reinterpret_cast<const float4*>(sx + r * K + i);
+            v.x = v.x * sc[r] * g4.x;
+            v.y = v.y * sc[r] * g4.y;
+            v.z = v.z * sc[r] * g4.z;
+            v.w = v.w * sc[r] * g4.w;
+            *reinterpret_cast<float4*>(sx + r * K + i) = v;
+        }
     }
     __syncthreads();
+    return sx;
 }
 
-// acc[r] = W[n] . sx[r] for the rows of this warp's output n (all lanes hold
-// the sums on return).  Eight 16-byte weight loads per lane are issued before
-// their products are formed.
-__device__ __forceinline__ void row_dots(const float* __restrict__ w, const float* sx, uint32_t R,
-                                         uint32_t K, float* acc) {
+// acc[n][r] = W_n . x_n[r] for NW weight rows of one warp (x_n holds R rows
+// of K floats; all lanes hold the sums on return).  A lane owns columns
+// lane*4 + 128*m; the 16-byte loads of kU consecutive m of every row are
+// issued (the last batch predicated) before any product is formed, so a row
+// costs ceil(K / (128 kU)) memory round trips.  Large kU suits launches with
+// few rows per SM; small kU keeps registers low so that many CTAs stay
+// resident.  Each lane sums its columns in increasing m and the warp then
+// reduces by shuffles, whatever kU is.
+template <int NW, int kU>
+__device__ __forceinline__ void row_dots_n(const float* const (&w)[NW],
+                                           const float* const (&x)[NW], uint32_t R, uint32_t K,
+                                           float (&acc)[NW][kDecRows]) {
     const uint32_t lane = threadIdx.x & 31;
 #pragma unroll
-    for (int r = 0; r < kDecRows; ++r) acc[r] = 0.f;
-    constexpr int kU = 8;
-    uint32_t i = lane * 4;
-    for (; i + (kU - 1) * 128 < K; i += kU * 128) {
-        float4 a4[kU];
+    for (int n = 0; n < NW; ++n)
 #pragma unroll
-        for (int u = 0; u < kU; ++u) a4[u] = __ldg(reinterpret_cast<const float4*>(w + i + u * 128));
+        for (int r = 0; r < kDecRows; ++r) acc[n][r] = 0.f;
+    for (uint32_t i0 = lane * 4; i0 < K; i0 += kU * 128) {
+        float4 a4[NW][kU];
 #pragma unroll
         for (int u = 0; u < kU; ++u)
 #pragma unroll
-            for (int r = 0; r < kDecRows; ++r)
-                if ((uint32_t)r < R)
-                    acc[r] = dot4(a4[u], *reinterpret_cast<const float4*>(sx + r * K + i + u * 128),
-                                  acc[r]);
-    }
-    for (; i < K; i += 128) {
-        const float4 a4 = __ldg(reinterpret_cast<const float4*>(w + i));
+            for (int n = 0; n < NW; ++n)
+                a4[n][u] = i0 + u * 128 < K
+                               ? __ldg(reinterpret_cast<const float4*>(w[n] + i0 + u * 128))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int r = 0; r < kDecRows; ++r)
-            if ((uint32_t)r < R) acc[r] = dot4(a4, *reinterpret_cast<const float4*>(sx + r * K + i), acc[r]);
+        for (int u = 0; u < kU; ++u) {
+            if (i0 + u * 128 >= K) break;
+#pragma unroll
+            for (int n = 0; n < NW; ++n)
+#pragma unroll
+                for (int r = 0; r < kDecRows; ++r)
+                    if ((uint32_t)r < R)
+                        acc[n][r] = dot4(a4[n][u],
+                                         *reinterpret_cast<const float4*>(x[n] + r * K + i0 + u * 128),
+                                         acc[n][r]);
+        }
     }
 #pragma unroll
-    for (int r = 0; r < kDecRows; ++r) acc[r] = warp_sum(acc[r]);
+    for (int n = 0; n < NW; ++n)
+#pragma unroll
+        for (int r = 0; r < kDecRows; ++r) acc[n][r] = warp_sum(acc[n][r]);
+}
+
+// Lane r < R picks row r's sum.
+__device__ __forceinline__ float pick_row(const float (&a)[kDecRows]) {
+    const uint32_t lane = threadIdx.x & 31;
+    float v = a[0];
+#pragma unroll
+    for (int r = 1; r < kDecRows; ++r)
+        if ((uint32_t)r == lane) v = a[r];
+    return v;
 }
 
 enum { kStore = 0, kAdd = 1, kSwiglu = 2 };
 
-template <int MODE>
+template <int MODE, int KU = 8>
 __global__ void __launch_bounds__(256) dec_gemv_kernel(const float* __restrict__ w, const float* x,
                                                        uint64_t ldx, const float* g,
                                                        const float* bias, float* out,
                                                        uint64_t ldo, uint32_t R, uint32_t N,
-                                                       uint32_t K, int clamp) {
+                                                       uint32_t K, int clamp, const float* pf,
+                                                       uint64_t pf_n) {
     extern __shared__ __align__(16) float dsm[];
-    float* sx = dsm + kDecRows;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (uint32_t n = blockIdx.x * 8 + warp; n < N; n += gridDim.x * 8) {
+    // the warp's first row only: a launch whose rows exceed the L2 (the LM
+    // head) would otherwise evict its own prefetched lines before use
+    if (const uint32_t n = blockIdx.x * 8 + warp; n < N) {
         prefetch_row(w + (uint64_t)n * K, K);
         if (MODE == kSwiglu) prefetch_row(w + (uint64_t)(N + n) * K, K);
     }
+    prefetch_share(pf, pf_n, cta_rank(), cta_count());
     pdl_wait();
     pdl_trigger();
-    stage_rows(sx, dsm, x, ldx, R, K, g, 1e-6f);
+    const float* sx = stage_rows(dsm, x, ldx, R, K, g, 1e-6f);
     for (uint32_t n = blockIdx.x * 8 + warp; n < N; n += gridDim.x * 8) {
-        float a[kDecRows], b[kDecRows] = {};
-        row_dots(w + (uint64_t)n * K, sx, R, K, a);
-        if (MODE == kSwiglu) row_dots(w + (uint64_t)(N + n) * K, sx, R, K, b);
+        float v, vb = 0.f;
+        if (MODE == kSwiglu) {
+            float ab[2][kDecRows];
+            row_dots_n<2, 4>({w + (uint64_t)n * K, w + (uint64_t)(N + n) * K}, {sx, sx}, R, K, ab);
+            v = pick_row(ab[0]);
+            vb = pick_row(ab[1]);
+        } else {
+            float a[1][kDecRows];
+            row_dots_n<1, KU>({w + (uint64_t)n * K}, {sx}, R, K, a);
+            v = pick_row(a[0]);
+        }
         if (lane < R) {                      // lane r writes row r's output
-            float v = a[0], vb = b[0];
-#pragma unroll
-            for (int r = 1; r < kDecRows; ++r)
-                if ((uint32_t)r == lane) { v = a[r]; vb = b[r]; }
             float* o = out + lane * ldo + n;
             if (MODE == kStore) {
                 *o = bias ? v + bias[n] : v;
@@ -327,39 +414,45 @@ __global__ void __launch_bounds__(256) dec_gemv_kernel(const float* __restrict__
 // rows of token r go to position pos0 + r of the fp32 cache [2][max_seq]
 // [kv_dim].  The rotation is the KV path's (tgkv_kernels.cu rope_append), so
 // the bits equal a separate RoPE launch's.
-__global__ void __launch_bounds__(256) dec_qkv_rope_kernel(const float* __restrict__ w,
+__global__ void __launch_bounds__(384, 1) dec_qkv_rope_kernel(const float* __restrict__ w,
                                                            const float* x, const float* g,
                                                            const float* bias, const float* cs,
                                                            const float* sn, float* q_out,
                                                            float* kvc, uint32_t R, uint32_t d,
                                                            uint32_t q_dim, uint32_t kv_dim,
                                                            uint32_t hd, uint32_t pos0,
-                                                           uint32_t max_seq) {
+                                                           uint32_t max_seq, const float* pf,
+                                                           uint64_t pf_n) {
     extern __shared__ __align__(16) float dsm[];
-    float* sx = dsm + kDecRows;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t npair = (q_dim + 2 * kv_dim) / 2;
-    for (uint32_t m = blockIdx.x * 8 + warp; m < npair; m += gridDim.x * 8)
+    const uint32_t nw = blockDim.x >> 5;
+    for (uint32_t m = blockIdx.x * nw + warp; m < npair; m += gridDim.x * nw)
         prefetch_row(w + (uint64_t)(2 * m) * d, 2 * d);
+    prefetch_share(pf, pf_n, cta_rank(), cta_count());
     pdl_wait();
     pdl_trigger();
-    stage_rows(sx, dsm, x, d, R, d, g, 1e-6f);
-    for (uint32_t m = blockIdx.x * 8 + warp; m < npair; m += gridDim.x * 8) {
+    const float* sx = stage_rows(dsm, x, d, R, d, g, 1e-6f);
+    for (uint32_t m = blockIdx.x * nw + warp; m < npair; m += gridDim.x * nw) {
         const uint32_t n0 = 2 * m;
-        float a[kDecRows], b[kDecRows];
-        row_dots(w + (uint64_t)n0 * d, sx, R, d, a);
-        row_dots(w + (uint64_t)(n0 + 1) * d, sx, R, d, b);
+        // the epilogue's bias and rotation factors, loaded ahead of the weight rows
+        const bool rot = n0 < q_dim + kv_dim;
+        const uint32_t half = hd >> 1, col = n0 < q_dim ? n0 : n0 - q_dim;
+        float b0 = 0.f, b1 = 0.f, c = 0.f, sn_ = 0.f;
         if (lane < R) {
-            float v0 = a[0], v1 = b[0];
-#pragma unroll
-            for (int r = 1; r < kDecRows; ++r)
-                if ((uint32_t)r == lane) { v0 = a[r]; v1 = b[r]; }
-            if (bias) { v0 += bias[n0]; v1 += bias[n0 + 1]; }
+            if (bias) { b0 = bias[n0]; b1 = bias[n0 + 1]; }
+            if (rot) {
+                c = cs[(uint64_t)(pos0 + lane) * half + (col % hd) / 2];
+                sn_ = sn[(uint64_t)(pos0 + lane) * half + (col % hd) / 2];
+            }
+        }
+        float ab[2][kDecRows];
+        row_dots_n<2, 12>({w + (uint64_t)n0 * d, w + (uint64_t)(n0 + 1) * d}, {sx, sx}, R, d, ab);
+        float v0 = pick_row(ab[0]), v1 = pick_row(ab[1]);
+        if (lane < R) {
+            if (bias) { v0 += b0; v1 += b1; }
             const uint64_t pos = pos0 + lane;
-            if (n0 < q_dim + kv_dim) {
-                const uint32_t col = n0 < q_dim ? n0 : n0 - q_dim;
-                const uint32_t half = hd >> 1;
-                const float c = cs[pos * half + (col % hd) / 2], sn_ = sn[pos * half + (col % hd) / 2];
+            if (rot) {
                 const float r0 = __fmaf_rn(v0, c, -__fmul_rn(v1, sn_));
                 const float r1 = __fmaf_rn(v0, sn_, __fmul_rn(v1, c));
                 float* dst = n0 < q_dim ? q_out + (uint64_t)lane * q_dim + col
@@ -377,16 +470,18 @@ __global__ void __launch_bounds__(256) dec_qkv_rope_kernel(const float* __restri
 
 // Expert W3, the k-ordered weighted sum and the residual of a decode step:
 // x[r][i] += sum_k top_w[r][k] * (W3[e_k][i] . h[r * na + k]).  One warp per
-// row i; the dot products of two k at a time share one load loop so that 16
-// weight loads per lane are in flight.
-__global__ void __launch_bounds__(256) dec_w3_combine_kernel(const float* __restrict__ w3,
+// row i; the dot products of two k at a time share one load batch (24 weight
+// loads per lane in flight).
+__global__ void __launch_bounds__(384, 1) dec_w3_combine_kernel(const float* __restrict__ w3,
                                                              const float* __restrict__ h,
                                                              const int32_t* top_ids,
                                                              const float* top_w, float* x,
                                                              uint32_t R, uint32_t d, uint32_t dff,
-                                                             uint32_t ne, uint32_t na) {
+                                                             uint32_t ne, uint32_t na,
+                                                             const float* pf, uint64_t pf_n) {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t i = blockIdx.x * 8 + warp;
+    const uint32_t i = blockIdx.x * (blockDim.x >> 5) + warp;
+    prefetch_share(pf, pf_n, cta_rank(), cta_count());
     pdl_wait();
     pdl_trigger();
     if (i >= d) return;
@@ -396,36 +491,19 @@ __global__ void __launch_bounds__(256) dec_w3_combine_kernel(const float* __rest
             const int e0 = top_ids[r * na + k];
             const int e1 = k + 1 < na ? top_ids[r * na + k + 1] : -1;
             const bool v0 = e0 >= 0 && (uint32_t)e0 < ne, v1 = e1 >= 0 && (uint32_t)e1 < ne;
-            const float* w0 = w3 + ((uint64_t)(v0 ? e0 : 0) * d + i) * dff;
-            const float* w1 = w3 + ((uint64_t)(v1 ? e1 : 0) * d + i) * dff;
             const float* h0 = h + (uint64_t)(r * na + k) * dff;
-            const float* h1 = h0 + dff;
-            float a0 = 0.f, a1 = 0.f;
-            constexpr int kU = 8;
-            uint32_t j = lane * 4;
-            for (; j + (kU - 1) * 128 < dff; j += kU * 128) {
-                float4 p0[kU], p1[kU];
-#pragma unroll
-                for (int u = 0; u < kU; ++u) {
-                    p0[u] = v0 ? __ldg(reinterpret_cast<const float4*>(w0 + j + u * 128))
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-                    p1[u] = v1 ? __ldg(reinterpret_cast<const float4*>(w1 + j + u * 128))
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-#pragma unroll
-                for (int u = 0; u < kU; ++u) {
-                    a0 = dot4(p0[u], *reinterpret_cast<const float4*>(h0 + j + u * 128), a0);
-                    if (v1) a1 = dot4(p1[u], *reinterpret_cast<const float4*>(h1 + j + u * 128), a1);
-                }
+            const float* w0 = w3 + ((uint64_t)(v0 ? e0 : 0) * d + i) * dff;
+            float a0, a1 = 0.f;
+            if (v1) {
+                float a[2][kDecRows];
+                row_dots_n<2, 12>({w0, w3 + ((uint64_t)e1 * d + i) * dff}, {h0, h0 + dff}, 1, dff, a);
+                a0 = a[0][0];
+                a1 = a[1][0];
+            } else {
+                float a[1][kDecRows];
+                row_dots_n<1, 12>({w0}, {h0}, 1, dff, a);
+                a0 = a[0][0];
             }
-            for (; j < dff; j += 128) {
-                if (v0) a0 = dot4(__ldg(reinterpret_cast<const float4*>(w0 + j)),
-                                  *reinterpret_cast<const float4*>(h0 + j), a0);
-                if (v1) a1 = dot4(__ldg(reinterpret_cast<const float4*>(w1 + j)),
-                                  *reinterpret_cast<const float4*>(h1 + j), a1);
-            }
-            a0 = warp_sum(a0);
-            a1 = warp_sum(a1);
             if (v0) ot = fmaf(top_w[r * na + k], a0, ot);
             if (v1) ot = fmaf(top_w[r * na + k + 1], a1, ot);
         }
@@ -439,68 +517,84 @@ __global__ void __launch_bounds__(256) dec_w3_combine_kernel(const float* __rest
 // arithmetic in every CTA, so all agree -- then streams W1/W2 rows of its
 // expert e_k: h[p][j] = silu(W1[e][j] . ln) * (W2[e][j] . ln), one warp per j.
 // The CTAs of column 0 publish top_ids / top_w for the W3 launch.
-__global__ void __launch_bounds__(256) dec_moe_w12_kernel(const float* x, const float* g,
+__global__ void __launch_bounds__(256, 2) dec_moe_w12_kernel(const float* x, const float* g,
                                                           const float* __restrict__ router,
                                                           const float* bias,
                                                           const float* __restrict__ w12,
                                                           int32_t* top_ids, float* top_w, float* h,
                                                           uint32_t d, uint32_t dff, uint32_t ne,
-                                                          uint32_t na) {
+                                                          uint32_t na, const float* w3_pf) {
     extern __shared__ __align__(16) float dsm[];
     __shared__ float slog[16];
     __shared__ int s_ids[8];
-    __shared__ float s_w[8];
     const uint32_t p = blockIdx.y, r = p / na, kk = p % na;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (uint32_t e = warp; e < ne; e += 8) prefetch_row(router + (uint64_t)e * d, d);
     pdl_wait();
     pdl_trigger();
-    float* sx = dsm + kDecRows;
-    stage_rows(sx, dsm, x + (uint64_t)r * d, d, 1, d, g, 1e-6f);
+    const float* sx = stage_rows(dsm, x + (uint64_t)r * d, d, 1, d, g, 1e-6f);
     for (uint32_t e = warp; e < ne; e += 8) {
-        float a[kDecRows];
-        row_dots(router + (uint64_t)e * d, sx, 1, d, a);
-        if (lane == 0) slog[e] = bias ? a[0] + bias[e] : a[0];
+        float a[1][kDecRows];
+        row_dots_n<1, 12>({router + (uint64_t)e * d}, {sx}, 1, d, a);
+        if (lane == 0) slog[e] = bias ? a[0][0] + bias[e] : a[0][0];
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int ids[8];
-        float vals[8];
+    if (warp == 0) {
+        // The engine's top-k: for k = 0..na-1 the first expert (lowest index)
+        // of the largest logit above -1e30 not chosen yet, else -1 with
+        // -1e30; lane k keeps choice k.  Argmax over the warp by shuffles on
+        // the order (larger value, then lower index; no candidate last).
+        const float v = lane < ne ? slog[lane] : 0.f;
+        bool used = false;
+        float my_v = -1e30f;
+        int my_id = -1;
         for (uint32_t k = 0; k < na; ++k) {
-            int best = -1;
-            float best_v = -1e30f;
-            for (uint32_t e = 0; e < ne; ++e) {
-                bool used = false;
-                for (uint32_t q = 0; q < k; ++q) used |= ids[q] == (int)e;
-                if (used) continue;
-                if (slog[e] > best_v) { best_v = slog[e]; best = (int)e; }
+            const bool cand = lane < ne && !used && v > -1e30f;
+            float bv = cand ? v : -1e30f;
+            int bi = cand ? (int)lane : -1;
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+                    bv = ov;
+                    bi = oi;
+                }
             }
-            ids[k] = best;
-            vals[k] = best_v;
+            if (bi >= 0 && (uint32_t)bi == lane) used = true;
+            if (lane == k) {
+                my_v = bi >= 0 ? bv : -1e30f;
+                my_id = bi;
+            }
         }
-        float mx = vals[0];
-        for (uint32_t k = 1; k < na; ++k) if (vals[k] > mx) mx = vals[k];
+        // softmax over the chosen logits: max (lanes >= na hold -1e30, below
+        // or equal to every choice), then the exponentials summed in k order
+        float mx = my_v;
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float ek = lane < na ? expf(my_v - mx) : 0.f;
         float ss = 0.f;
-        for (uint32_t k = 0; k < na; ++k) { vals[k] = expf(vals[k] - mx); ss += vals[k]; }
-        for (uint32_t k = 0; k < na; ++k) {
-            s_ids[k] = ids[k];
-            s_w[k] = vals[k] / ss;
-        }
-        if (blockIdx.x == 0 && kk == 0)
-            for (uint32_t k = 0; k < na; ++k) {
-                top_ids[r * na + k] = s_ids[k];
-                top_w[r * na + k] = s_w[k];
+        for (uint32_t k = 0; k < na; ++k) ss += __shfl_sync(0xffffffffu, ek, k);
+        if (lane < na) {
+            s_ids[lane] = my_id;
+            if (blockIdx.x == 0 && kk == 0) {
+                top_ids[r * na + lane] = my_id;
+                top_w[r * na + lane] = ek / ss;
             }
+        }
     }
     __syncthreads();
     const int e = s_ids[kk];
-    const uint32_t j = blockIdx.x * 8 + warp;
-    if (e < 0 || (uint32_t)e >= ne || j >= dff) return;
-    const float* wa = w12 + ((uint64_t)e * 2 * dff + j) * d;
-    float a[kDecRows], b[kDecRows];
-    row_dots(wa, sx, 1, d, a);
-    row_dots(wa + (uint64_t)dff * d, sx, 1, d, b);
-    if (lane == 0) h[(uint64_t)p * dff + j] = silu_mul(a[0], b[0]);
+    if (e < 0 || (uint32_t)e >= ne) return;
+    // the W3 launch reads expert e's [d][dff] rows: this column of CTAs pulls them into L2
+    if (w3_pf) prefetch_share(w3_pf + (uint64_t)e * d * dff, (uint64_t)d * dff, blockIdx.x, gridDim.x);
+    const float* we = w12 + (uint64_t)e * 2 * dff * d;
+    for (uint32_t j = blockIdx.x * 8 + warp; j < dff; j += gridDim.x * 8) {
+        const float* wa = we + (uint64_t)j * d;
+        float ab[2][kDecRows];
+        row_dots_n<2, 12>({wa, wa + (uint64_t)dff * d}, {sx, sx}, 1, d, ab);
+        if (lane == 0) h[(uint64_t)p * dff + j] = silu_mul(ab[0][0], ab[1][0]);
+    }
 }
 
 inline uint32_t blocks_for(uint64_t n, uint32_t per) { return (uint32_t)((n + per - 1) / per); }
@@ -577,7 +671,19 @@ extern "C" int tgkv_fwd_moe_combine(float* x, const float* y, const int32_t* top
 
 
 // ---- decode launchers
-static size_t dec_smem(uint32_t R, uint32_t K) { return (size_t)(kDecRows + kDecRows * 16 + R * K) * 4; }
+static size_t dec_smem(uint32_t R, uint32_t K) {
+    return ((size_t)dec_red_floats() + K + (size_t)R * K) * 4;
+}
+
+// SMs of the current device (grids of the streaming launches are sized to
+// what stays resident, so that no CTA waits for a second wave).
+static uint32_t sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        return 148;
+    return (uint32_t)n;
+}
 
 static bool pdl_on() {
     static const bool on = [] {
@@ -589,10 +695,11 @@ static bool pdl_on() {
 
 // Launch as a programmatic dependent of the previous work on the stream.
 template <typename... KArgs, typename... Args>
-static int launch_pdl(void (*k)(KArgs...), dim3 grid, size_t smem, void* stream, Args... args) {
+static int launch_pdl_n(void (*k)(KArgs...), dim3 grid, uint32_t threads, size_t smem,
+                        void* stream, Args... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(256);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = (cudaStream_t)stream;
     cudaLaunchAttribute attr[1];
@@ -601,6 +708,19 @@ static int launch_pdl(void (*k)(KArgs...), dim3 grid, size_t smem, void* stream,
     cfg.attrs = attr;
     cfg.numAttrs = pdl_on() ? 1 : 0;
     return (int)cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+template <typename... KArgs, typename... Args>
+static int launch_pdl(void (*k)(KArgs...), dim3 grid, size_t smem, void* stream, Args... args) {
+    return launch_pdl_n(k, grid, 256, smem, stream, args...);
+}
+
+// Warps per CTA (at most 12) for a launch of `units` equal warp tasks with
+// one CTA per SM: the fewest warps whose CTAs fit on the SMs, so that no SM
+// streams more than ceil(units / SMs) tasks.
+static uint32_t warps_for(uint32_t units, uint32_t sms) {
+    for (uint32_t w = 8; w < 12; ++w)
+        if ((units + w - 1) / w <= sms) return w;
+    return 12;
 }
 
 template <typename F>
@@ -613,25 +733,29 @@ extern "C" uint32_t tgkv_fwd_decode_rows(void) { return kDecRows; }
 
 extern "C" int tgkv_fwd_dec_gemv(int mode, const float* w, const float* x, uint64_t ldx,
                                  const float* g, const float* bias, float* out, uint64_t ldo,
-                                 uint32_t R, uint32_t N, uint32_t K, int clamp, void* stream) {
+                                 uint32_t R, uint32_t N, uint32_t K, int clamp, const float* pf,
+                                 uint64_t pf_n, void* stream) {
     if (R == 0 || R > kDecRows || K % 4 || ldx % 4) return (int)cudaErrorInvalidValue;
     const size_t sm = dec_smem(R, K);
     if (sm > 200 * 1024) return (int)cudaErrorInvalidValue;
-    const dim3 grid(blocks_for(N, 8));
+    // CTAs loop over rows: at most 4 per SM (64 registers a thread) so that the
+    // LM head's 32000 rows stage the normalised input once per CTA
+    const uint32_t nb = blocks_for(N, 8), cap = 4 * sm_count();
+    const dim3 grid(nb < cap ? nb : cap);
     int e;
     switch (mode) {
     case kStore:
         if ((e = set_smem(dec_gemv_kernel<kStore>, sm))) return e;
         return launch_pdl(dec_gemv_kernel<kStore>, grid, sm, stream, w, x, ldx, g, bias, out, ldo,
-                          R, N, K, clamp);
+                          R, N, K, clamp, pf, pf_n);
     case kAdd:
         if ((e = set_smem(dec_gemv_kernel<kAdd>, sm))) return e;
         return launch_pdl(dec_gemv_kernel<kAdd>, grid, sm, stream, w, x, ldx, g, bias, out, ldo,
-                          R, N, K, clamp);
+                          R, N, K, clamp, pf, pf_n);
     case kSwiglu:
         if ((e = set_smem(dec_gemv_kernel<kSwiglu>, sm))) return e;
         return launch_pdl(dec_gemv_kernel<kSwiglu>, grid, sm, stream, w, x, ldx, g, bias, out,
-                          ldo, R, N, K, clamp);
+                          ldo, R, N, K, clamp, pf, pf_n);
     default:
         return (int)cudaErrorInvalidValue;
     }
@@ -641,7 +765,8 @@ extern "C" int tgkv_fwd_dec_qkv_rope(const float* w, const float* x, const float
                                      const float* bias, const float* cs, const float* sn,
                                      float* q_out, float* kvc, uint32_t R, uint32_t d,
                                      uint32_t q_dim, uint32_t kv_dim, uint32_t hd, uint32_t pos0,
-                                     uint32_t max_seq, void* stream) {
+                                     uint32_t max_seq, const float* pf, uint64_t pf_n,
+                                     void* stream) {
     if (R == 0 || R > kDecRows || d % 4 || hd % 2 || q_dim % hd || kv_dim % hd ||
         (uint64_t)pos0 + R > max_seq)
         return (int)cudaErrorInvalidValue;
@@ -649,30 +774,38 @@ extern "C" int tgkv_fwd_dec_qkv_rope(const float* w, const float* x, const float
     if (sm > 200 * 1024) return (int)cudaErrorInvalidValue;
     int e;
     if ((e = set_smem(dec_qkv_rope_kernel, sm))) return e;
-    const uint32_t npair = (q_dim + 2 * kv_dim) / 2;
-    return launch_pdl(dec_qkv_rope_kernel, dim3(blocks_for(npair, 8)), sm, stream, w, x, g, bias,
-                      cs, sn, q_out, kvc, R, d, q_dim, kv_dim, hd, pos0, max_seq);
+    // one warp per pair of rows, one CTA per SM
+    const uint32_t npair = (q_dim + 2 * kv_dim) / 2, nw = warps_for(npair, sm_count());
+    return launch_pdl_n(dec_qkv_rope_kernel, dim3(blocks_for(npair, nw)), nw * 32, sm, stream, w,
+                        x, g, bias, cs, sn, q_out, kvc, R, d, q_dim, kv_dim, hd, pos0, max_seq,
+                        pf, pf_n);
 }
 
 extern "C" int tgkv_fwd_dec_w3_combine(const float* w3, const float* h, const int32_t* top_ids,
                                        const float* top_w, float* x, uint32_t R, uint32_t d,
-                                       uint32_t dff, uint32_t ne, uint32_t na, void* stream) {
+                                       uint32_t dff, uint32_t ne, uint32_t na, const float* pf,
+                                       uint64_t pf_n, void* stream) {
     if (R == 0 || R > kDecRows || dff % 4) return (int)cudaErrorInvalidValue;
-    return launch_pdl(dec_w3_combine_kernel, dim3(blocks_for(d, 8)), 0, stream, w3, h, top_ids,
-                      top_w, x, R, d, dff, ne, na);
+    // one warp per output row, one CTA per SM
+    const uint32_t nw = warps_for(d, sm_count());
+    return launch_pdl_n(dec_w3_combine_kernel, dim3(blocks_for(d, nw)), nw * 32, 0, stream, w3, h,
+                        top_ids, top_w, x, R, d, dff, ne, na, pf, pf_n);
 }
 
 extern "C" int tgkv_fwd_dec_moe_w12(const float* x, const float* g, const float* router,
                                     const float* bias, const float* w12, int32_t* top_ids,
                                     float* top_w, float* h, uint32_t R, uint32_t d, uint32_t dff,
-                                    uint32_t ne, uint32_t na, void* stream) {
+                                    uint32_t ne, uint32_t na, const float* w3_pf, void* stream) {
     if (R == 0 || R > kDecRows || d % 4 || ne == 0 || ne > 16 || na == 0 || na > 8 || na > ne)
         return (int)cudaErrorInvalidValue;
     const size_t sm = dec_smem(1, d);
     int e;
     if ((e = set_smem(dec_moe_w12_kernel, sm))) return e;
-    return launch_pdl(dec_moe_w12_kernel, dim3(blocks_for(dff, 8), R * na), sm, stream, x, g,
-                      router, bias, w12, top_ids, top_w, h, d, dff, ne, na);
+    // two CTAs per SM over all (token, choice) columns; warps loop over rows
+    const uint32_t cols = R * na, per = 2 * sm_count() / cols;
+    const uint32_t gx = blocks_for(dff, 8) < per ? blocks_for(dff, 8) : (per ? per : 1);
+    return launch_pdl(dec_moe_w12_kernel, dim3(gx, cols), sm, stream, x, g,
+                      router, bias, w12, top_ids, top_w, h, d, dff, ne, na, w3_pf);
 }
 
 extern "C" void* tgkv_fwd_host_alloc(size_t bytes) {

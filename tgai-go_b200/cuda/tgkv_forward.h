@@ -52,7 +52,10 @@ int tgkv_fwd_moe_combine(float* x, const float* y, const int32_t* top_ids, const
                          uint32_t seq, uint32_t d, uint32_t ne, uint32_t na, void* stream);
 
 /* Decode steps (at most tgkv_fwd_decode_rows() token rows), fused kernels,
- * launched as programmatic dependents (TGKV_PDL=0: plain launches).
+ * launched as programmatic dependents (TGKV_PDL=0: plain launches).  pf /
+ * pf_n (floats), when pf is not NULL, name weights of a later launch on the
+ * stream that the kernel prefetches into L2 (w3_pf: the expert W3 tensor
+ * [ne][d][dff], of which the routed experts are prefetched).
  * dec_gemv: out[r][n] for r < R, n < N from W [N][K] (mode 1: += ; mode 2:
  * SwiGLU over W = [W1; W2] of 2N rows, a clamped to +-88 when clamp != 0),
  * the input rows RMS-normalised with g first when g is not NULL, bias [N]
@@ -60,25 +63,27 @@ int tgkv_fwd_moe_combine(float* x, const float* y, const int32_t* top_ids, const
 uint32_t tgkv_fwd_decode_rows(void);
 int tgkv_fwd_dec_gemv(int mode, const float* w, const float* x, uint64_t ldx, const float* g,
                       const float* bias, float* out, uint64_t ldo, uint32_t R, uint32_t N,
-                      uint32_t K, int clamp, void* stream);
+                      uint32_t K, int clamp, const float* pf, uint64_t pf_n, void* stream);
 /* Q/K/V rows of R tokens from rmsnorm(x, g) . W^T (+ bias), RoPE with the
  * cs/sn tables [max_seq][hd/2] at positions pos0 + r, queries to q_out
  * [R][q_dim], keys/values into the fp32 cache kvc [2][max_seq][kv_dim]. */
 int tgkv_fwd_dec_qkv_rope(const float* w, const float* x, const float* g, const float* bias,
                           const float* cs, const float* sn, float* q_out, float* kvc, uint32_t R,
                           uint32_t d, uint32_t q_dim, uint32_t kv_dim, uint32_t hd, uint32_t pos0,
-                          uint32_t max_seq, void* stream);
+                          uint32_t max_seq, const float* pf, uint64_t pf_n, void* stream);
 /* Router and experts W1/W2 in one launch: for every pair p = (r, k),
  * ln = rmsnorm(x[r], g), the router's top-na of ln . router^T (+ bias) with
  * softmax weights, and h[p] = silu(W1[e_k] ln) * (W2[e_k] ln); top_ids /
  * top_w [R][na] written for tgkv_fwd_dec_w3_combine. */
 int tgkv_fwd_dec_moe_w12(const float* x, const float* g, const float* router, const float* bias,
                          const float* w12, int32_t* top_ids, float* top_w, float* h, uint32_t R,
-                         uint32_t d, uint32_t dff, uint32_t ne, uint32_t na, void* stream);
+                         uint32_t d, uint32_t dff, uint32_t ne, uint32_t na, const float* w3_pf,
+                         void* stream);
 /* x[r] += sum_k top_w[r][k] * W3[e_k] . h[r * na + k]  (w3 = [ne][d][dff]). */
 int tgkv_fwd_dec_w3_combine(const float* w3, const float* h, const int32_t* top_ids,
                             const float* top_w, float* x, uint32_t R, uint32_t d, uint32_t dff,
-                            uint32_t ne, uint32_t na, void* stream);
+                            uint32_t ne, uint32_t na, const float* pf, uint64_t pf_n,
+                            void* stream);
 
 /* Page-locked host memory (NULL on failure). */
 void* tgkv_fwd_host_alloc(size_t bytes);

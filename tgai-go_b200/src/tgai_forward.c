@@ -637,16 +637,32 @@ static int decode_fits(uint32_t R, uint32_t K) {
 
 /* Attention half of a layer: q/k/v, RoPE + KV append, attention.  Leaves the
  * attention output in s->attn. */
+/* A decode step's launches may prefetch the weights of a later launch into
+ * L2.  TGKV_PREFETCH is a mask of the sites: 1 Wo (by the Q/K/V launch),
+ * 2 the routed experts' W3 (by the W1/W2 launch), 4 the next layer's Q/K/V
+ * (by the W3 launch), 8 the dense FFN's W1/W2 and W3; unset or 0: none.
+ * NULL when the site is off. */
+static const float* pf(const float* w, int site) {
+    static int mask = -1;
+    if (mask < 0) {
+        const char* e = getenv("TGKV_PREFETCH");
+        mask = e && e[0] ? atoi(e) : 0;
+    }
+    return (mask & site) ? w : NULL;
+}
+
 static int attn_half(TGFwdModel* m, Slot* s, const Layer* L, TGKvCache* kv, uint32_t seq,
                      uint32_t pos, int decode) {
     const TGFwdConfig* c = &m->c;
     const uint32_t d = c->d_model;
     void* st = s->stream;
     if (decode) {
-        /* norm + projection + bias + RoPE + KV append in one launch */
+        /* norm + projection + bias + RoPE + KV append in one launch; it
+         * prefetches Wo for the out projection after the attention */
         CHECK_LAUNCH(tgkv_fwd_dec_qkv_rope(L->wqkv, s->x, L->ln1, L->bqkv, m->cs, m->sn, s->q,
                                            (float*)tg_kv_device_handle(kv), seq, d, m->q_dim,
-                                           m->kv_dim, m->hd, pos, c->max_seq_len, st));
+                                           m->kv_dim, m->hd, pos, c->max_seq_len, pf(L->wo, 1),
+                                           (uint64_t)d * m->q_dim, st));
     } else {
         CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, s->x, L->ln1, seq, d, d, d, 1e-6f, st));
         if (!gemm(s, seq, m->qkv_dim, d, s->ln, d, L->wqkv, s->qkv, m->qkv_dim, 0)) return 0;
@@ -676,20 +692,27 @@ static int run_layer(TGFwdModel* m, Slot* s, uint32_t l, uint32_t seq, uint32_t 
     const int decode = decode_fits(seq, d) && decode_fits(seq, m->q_dim) && decode_fits(seq, dff);
     if (!attn_half(m, s, L, s->kv[l], seq, pos, decode)) return 0;
     if (decode) {
-        /* out projection + residual, then the FFN, each with its norm fused */
-        CHECK_LAUNCH(tgkv_fwd_dec_gemv(1, L->wo, s->attn, m->q_dim, NULL, NULL, s->x, d, seq, d,
-                                       m->q_dim, 0, st));
+        /* out projection + residual, then the FFN, each with its norm fused;
+         * each launch prefetches the weights of a later one (the routed
+         * experts' W3 once the router has chosen; the next layer's Q/K/V) */
+        const Layer* Ln = l + 1 < c->n_layers ? &m->L[l + 1] : NULL;
+        const float* next_qkv = Ln ? pf(Ln->wqkv, 4) : NULL;
+        const uint64_t next_qkv_n = (uint64_t)m->qkv_dim * d;
         if (ne == 0) {
+            CHECK_LAUNCH(tgkv_fwd_dec_gemv(1, L->wo, s->attn, m->q_dim, NULL, NULL, s->x, d, seq, d,
+                                           m->q_dim, 0, pf(L->w12, 8), (uint64_t)2 * dff * d, st));
             CHECK_LAUNCH(tgkv_fwd_dec_gemv(2, L->w12, s->x, d, L->ln2, NULL, s->h, dff, seq, dff,
-                                           d, 1, st));
+                                           d, 1, pf(L->w3, 8), (uint64_t)d * dff, st));
             CHECK_LAUNCH(tgkv_fwd_dec_gemv(1, L->w3, s->h, dff, NULL, NULL, s->x, d, seq, d, dff,
-                                           0, st));
+                                           0, next_qkv, next_qkv_n, st));
             return 1;
         }
+        CHECK_LAUNCH(tgkv_fwd_dec_gemv(1, L->wo, s->attn, m->q_dim, NULL, NULL, s->x, d, seq, d,
+                                       m->q_dim, 0, NULL, 0, st));
         CHECK_LAUNCH(tgkv_fwd_dec_moe_w12(s->x, L->ln2, L->router, L->qb, L->w12, s->top_ids,
-                                          s->top_w, s->h, seq, d, dff, ne, na, st));
+                                          s->top_w, s->h, seq, d, dff, ne, na, pf(L->w3, 2), st));
         CHECK_LAUNCH(tgkv_fwd_dec_w3_combine(L->w3, s->h, s->top_ids, s->top_w, s->x, seq, d, dff,
-                                             ne, na, st));
+                                             ne, na, next_qkv, next_qkv_n, st));
         return 1;
     }
     if (!gemm(s, seq, d, m->q_dim, s->attn, m->q_dim, L->wo, s->x, d, 1)) return 0;
@@ -739,7 +762,7 @@ static int run_forward(TGFwdModel* m, Slot* s, const int32_t* ids, uint32_t seq,
     const float* xl = s->x + (uint64_t)(seq - 1) * d;
     if (decode_fits(1, d)) {
         CHECK_LAUNCH(tgkv_fwd_dec_gemv(0, m->emb, xl, d, m->fnorm, NULL, s->logits, m->rows, 1,
-                                       m->rows, d, 0, st));
+                                       m->rows, d, 0, NULL, 0, st));
     } else {
         CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, xl, m->fnorm, 1, d, d, d, 1e-6f, st));
         if (!gemm(s, 1, m->rows, d, s->ln, d, m->emb, s->logits, m->rows, 0)) return 0;
