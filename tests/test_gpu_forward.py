@@ -79,6 +79,47 @@ def test_long_prefill_and_decode_against_oracle(cuda):
         f.close()
 
 
+def run_against_oracle(cuda, cfg, w, steps):
+    f = tgkv.Forward(cuda, fwd_config(cfg), w)
+    o = fwd_oracle.Forward(cfg, w)
+    rng = np.random.default_rng(8)
+    ids = rng.integers(0, cfg["vocab"], 64).astype(np.int32)
+    try:
+        for pos, n in steps:
+            e = rel(f.forward("s", ids[pos:pos + n], pos), o.forward("s", ids[pos:pos + n], pos))
+            assert e < FWD_TOL, (pos, n, e)
+    finally:
+        f.close()
+    assert cuda.tg_cuda_kv_device_error() == 0
+
+
+# a prefill (grouped expert kernels, one thread per token routes) and decode
+# steps of 1-4 tokens (routing by one warp of every expert CTA)
+STEPS = ((0, 6), (6, 1), (7, 1), (8, 3), (11, 4))
+
+
+def test_router_ties_follow_the_engine(cuda):
+    """Equal router logits: the engine's top-k takes the lowest expert index
+    among equals, never one already chosen (strict greater from -1e30,
+    src/tgai_engine.c:4166-4192).  Zero routers make the logits the bias:
+    layer 0 ties three experts for the maximum, layer 1 all four, layer 2 the
+    first and the last."""
+    cfg = FM.CONFIGS["moe"]
+    w = FM.weights(cfg, 13)
+    ties = ([0.5, 1.0, 1.0, 1.0], [0.0, 0.0, 0.0, 0.0], [1.0, 0.0, 0.0, 1.0])
+    for l in range(cfg["n_layers"]):
+        w[f"blocks.{l}.moe.router.weight"] = np.zeros_like(w[f"blocks.{l}.moe.router.weight"])
+        w[f"blocks.{l}.moe._qb_bias"] = np.array(ties[l], np.float32)
+    run_against_oracle(cuda, cfg, w, STEPS)
+
+
+def test_odd_top_k_against_oracle(cuda):
+    """Top-3 of 8 experts: the decode W3 launch pairs choices (0, 1) and
+    takes choice 2 alone."""
+    cfg = dict(FM.CONFIGS["moe"], n_experts=8, n_activated=3)
+    run_against_oracle(cuda, cfg, FM.weights(cfg, 14), STEPS)
+
+
 def test_position_gap_clears_the_slot(cuda):
     """cache_pos past the slot's last position clears its KV first
     (cuda/tgai_cuda.cu:1703-1711): the result equals a fresh slot started at
