@@ -62,7 +62,68 @@ def measured_peak():
         return HBM_FALLBACK_GBS, "fallback"
 
 
-class ClockSampler:
+class NvmlSampler:
+    """SM clock and clock-event reasons read through NVML every 10 ms from a
+    thread during the timed region (read-only queries), so that a region of a
+    few hundred milliseconds still gets tens of samples.  The device is found
+    by the PCI address torch reports for the CUDA device, so the CUDA and NVML
+    orders need not agree."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap"}
+
+    def __init__(self, cuda_dev):
+        import pynvml
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        try:
+            import torch
+            pr = torch.cuda.get_device_properties(cuda_dev)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(cuda_dev)
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        self.sm, self.bits, self.stop_ev, self.th = [], 0, None, None
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop_ev.is_set():
+            try:
+                self.sm.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                self.bits |= nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            self.stop_ev.wait(0.01)
+
+    def start(self):
+        import threading
+        self.stop_ev = threading.Event()
+        self.th = threading.Thread(target=self._run, daemon=True)
+        self.th.start()
+
+    def stop(self):
+        if not self.th:
+            return None
+        self.stop_ev.set()
+        self.th.join(timeout=5)
+        if not self.sm:
+            return None
+        return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": self.max_mhz,
+                "samples": len(self.sm),
+                "reasons": sorted(n for b, n in self.REASONS.items() if self.bits & b),
+                "source": "nvml every 10 ms"}
+
+
+def ClockSampler(cuda_dev):
+    """The NVML sampler where pynvml is importable and answers, else nvidia-smi."""
+    try:
+        return NvmlSampler(cuda_dev)
+    except Exception:
+        return SmiClockSampler(cuda_dev)
+
+
+class SmiClockSampler:
     """nvidia-smi clocks and throttle reasons sampled during the timed region."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -108,7 +169,7 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
-                "reasons": sorted(reasons)}
+                "reasons": sorted(reasons), "source": "nvidia-smi every 200 ms"}
 
 
 def lengths_for(wl, seed, rank):
