@@ -403,8 +403,8 @@ def run_ours(args):
     barrier()
     clock = clocks.stop()
     timed_launches = launches[0]
-    kfam = {1: "attention_kernel (CUDA cores)", 3: "attention_tc_kernel (tcgen05)"}.get(
-        lib.tg_cuda_kv_attn_last_kernel(), "?")
+    kid = lib.tg_cuda_kv_attn_last_kernel()
+    kfam = {1: "attention_kernel (CUDA cores)", 3: "attention_tc_kernel (tcgen05)"}.get(kid, "?")
     ms = t0.elapsed_time(t1) / args.steps
     ms_max = max_over_ranks(ms)
     algo = sum(attn_bytes(lens_step[0] + s_, nh, nkv, hd) for s_ in range(args.steps)) * layers
@@ -479,7 +479,9 @@ def run_ours(args):
     tp = os.path.join(ROOT, "profiles", "attention_dram_ratio.json")
     if os.path.exists(tp):
         try:
-            traffic = per_launch_bytes * float(json.load(open(tp))[args.workload])
+            # DRAM bytes / algorithmic bytes of the kernel that ran, from its ncu capture
+            key = {1: "attention_kernel", 3: "attention_tc_kernel"}[kid]
+            traffic = per_launch_bytes * float(json.load(open(tp))[key])
         except Exception:
             traffic = None
     cpu = None
