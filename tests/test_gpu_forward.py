@@ -60,7 +60,7 @@ def test_forward_matches_engine(cuda, golden, name):
     assert cuda.tg_cuda_kv_device_error() == 0
 
 
-def test_long_prefill_and_decode_against_oracle(cuda):
+def test_long_prefill_and_decode_against_oracle(cuda, decode_path):
     """A 200-token prefill (longer than the workspaces' first size) and decode
     steps near the capacity, checked against the float64 oracle."""
     cfg = dict(FM.CONFIGS["moe"])
@@ -77,6 +77,40 @@ def test_long_prefill_and_decode_against_oracle(cuda):
             f.forward("s", ids[:2], 255)
     finally:
         f.close()
+
+
+@pytest.fixture(params=["launches", "one-launch step"])
+def decode_path(request, monkeypatch):
+    """Decode tokens through the per-layer launches, or through the
+    one-launch decode step (all layers in one cooperative launch)."""
+    if request.param == "launches":
+        monkeypatch.delenv("TGKV_FWD_STEP", raising=False)
+    else:
+        monkeypatch.setenv("TGKV_FWD_STEP", "1")
+    return request.param
+
+
+@pytest.mark.parametrize("name", sorted(FM.CONFIGS))
+def test_decode_step_matches_engine(cuda, golden, name, monkeypatch):
+    """The engine's scripts with every one-token decode on the one-launch
+    step: a handful of launches per token instead of five per layer."""
+    monkeypatch.setenv("TGKV_FWD_STEP", "1")
+    cfg = FM.CONFIGS[name]
+    f = tgkv.Forward(cuda, fwd_config(cfg), FM.weights(cfg, FM.SEEDS[name]))
+    try:
+        gold = golden[f"{name}_logits"]
+        steps = 0
+        for i, (key, ids, pos) in enumerate(FM.script(cfg, FM.SEEDS[name])):
+            lg = f.forward(key, ids, pos)
+            if len(ids) == 1:
+                assert cuda.tg_fwd_last_launches() < 3 * cfg["n_layers"]
+                steps += 1
+            e = rel(lg, gold[i])
+            assert e < FWD_TOL, (name, i, e)
+        assert steps >= 3
+    finally:
+        f.close()
+    assert cuda.tg_cuda_kv_device_error() == 0
 
 
 def run_against_oracle(cuda, cfg, w, steps):
@@ -98,7 +132,7 @@ def run_against_oracle(cuda, cfg, w, steps):
 STEPS = ((0, 6), (6, 1), (7, 1), (8, 3), (11, 4))
 
 
-def test_router_ties_follow_the_engine(cuda):
+def test_router_ties_follow_the_engine(cuda, decode_path):
     """Equal router logits: the engine's top-k takes the lowest expert index
     among equals, never one already chosen (strict greater from -1e30,
     src/tgai_engine.c:4166-4192).  Zero routers make the logits the bias:
@@ -113,7 +147,7 @@ def test_router_ties_follow_the_engine(cuda):
     run_against_oracle(cuda, cfg, w, STEPS)
 
 
-def test_odd_top_k_against_oracle(cuda):
+def test_odd_top_k_against_oracle(cuda, decode_path):
     """Top-3 of 8 experts: the decode W3 launch pairs choices (0, 1) and
     takes choice 2 alone."""
     cfg = dict(FM.CONFIGS["moe"], n_experts=8, n_activated=3)

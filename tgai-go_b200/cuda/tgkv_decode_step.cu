@@ -1,0 +1,548 @@
+// tgkv_decode_step.cu -- one decode token through every layer of the model in
+// ONE cooperative launch (sm_100a): one CTA per SM, the phases of a layer
+// separated by grid barriers instead of kernel boundaries.
+//
+// The per-launch decode path (tgkv_forward.cu) runs five dependent launches
+// per layer; each pays a fixed chain of launch, wait, input staging and
+// epilogue (2.5-3 us), which is most of a layer's time on a 3B MoE.  Here a
+// layer is five phases of one resident grid:
+//   P1  RMSNorm(x) . Wqkv in row pairs, bias, RoPE, K/V row appended at pos;
+//   P2  split attention over the cache: warp tasks of (KV head, position
+//       range) for all query heads of the group, online softmax, partials;
+//       the last task of a KV head (arrival counter) merges its heads;
+//   P3  out projection + residual;
+//   P4  RMSNorm(x), router + top-k (every CTA, same arithmetic as the
+//       engine's), routed experts' W1/W2 rows + SiLU (or the dense FFN's);
+//   P5  routed experts' W3 rows, k-ordered sum + residual (or dense W3).
+// Every barrier is bounded: a CTA that waits more than ~1 s sets the error
+// word and the grid leaves at the next barrier, so a broken run returns a
+// status instead of hanging the GPU.  Data written inside the launch (x, q,
+// the K/V rows, partials, h) is read with ld.global.cg (L2, not the SM's L1,
+// which other SMs' stores do not update); weights with the read-only path.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "tgkv_forward.h"
+
+namespace tgkvs {
+
+constexpr int kThreads = 384;        // 12 warps, one CTA per SM
+constexpr int kWarps = kThreads / 32;
+constexpr int kSub = 8;              // positions per attention load batch
+constexpr int kErrBarrier = 6;       // error word: a grid barrier timed out
+constexpr long long kSpinCycles = 2000000000ll;   // ~1 s at 2 GHz
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
+    acc = fmaf(a.x, b.x, acc);
+    acc = fmaf(a.y, b.y, acc);
+    acc = fmaf(a.z, b.z, acc);
+    return fmaf(a.w, b.w, acc);
+}
+__device__ __forceinline__ float4 ldcg4(const float* p) {
+    return __ldcg(reinterpret_cast<const float4*>(p));
+}
+__device__ __forceinline__ float silu_mul(float a, float b) { return (a / (1.0f + expf(-a))) * b; }
+
+// Grid barrier over a counter that only grows within the launch: barrier b
+// completes when the counter reaches (b + 1) * gridDim.x.  Thread 0 of each
+// CTA makes the CTA's writes visible (fence) before it arrives and waits with
+// acquire loads; the result (1 = go on) is read by all threads of the CTA
+// from shared memory, so the CTA leaves together.
+__device__ __forceinline__ int grid_sync(uint32_t* bar, uint32_t& target, int* err, int* s_ok) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        target += gridDim.x;
+        __threadfence();
+        atomicAdd(bar, 1u);
+        const long long t0 = clock64();
+        int ok = 1;
+        while (true) {
+            uint32_t v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+            if (v >= target) break;
+            if (*(volatile int*)err) { ok = 0; break; }
+            if (clock64() - t0 > kSpinCycles) {
+                atomicExch(err, kErrBarrier);
+                ok = 0;
+                break;
+            }
+            __nanosleep(64);
+        }
+        if (ok && *(volatile int*)err) ok = 0;
+        *s_ok = ok;
+    }
+    __syncthreads();
+    return *(volatile int*)s_ok;
+}
+
+// dst[0, K) = src * (1/sqrt(mean(src^2) + eps)) * g  (g NULL: plain copy);
+// src written inside the launch.  Ends with __syncthreads.
+__device__ __forceinline__ void stage(float* dst, const float* src, const float* g, uint32_t K,
+                                      float* red) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float ss = 0.f;
+    for (uint32_t i = threadIdx.x * 4; i < K; i += kThreads * 4) {
+        const float4 v = ldcg4(src + i);
+        *reinterpret_cast<float4*>(dst + i) = v;
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+    }
+    if (!g) {
+        __syncthreads();
+        return;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) t += red[w];
+    const float sc = 1.0f / sqrtf(t / (float)K + 1e-6f);
+    for (uint32_t i = threadIdx.x * 4; i < K; i += kThreads * 4) {
+        float4 v = *reinterpret_cast<const float4*>(dst + i);
+        const float4 g4 = __ldg(reinterpret_cast<const float4*>(g + i));
+        v.x = v.x * sc * g4.x;
+        v.y = v.y * sc * g4.y;
+        v.z = v.z * sc * g4.z;
+        v.w = v.w * sc * g4.w;
+        *reinterpret_cast<float4*>(dst + i) = v;
+    }
+    __syncthreads();
+}
+
+// acc[n] = W_n . x_n over K columns (x_n in shared memory), NW rows of one
+// warp; the 16-byte loads of kU column blocks of every row are issued before
+// any product.  All lanes hold the sums.
+template <int NW, int kU>
+__device__ __forceinline__ void dots(const float* const (&w)[NW], const float* const (&x)[NW],
+                                     uint32_t K, float (&acc)[NW]) {
+    const uint32_t lane = threadIdx.x & 31;
+#pragma unroll
+    for (int n = 0; n < NW; ++n) acc[n] = 0.f;
+    for (uint32_t i0 = lane * 4; i0 < K; i0 += kU * 128) {
+        float4 a4[NW][kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+#pragma unroll
+            for (int n = 0; n < NW; ++n)
+                a4[n][u] = i0 + u * 128 < K
+                               ? __ldg(reinterpret_cast<const float4*>(w[n] + i0 + u * 128))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            if (i0 + u * 128 >= K) break;
+#pragma unroll
+            for (int n = 0; n < NW; ++n)
+                acc[n] = dot4(a4[n][u], *reinterpret_cast<const float4*>(x[n] + i0 + u * 128), acc[n]);
+        }
+    }
+#pragma unroll
+    for (int n = 0; n < NW; ++n) acc[n] = warp_sum(acc[n]);
+}
+
+}  // namespace tgkvs
+
+using namespace tgkvs;
+
+// P2 for one KV head's position range [p_begin, p_end): the G query heads of
+// the group against K/V rows of the fp32 cache, lane l owning dimensions
+// [4l, 4l + 4) (lanes past head_dim / 4 idle).  Online softmax in the natural
+// exponent; the partial goes to part as [m, l, 0, 0, o[head_dim]] (running
+// max, sum, unnormalised output; stride head_dim + 4 keeps o 16-byte aligned).
+template <int G>
+__device__ __forceinline__ void attn_task(const TGFwdStepParams& p, const float* kvc, uint32_t kvh,
+                                          uint32_t task, uint32_t p_begin, uint32_t p_end) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t hd = p.head_dim, kv_dim = p.n_kv_heads * hd;
+    const bool on = lane * 4 < hd;
+    float4 qv[G];
+#pragma unroll
+    for (int t = 0; t < G; ++t)
+        qv[t] = on ? ldcg4(p.q + (uint64_t)(kvh * G + t) * hd + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float m[G], l[G];
+    float4 o[G];
+#pragma unroll
+    for (int t = 0; t < G; ++t) {
+        m[t] = -INFINITY;
+        l[t] = 0.f;
+        o[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const float* K = kvc + (uint64_t)kvh * hd + lane * 4;
+    const float* V = kvc + (uint64_t)p.max_seq * kv_dim + (uint64_t)kvh * hd + lane * 4;
+    for (uint32_t p0 = p_begin; p0 < p_end; p0 += kSub) {
+        float4 kr[kSub], vr[kSub];
+#pragma unroll
+        for (int u = 0; u < kSub; ++u) {
+            const bool in = on && p0 + u < p_end;
+            kr[u] = in ? ldcg4(K + (uint64_t)(p0 + u) * kv_dim) : make_float4(0.f, 0.f, 0.f, 0.f);
+            vr[u] = in ? ldcg4(V + (uint64_t)(p0 + u) * kv_dim) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int t = 0; t < G; ++t) {
+            float s[kSub];
+            float mx = m[t];
+#pragma unroll
+            for (int u = 0; u < kSub; ++u) {
+                s[u] = warp_sum(dot4(qv[t], kr[u], 0.f)) * p.scale;
+                if (p0 + u >= p_end) s[u] = -INFINITY;
+                mx = fmaxf(mx, s[u]);
+            }
+            const float corr = m[t] == -INFINITY ? 0.f : expf(m[t] - mx);
+            float4 acc = make_float4(o[t].x * corr, o[t].y * corr, o[t].z * corr, o[t].w * corr);
+            float ls = l[t] * corr;
+#pragma unroll
+            for (int u = 0; u < kSub; ++u) {
+                const float e = s[u] == -INFINITY ? 0.f : expf(s[u] - mx);
+                ls += e;
+                acc.x = fmaf(e, vr[u].x, acc.x);
+                acc.y = fmaf(e, vr[u].y, acc.y);
+                acc.z = fmaf(e, vr[u].z, acc.z);
+                acc.w = fmaf(e, vr[u].w, acc.w);
+            }
+            m[t] = mx;
+            l[t] = ls;
+            o[t] = acc;
+        }
+    }
+    const uint32_t stride = hd + 4;
+#pragma unroll
+    for (int t = 0; t < G; ++t) {
+        float* dst = p.part + ((uint64_t)(kvh * kTgStepMaxTasks + task) * G + t) * stride;
+        if (lane == 0) {
+            dst[0] = m[t];
+            dst[1] = l[t];
+        }
+        if (on) *reinterpret_cast<float4*>(dst + 4 + lane * 4) = o[t];
+    }
+}
+
+// Merge of KV head kvh's n_tasks partials into attn for its G heads, by one
+// warp: the maximum of the running maxima, then the rescaled sums with 16
+// partials' loads in flight at a time.
+template <int G>
+__device__ __forceinline__ void attn_merge(const TGFwdStepParams& p, uint32_t kvh, uint32_t n_tasks) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t hd = p.head_dim, stride = hd + 4;
+    const bool on = lane * 4 < hd;
+#pragma unroll 1
+    for (int t = 0; t < G; ++t) {
+        const float* base = p.part + ((uint64_t)kvh * kTgStepMaxTasks * G + t) * stride;
+        float M = -INFINITY;
+        for (uint32_t c = lane; c < n_tasks; c += 32) M = fmaxf(M, __ldcg(base + (uint64_t)c * G * stride));
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        float L = 0.f;
+        for (uint32_t c0 = 0; c0 < n_tasks; c0 += 16) {
+            float mc[16], lc[16];
+            float4 oc[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const bool in = c0 + u < n_tasks;
+                const float* pc = base + (uint64_t)(c0 + u) * G * stride;
+                mc[u] = in ? __ldcg(pc) : -INFINITY;
+                lc[u] = in ? __ldcg(pc + 1) : 0.f;
+                oc[u] = in && on ? ldcg4(pc + 4 + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const float f = mc[u] == -INFINITY ? 0.f : expf(mc[u] - M);
+                L = fmaf(f, lc[u], L);
+                O.x = fmaf(f, oc[u].x, O.x);
+                O.y = fmaf(f, oc[u].y, O.y);
+                O.z = fmaf(f, oc[u].z, O.z);
+                O.w = fmaf(f, oc[u].w, O.w);
+            }
+        }
+        if (on) {
+            const float inv = 1.0f / L;
+            float* dst = p.attn + (uint64_t)(kvh * G + t) * hd + lane * 4;
+            dst[0] = O.x * inv;
+            dst[1] = O.y * inv;
+            dst[2] = O.z * inv;
+            dst[3] = O.w * inv;
+        }
+    }
+}
+
+// The engine's top-k of warp 0 over slog[0, ne): for k = 0..na-1 the first
+// expert (lowest index) of the largest logit above -1e30 not chosen yet, else
+// -1 with -1e30 (src/tgai_engine.c:4166-4192), then the softmax over the
+// chosen logits with the exponentials summed in k order.
+__device__ __forceinline__ void top_k_warp(const float* slog, uint32_t ne, uint32_t na,
+                                           int* s_ids, float* s_w) {
+    const uint32_t lane = threadIdx.x & 31;
+    const float v = lane < ne ? slog[lane] : 0.f;
+    bool used = false;
+    float my_v = -1e30f;
+    int my_id = -1;
+    for (uint32_t k = 0; k < na; ++k) {
+        const bool cand = lane < ne && !used && v > -1e30f;
+        float bv = cand ? v : -1e30f;
+        int bi = cand ? (int)lane : -1;
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (bi >= 0 && (uint32_t)bi == lane) used = true;
+        if (lane == k) {
+            my_v = bi >= 0 ? bv : -1e30f;
+            my_id = bi;
+        }
+    }
+    float mx = my_v;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float ek = lane < na ? expf(my_v - mx) : 0.f;
+    float ss = 0.f;
+    for (uint32_t k = 0; k < na; ++k) ss += __shfl_sync(0xffffffffu, ek, k);
+    if (lane < na) {
+        s_ids[lane] = my_id;
+        s_w[lane] = ek / ss;
+    }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdStepParams p) {
+    extern __shared__ __align__(16) float smem[];
+    __shared__ float red[kWarps];
+    __shared__ float slog[16];
+    __shared__ int s_ids[8];
+    __shared__ float s_w[8];
+    __shared__ int s_ok;
+    const uint32_t d = p.d, hd = p.head_dim, nkv = p.n_kv_heads;
+    const uint32_t q_dim = nkv * G * hd, kv_dim = nkv * hd, dff = p.dff, ne = p.ne, na = p.na;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t gw = blockIdx.x * kWarps + warp, tw = gridDim.x * kWarps;
+    float* sx = smem;                     // [max(d, q_dim)]
+    float* sh = smem + p.sx_floats;       // [na or 1][dff]
+    uint32_t* bar = p.state;
+    int* err = reinterpret_cast<int*>(p.state + 1);
+    uint32_t* ctr = p.state + 2;
+    uint32_t target = 0;
+    // attention split: at most kTgStepMaxTasks position ranges per KV head,
+    // each a multiple of kSub positions, about 16 positions where L allows
+    const uint32_t L = p.pos + 1;
+    uint32_t n_tasks = (L + 15) / 16;
+    if (n_tasks > kTgStepMaxTasks) n_tasks = kTgStepMaxTasks;
+    const uint32_t ch = ((L + n_tasks - 1) / n_tasks + kSub - 1) / kSub * kSub;
+    n_tasks = (L + ch - 1) / ch;
+    const uint32_t half = hd >> 1;
+
+    for (uint32_t l = 0; l < p.n_layers; ++l) {
+        const TGFwdStepLayer W = p.layers[l];
+        float* kvc = p.kvc[l];
+        // ---- P1: norm, Q/K/V row pairs, bias, RoPE at pos, K/V append
+        stage(sx, p.x, W.ln1, d, red);
+        const uint32_t npair = (q_dim + 2 * kv_dim) / 2;
+        for (uint32_t mp = gw; mp < npair; mp += tw) {
+            const uint32_t n0 = 2 * mp;
+            float a[2];
+            dots<2, 12>({W.wqkv + (uint64_t)n0 * d, W.wqkv + (uint64_t)(n0 + 1) * d}, {sx, sx}, d, a);
+            if (lane == 0) {
+                float v0 = a[0], v1 = a[1];
+                if (W.bqkv) {
+                    v0 += W.bqkv[n0];
+                    v1 += W.bqkv[n0 + 1];
+                }
+                if (n0 < q_dim + kv_dim) {
+                    const uint32_t col = n0 < q_dim ? n0 : n0 - q_dim;
+                    const uint64_t ti = (uint64_t)p.pos * half + (col % hd) / 2;
+                    const float c = p.cs[ti], s = p.sn[ti];
+                    const float r0 = __fmaf_rn(v0, c, -__fmul_rn(v1, s));
+                    const float r1 = __fmaf_rn(v0, s, __fmul_rn(v1, c));
+                    float* dst = n0 < q_dim ? p.q + col : kvc + (uint64_t)p.pos * kv_dim + col;
+                    dst[0] = r0;
+                    dst[1] = r1;
+                } else {
+                    float* dst = kvc + ((uint64_t)p.max_seq + p.pos) * kv_dim + (n0 - q_dim - kv_dim);
+                    dst[0] = v0;
+                    dst[1] = v1;
+                }
+            }
+        }
+        if (!grid_sync(bar, target, err, &s_ok)) return;
+        // ---- P2: split attention; the last task of a KV head merges it
+        for (uint32_t t = gw; t < nkv * n_tasks; t += tw) {
+            const uint32_t kvh = t / n_tasks, task = t % n_tasks;
+            const uint32_t pb = task * ch, pe = pb + ch < L ? pb + ch : L;
+            attn_task<G>(p, kvc, kvh, task, pb, pe);
+            __threadfence();
+            __syncwarp();
+            uint32_t old = 0;
+            if (lane == 0) old = atomicAdd(ctr + kvh, 1u);
+            old = __shfl_sync(0xffffffffu, old, 0);
+            if (old == n_tasks - 1) {
+                __threadfence();
+                attn_merge<G>(p, kvh, n_tasks);
+                if (lane == 0) atomicExch(ctr + kvh, 0u);   // ready for the next layer
+            }
+        }
+        if (!grid_sync(bar, target, err, &s_ok)) return;
+        // ---- P3: out projection + residual
+        stage(sx, p.attn, nullptr, q_dim, red);
+        for (uint32_t n = gw; n < d; n += tw) {
+            float a[1];
+            dots<1, 12>({W.wo + (uint64_t)n * q_dim}, {sx}, q_dim, a);
+            if (lane == 0) p.x[n] = __ldcg(p.x + n) + a[0];
+        }
+        if (!grid_sync(bar, target, err, &s_ok)) return;
+        // ---- P4: norm, router + top-k (every CTA), expert W1/W2 rows + SiLU
+        stage(sx, p.x, W.ln2, d, red);
+        if (ne) {
+            for (uint32_t e = warp; e < ne; e += kWarps) {
+                float a[1];
+                dots<1, 12>({W.router + (uint64_t)e * d}, {sx}, d, a);
+                if (lane == 0) slog[e] = W.qb ? a[0] + W.qb[e] : a[0];
+            }
+            __syncthreads();
+            if (warp == 0) top_k_warp(slog, ne, na, s_ids, s_w);
+            __syncthreads();
+            for (uint32_t t = gw; t < na * dff; t += tw) {
+                const uint32_t k = t / dff, j = t % dff;
+                const int e = s_ids[k];
+                float hv = 0.f;
+                if (e >= 0 && (uint32_t)e < ne) {
+                    const float* wa = W.w12 + ((uint64_t)e * 2 * dff + j) * d;
+                    float a[2];
+                    dots<2, 12>({wa, wa + (uint64_t)dff * d}, {sx, sx}, d, a);
+                    hv = silu_mul(a[0], a[1]);
+                }
+                if (lane == 0) p.h[(uint64_t)k * dff + j] = hv;
+            }
+        } else {
+            for (uint32_t j = gw; j < dff; j += tw) {
+                float a[2];
+                dots<2, 12>({W.w12 + (uint64_t)j * d, W.w12 + (uint64_t)(dff + j) * d}, {sx, sx}, d, a);
+                if (lane == 0) p.h[j] = silu_mul(fminf(fmaxf(a[0], -88.0f), 88.0f), a[1]);
+            }
+        }
+        if (!grid_sync(bar, target, err, &s_ok)) return;
+        // ---- P5: W3 rows, k-ordered weighted sum (or dense W3) + residual
+        stage(sh, p.h, nullptr, (ne ? na : 1) * dff, red);
+        for (uint32_t i = gw; i < d; i += tw) {
+            float ot = 0.f;
+            if (ne) {
+                for (uint32_t k = 0; k < na; k += 2) {
+                    const int e0 = s_ids[k];
+                    const int e1 = k + 1 < na ? s_ids[k + 1] : -1;
+                    const bool v0 = e0 >= 0 && (uint32_t)e0 < ne, v1 = e1 >= 0 && (uint32_t)e1 < ne;
+                    const float* w0 = W.w3 + ((uint64_t)(v0 ? e0 : 0) * d + i) * dff;
+                    float a0 = 0.f, a1 = 0.f;
+                    if (v1) {
+                        float a[2];
+                        dots<2, 12>({w0, W.w3 + ((uint64_t)e1 * d + i) * dff},
+                                    {sh + (uint64_t)k * dff, sh + (uint64_t)(k + 1) * dff}, dff, a);
+                        a0 = a[0];
+                        a1 = a[1];
+                    } else if (v0) {
+                        float a[1];
+                        dots<1, 12>({w0}, {sh + (uint64_t)k * dff}, dff, a);
+                        a0 = a[0];
+                    }
+                    if (v0) ot = fmaf(s_w[k], a0, ot);
+                    if (v1) ot = fmaf(s_w[k + 1], a1, ot);
+                }
+            } else {
+                float a[1];
+                dots<1, 12>({W.w3 + (uint64_t)i * dff}, {sh}, dff, a);
+                ot = a[0];
+            }
+            if (lane == 0) p.x[i] = __ldcg(p.x + i) + ot;
+        }
+        if (!grid_sync(bar, target, err, &s_ok)) return;
+    }
+}
+
+namespace {
+
+template <int G>
+int launch_step(const TGFwdStepParams& p, size_t smem, uint32_t grid, cudaStream_t st) {
+    void* args[] = {const_cast<TGFwdStepParams*>(&p)};
+    return (int)cudaLaunchCooperativeKernel((const void*)decode_step_kernel<G>, dim3(grid),
+                                            dim3(kThreads), args, smem, st);
+}
+
+template <int G>
+int step_grid(size_t smem, uint32_t* grid) {
+    int dev = 0, sms = 0, per = 0, coop = 0;
+    cudaError_t e;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return (int)e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        return (int)e;
+    if ((e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev)) != cudaSuccess)
+        return (int)e;
+    if (!coop) return (int)cudaErrorNotSupported;
+    if (smem > 48 * 1024 &&
+        (e = cudaFuncSetAttribute(decode_step_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem)) != cudaSuccess)
+        return (int)e;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, decode_step_kernel<G>, kThreads,
+                                                           smem)) != cudaSuccess)
+        return (int)e;
+    if (per < 1) return (int)cudaErrorCooperativeLaunchTooLarge;
+    *grid = (uint32_t)sms;                 // one CTA per SM
+    return 0;
+}
+
+}  // namespace
+
+extern "C" int tgkv_fwd_step_supported(uint32_t d, uint32_t n_heads, uint32_t n_kv_heads,
+                                       uint32_t head_dim, uint32_t dff, uint32_t ne, uint32_t na) {
+    if (!n_kv_heads || n_heads % n_kv_heads) return 0;
+    const uint32_t g = n_heads / n_kv_heads;
+    if (g != 1 && g != 2 && g != 3 && g != 4 && g != 8) return 0;
+    if (head_dim != 32 && head_dim != 64 && head_dim != 128) return 0;
+    if (d % 4 || dff % 4 || ne > 16 || na > 8 || (ne && (na == 0 || na > ne))) return 0;
+    return tgkv_fwd_step_smem(d, n_heads * head_dim, dff, ne, na) <= 160 * 1024;
+}
+
+extern "C" size_t tgkv_fwd_step_smem(uint32_t d, uint32_t q_dim, uint32_t dff, uint32_t ne,
+                                     uint32_t na) {
+    const size_t sx = d > q_dim ? d : q_dim;
+    return (sx + (size_t)(ne ? na : 1) * dff) * 4;
+}
+
+extern "C" size_t tgkv_fwd_step_part_floats(uint32_t n_heads, uint32_t n_kv_heads,
+                                            uint32_t head_dim) {
+    (void)n_kv_heads;
+    return (size_t)n_heads * kTgStepMaxTasks * (head_dim + 4);
+}
+
+extern "C" int tgkv_fwd_decode_step(const TGFwdStepParams* p, void* stream) {
+    if (!p || !p->n_kv_heads || p->n_heads % p->n_kv_heads || p->pos >= p->max_seq)
+        return (int)cudaErrorInvalidValue;
+    const uint32_t g = p->n_heads / p->n_kv_heads;
+    const size_t smem = tgkv_fwd_step_smem(p->d, p->n_heads * p->head_dim, p->dff, p->ne, p->na);
+    if (p->sx_floats != (smem / 4 - (size_t)(p->ne ? p->na : 1) * p->dff))
+        return (int)cudaErrorInvalidValue;
+    cudaStream_t st = (cudaStream_t)stream;
+    uint32_t grid = 0;
+    int e;
+    switch (g) {
+#define TGKV_STEP_CASE(GV)                                       \
+    case GV:                                                     \
+        if ((e = step_grid<GV>(smem, &grid))) return e;          \
+        return launch_step<GV>(*p, smem, grid, st);
+        TGKV_STEP_CASE(1)
+        TGKV_STEP_CASE(2)
+        TGKV_STEP_CASE(3)
+        TGKV_STEP_CASE(4)
+        TGKV_STEP_CASE(8)
+#undef TGKV_STEP_CASE
+    default:
+        return (int)cudaErrorInvalidValue;
+    }
+}

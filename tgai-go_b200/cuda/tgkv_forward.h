@@ -4,6 +4,7 @@
 #ifndef TGKV_FORWARD_H
 #define TGKV_FORWARD_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -84,6 +85,33 @@ int tgkv_fwd_dec_w3_combine(const float* w3, const float* h, const int32_t* top_
                             const float* top_w, float* x, uint32_t R, uint32_t d, uint32_t dff,
                             uint32_t ne, uint32_t na, const float* pf, uint64_t pf_n,
                             void* stream);
+
+/* One decode token through all layers as ONE cooperative launch
+ * (tgkv_decode_step.cu): one CTA per SM, the five phases of a layer (Q/K/V +
+ * RoPE + append, split attention, out projection, router + experts W1/W2 or
+ * the dense W1/W2, W3 + combine) separated by bounded grid barriers.  x [d]
+ * holds the embedded token on entry and the last layer's output on return;
+ * the caller zeroes state [2 + n_kv_heads] before each launch and reads
+ * state[1] (0, or 6 when a barrier timed out) after it. */
+enum { kTgStepMaxTasks = 256 };     /* attention partials per KV head */
+typedef struct {
+    const float *ln1, *ln2, *wqkv, *bqkv, *wo, *w12, *w3, *router, *qb;
+} TGFwdStepLayer;
+typedef struct {
+    const TGFwdStepLayer* layers;   /* device [n_layers] */
+    float* const* kvc;              /* device [n_layers]: fp32 caches [2][max_seq][kv_dim] */
+    float *x, *q, *attn, *h, *part; /* [d], [q_dim], [q_dim], [na or 1][dff], partials */
+    uint32_t* state;                /* barrier count, error word, arrival counters */
+    const float *cs, *sn;           /* RoPE tables [max_seq][head_dim / 2] */
+    uint32_t n_layers, d, n_heads, n_kv_heads, head_dim, dff, ne, na, pos, max_seq;
+    uint32_t sx_floats;             /* max(d, q_dim) */
+    float scale;                    /* score scale: 1/sqrt(head_dim) times the YaRN mscale */
+} TGFwdStepParams;
+int tgkv_fwd_step_supported(uint32_t d, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                            uint32_t dff, uint32_t ne, uint32_t na);
+size_t tgkv_fwd_step_smem(uint32_t d, uint32_t q_dim, uint32_t dff, uint32_t ne, uint32_t na);
+size_t tgkv_fwd_step_part_floats(uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim);
+int tgkv_fwd_decode_step(const TGFwdStepParams* p, void* stream);
 
 /* Page-locked host memory (NULL on failure). */
 void* tgkv_fwd_host_alloc(size_t bytes);

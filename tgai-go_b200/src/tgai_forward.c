@@ -133,6 +133,11 @@ typedef struct Slot {
     uint32_t *counts, *lists;
     int32_t* h_ids;          /* page-locked */
     float* h_logits;         /* page-locked [vocab] */
+    /* one-launch decode step (tgkv_decode_step.cu), allocated at its first use */
+    float** step_kvc;        /* device [n_layers]: this slot's cache buffers */
+    float* step_part;        /* attention partials */
+    uint32_t* step_state;    /* barrier count, error word, arrival counters */
+    int32_t* h_step;         /* page-locked copy of the error word */
 } Slot;
 
 struct TGFwdModel {
@@ -140,6 +145,7 @@ struct TGFwdModel {
     uint32_t hd, nkv, q_dim, kv_dim, qkv_dim, rows;
     Layer* L;
     float *emb, *fnorm, *cs, *sn;
+    TGFwdStepLayer* step_layers;   /* device [n_layers], when the one-launch step fits */
     uint64_t wbytes;
     pthread_mutex_t mu;
     Slot* slots;
@@ -216,6 +222,7 @@ void tg_fwd_destroy(TGFwdModel* m) {
     tg_cuda_kv_free(m->fnorm);
     tg_cuda_kv_free(m->cs);
     tg_cuda_kv_free(m->sn);
+    tg_cuda_kv_free(m->step_layers);
     pthread_mutex_destroy(&m->mu);
     free(m);
 }
@@ -393,6 +400,22 @@ TGFwdModel* tg_fwd_create(const TGFwdConfig* cfg, TGFwdWeightFn get, void* ctx) 
         free(sn);
         if (!ok) goto fail;
     }
+    if (tgkv_fwd_step_supported(c.d_model, c.n_heads, m->nkv, m->hd, c.d_ff, c.n_experts,
+                                c.n_activated)) {
+        /* the layer table of the one-launch decode step */
+        TGFwdStepLayer* t = (TGFwdStepLayer*)calloc(c.n_layers, sizeof(TGFwdStepLayer));
+        if (!t) { set_err("host allocation failed"); goto fail; }
+        for (uint32_t l = 0; l < c.n_layers; l++) {
+            const Layer* L = &m->L[l];
+            t[l] = (TGFwdStepLayer){L->ln1, L->ln2, L->wqkv, L->bqkv, L->wo, L->w12, L->w3,
+                                    L->router, L->qb};
+        }
+        const size_t b = (size_t)c.n_layers * sizeof(TGFwdStepLayer);
+        m->step_layers = (TGFwdStepLayer*)tg_cuda_kv_malloc(b);
+        const int ok = m->step_layers && tg_cuda_kv_h2d(m->step_layers, t, b, NULL);
+        free(t);
+        if (!ok) { set_err("step layer table: %s", tg_cuda_kv_last_error()); goto fail; }
+    }
     return m;
 fail:
     tg_fwd_destroy(m);
@@ -420,6 +443,14 @@ static void slot_free_ws(Slot* s) {
 static void slot_release_mem(TGFwdModel* m, Slot* s) {
     if (s->stream) tg_cuda_kv_sync(s->stream);
     slot_free_ws(s);
+    tg_cuda_kv_free(s->step_kvc);
+    tg_cuda_kv_free(s->step_part);
+    tg_cuda_kv_free(s->step_state);
+    tgkv_fwd_host_free(s->h_step);
+    s->step_kvc = NULL;
+    s->step_part = NULL;
+    s->step_state = NULL;
+    s->h_step = NULL;
     if (s->kv) {
         for (uint32_t l = 0; l < m->c.n_layers; l++) tg_kv_destroy(s->kv[l]);
         free(s->kv);
@@ -738,6 +769,74 @@ static int run_layer(TGFwdModel* m, Slot* s, uint32_t l, uint32_t seq, uint32_t 
     return 1;
 }
 
+/* One-token decode steps run as one cooperative launch over all layers
+ * (tgkv_fwd_decode_step) with TGKV_FWD_STEP=1, where the model fits it. */
+static int step_on(void) {
+    const char* e = getenv("TGKV_FWD_STEP");
+    return e && e[0] == '1';
+}
+
+/* All layers of one decode token at position pos (x holds its embedding);
+ * the error word comes back with the logits. */
+static int run_step(TGFwdModel* m, Slot* s, uint32_t pos) {
+    const TGFwdConfig* c = &m->c;
+    void* st = s->stream;
+    const uint32_t state_n = 2 + m->nkv;
+    if (!s->step_kvc) {
+        float** h = (float**)malloc(c->n_layers * sizeof(float*));
+        if (!h) { set_err("host allocation failed"); return 0; }
+        for (uint32_t l = 0; l < c->n_layers; l++) h[l] = (float*)tg_kv_device_handle(s->kv[l]);
+        s->step_kvc = (float**)tg_cuda_kv_malloc(c->n_layers * sizeof(float*));
+        int ok = s->step_kvc && tg_cuda_kv_h2d(s->step_kvc, h, c->n_layers * sizeof(float*), NULL);
+        free(h);
+        s->step_part = (float*)tg_cuda_kv_malloc(
+            tgkv_fwd_step_part_floats(c->n_heads, m->nkv, m->hd) * sizeof(float));
+        s->step_state = (uint32_t*)tg_cuda_kv_malloc(state_n * 4);
+        s->h_step = (int32_t*)tgkv_fwd_host_alloc(16);
+        if (!ok || !s->step_part || !s->step_state || !s->h_step) {
+            set_err("decode step buffers: allocation failed");
+            return 0;
+        }
+    }
+    t_launches++;
+    if (!tg_cuda_kv_memset(s->step_state, 0, state_n * 4, st)) {
+        set_err("memset: %s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    TGFwdStepParams p;
+    memset(&p, 0, sizeof(p));
+    p.layers = m->step_layers;
+    p.kvc = s->step_kvc;
+    p.x = s->x;
+    p.q = s->q;
+    p.attn = s->attn;
+    p.h = s->h;
+    p.part = s->step_part;
+    p.state = s->step_state;
+    p.cs = m->cs;
+    p.sn = m->sn;
+    p.n_layers = c->n_layers;
+    p.d = c->d_model;
+    p.n_heads = c->n_heads;
+    p.n_kv_heads = m->nkv;
+    p.head_dim = m->hd;
+    p.dff = c->d_ff;
+    p.ne = c->n_experts;
+    p.na = c->n_activated;
+    p.pos = pos;
+    p.max_seq = c->max_seq_len;
+    p.sx_floats = c->d_model > m->q_dim ? c->d_model : m->q_dim;
+    p.scale = 1.0f / sqrtf((float)m->hd);
+    CHECK_LAUNCH(tgkv_fwd_decode_step(&p, st));
+    for (uint32_t l = 0; l < c->n_layers; l++) tg_kv_advance(s->kv[l], 1);
+    s->h_step[0] = -1;
+    if (!tg_cuda_kv_d2h(s->h_step, s->step_state + 1, 4, st)) {
+        set_err("decode step status: %s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    return 1;
+}
+
 static int run_forward(TGFwdModel* m, Slot* s, const int32_t* ids, uint32_t seq, uint32_t pos) {
     const TGFwdConfig* c = &m->c;
     const uint32_t d = c->d_model;
@@ -756,8 +855,13 @@ static int run_forward(TGFwdModel* m, Slot* s, const int32_t* ids, uint32_t seq,
         return 0;
     }
     CHECK_LAUNCH(tgkv_fwd_embed(s->x, m->emb, s->ids, seq, d, m->rows, c->unk_id, st));
-    for (uint32_t l = 0; l < c->n_layers; l++)
-        if (!run_layer(m, s, l, seq, pos)) return 0;
+    const int step = seq == 1 && m->step_layers && step_on();
+    if (step) {
+        if (!run_step(m, s, pos)) return 0;
+    } else {
+        for (uint32_t l = 0; l < c->n_layers; l++)
+            if (!run_layer(m, s, l, seq, pos)) return 0;
+    }
     /* final norm of the last row, then the tied-embedding LM head */
     const float* xl = s->x + (uint64_t)(seq - 1) * d;
     if (decode_fits(1, d)) {
@@ -770,6 +874,10 @@ static int run_forward(TGFwdModel* m, Slot* s, const int32_t* ids, uint32_t seq,
     t_launches++;
     if (!tg_cuda_kv_d2h(s->h_logits, s->logits, (size_t)m->rows * 4, st) || !tg_cuda_kv_sync(st)) {
         set_err("forward: %s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    if (step && s->h_step[0] != 0) {
+        set_err("decode step: grid barrier timed out (status %d)", s->h_step[0]);
         return 0;
     }
     s->last_pos = (int)(pos + seq);
