@@ -9,8 +9,8 @@
 //   P1  RMSNorm(x) . Wqkv in row pairs, bias, RoPE, K/V row appended at pos;
 //   P2  split attention over the cache: warp tasks of (KV head, position
 //       range) for all query heads of the group, online softmax, partials;
-//       the last task of a KV head (arrival counter) merges its heads;
-//   P3  out projection + residual;
+//   P3  every CTA merges the partials of all heads into shared memory (one
+//       warp per head), then the out projection + residual;
 //   P4  RMSNorm(x), router + top-k (every CTA, same arithmetic as the
 //       engine's), routed experts' W1/W2 rows + SiLU (or the dense FFN's);
 //   P5  routed experts' W3 rows, k-ordered sum + residual (or dense W3).
@@ -223,52 +223,53 @@ __device__ __forceinline__ void attn_task(const TGFwdStepParams& p, const float*
     }
 }
 
-// Merge of KV head kvh's n_tasks partials into attn for its G heads, by one
-// warp: the maximum of the running maxima, then the rescaled sums with 16
-// partials' loads in flight at a time.
+// Head h's attention output from its n_tasks partials, by one warp, into
+// dst [head_dim] (shared memory): an online merge over batches of 16
+// partials (all their loads in flight), each rescaled to the running maximum.
 template <int G>
-__device__ __forceinline__ void attn_merge(const TGFwdStepParams& p, uint32_t kvh, uint32_t n_tasks) {
+__device__ __forceinline__ void attn_merge_head(const TGFwdStepParams& p, uint32_t h,
+                                                uint32_t n_tasks, float* dst) {
     const uint32_t lane = threadIdx.x & 31;
-    const uint32_t hd = p.head_dim, stride = hd + 4;
+    const uint32_t hd = p.head_dim, stride = hd + 4, kvh = h / G, t = h % G;
     const bool on = lane * 4 < hd;
-#pragma unroll 1
-    for (int t = 0; t < G; ++t) {
-        const float* base = p.part + ((uint64_t)kvh * kTgStepMaxTasks * G + t) * stride;
-        float M = -INFINITY;
-        for (uint32_t c = lane; c < n_tasks; c += 32) M = fmaxf(M, __ldcg(base + (uint64_t)c * G * stride));
+    const float* base = p.part + ((uint64_t)kvh * kTgStepMaxTasks * G + t) * stride;
+    float M = -INFINITY, L = 0.f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t c0 = 0; c0 < n_tasks; c0 += 16) {
+        float mc[16], lc[16];
+        float4 oc[16];
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-        float L = 0.f;
-        for (uint32_t c0 = 0; c0 < n_tasks; c0 += 16) {
-            float mc[16], lc[16];
-            float4 oc[16];
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const bool in = c0 + u < n_tasks;
-                const float* pc = base + (uint64_t)(c0 + u) * G * stride;
-                mc[u] = in ? __ldcg(pc) : -INFINITY;
-                lc[u] = in ? __ldcg(pc + 1) : 0.f;
-                oc[u] = in && on ? ldcg4(pc + 4 + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const float f = mc[u] == -INFINITY ? 0.f : expf(mc[u] - M);
-                L = fmaf(f, lc[u], L);
-                O.x = fmaf(f, oc[u].x, O.x);
-                O.y = fmaf(f, oc[u].y, O.y);
-                O.z = fmaf(f, oc[u].z, O.z);
-                O.w = fmaf(f, oc[u].w, O.w);
-            }
+        for (int u = 0; u < 16; ++u) {
+            const bool in = c0 + u < n_tasks;
+            const float* pc = base + (uint64_t)(c0 + u) * G * stride;
+            mc[u] = in ? __ldcg(pc) : -INFINITY;
+            lc[u] = in ? __ldcg(pc + 1) : 0.f;
+            oc[u] = in && on ? ldcg4(pc + 4 + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        if (on) {
-            const float inv = 1.0f / L;
-            float* dst = p.attn + (uint64_t)(kvh * G + t) * hd + lane * 4;
-            dst[0] = O.x * inv;
-            dst[1] = O.y * inv;
-            dst[2] = O.z * inv;
-            dst[3] = O.w * inv;
+        float nm = M;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) nm = fmaxf(nm, mc[u]);
+        const float corr = M == -INFINITY ? 0.f : expf(M - nm);
+        L *= corr;
+        O.x *= corr;
+        O.y *= corr;
+        O.z *= corr;
+        O.w *= corr;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+            const float f = mc[u] == -INFINITY ? 0.f : expf(mc[u] - nm);
+            L = fmaf(f, lc[u], L);
+            O.x = fmaf(f, oc[u].x, O.x);
+            O.y = fmaf(f, oc[u].y, O.y);
+            O.z = fmaf(f, oc[u].z, O.z);
+            O.w = fmaf(f, oc[u].w, O.w);
         }
+        M = nm;
+    }
+    if (on) {
+        const float inv = 1.0f / L;
+        *reinterpret_cast<float4*>(dst + lane * 4) =
+            make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
     }
 }
 
@@ -330,7 +331,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
     float* sh = smem + p.sx_floats;       // [na or 1][dff]
     uint32_t* bar = p.state;
     int* err = reinterpret_cast<int*>(p.state + 1);
-    uint32_t* ctr = p.state + 2;
     uint32_t target = 0;
     // attention split: at most kTgStepMaxTasks position ranges per KV head,
     // each a multiple of kSub positions, about 16 positions where L allows
@@ -374,25 +374,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
             }
         }
         if (!grid_sync(bar, target, err, &s_ok)) return;
-        // ---- P2: split attention; the last task of a KV head merges it
+        // ---- P2: split attention, partials per (KV head, position range)
         for (uint32_t t = gw; t < nkv * n_tasks; t += tw) {
             const uint32_t kvh = t / n_tasks, task = t % n_tasks;
             const uint32_t pb = task * ch, pe = pb + ch < L ? pb + ch : L;
             attn_task<G>(p, kvc, kvh, task, pb, pe);
-            __threadfence();
-            __syncwarp();
-            uint32_t old = 0;
-            if (lane == 0) old = atomicAdd(ctr + kvh, 1u);
-            old = __shfl_sync(0xffffffffu, old, 0);
-            if (old == n_tasks - 1) {
-                __threadfence();
-                attn_merge<G>(p, kvh, n_tasks);
-                if (lane == 0) atomicExch(ctr + kvh, 0u);   // ready for the next layer
-            }
         }
         if (!grid_sync(bar, target, err, &s_ok)) return;
-        // ---- P3: out projection + residual
-        stage(sx, p.attn, nullptr, q_dim, red);
+        // ---- P3: every CTA merges all heads into sx, then out projection + residual
+        for (uint32_t h = warp; h < nkv * G; h += kWarps) attn_merge_head<G>(p, h, n_tasks, sx + h * hd);
+        __syncthreads();
         for (uint32_t n = gw; n < d; n += tw) {
             float a[1];
             dots<1, 12>({W.wo + (uint64_t)n * q_dim}, {sx}, q_dim, a);

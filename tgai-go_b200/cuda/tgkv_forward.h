@@ -91,9 +91,9 @@ int tgkv_fwd_dec_w3_combine(const float* w3, const float* h, const int32_t* top_
  * RoPE + append, split attention, out projection, router + experts W1/W2 or
  * the dense W1/W2, W3 + combine) separated by bounded grid barriers.  x [d]
  * holds the embedded token on entry and the last layer's output on return;
- * the caller zeroes state [2 + n_kv_heads] before each launch and reads
- * state[1] (0, or 6 when a barrier timed out) after it. */
-enum { kTgStepMaxTasks = 256 };     /* attention partials per KV head */
+ * the caller zeroes state [2] (barrier count, error word) before each launch
+ * and reads state[1] (0, or 6 when a barrier timed out) after it. */
+enum { kTgStepMaxTasks = 128 };     /* attention partials per KV head */
 typedef struct {
     const float *ln1, *ln2, *wqkv, *bqkv, *wo, *w12, *w3, *router, *qb;
 } TGFwdStepLayer;
@@ -101,7 +101,7 @@ typedef struct {
     const TGFwdStepLayer* layers;   /* device [n_layers] */
     float* const* kvc;              /* device [n_layers]: fp32 caches [2][max_seq][kv_dim] */
     float *x, *q, *attn, *h, *part; /* [d], [q_dim], [q_dim], [na or 1][dff], partials */
-    uint32_t* state;                /* barrier count, error word, arrival counters */
+    uint32_t* state;                /* barrier count, error word */
     const float *cs, *sn;           /* RoPE tables [max_seq][head_dim / 2] */
     uint32_t n_layers, d, n_heads, n_kv_heads, head_dim, dff, ne, na, pos, max_seq;
     uint32_t sx_floats;             /* max(d, q_dim) */

@@ -136,7 +136,7 @@ typedef struct Slot {
     /* one-launch decode step (tgkv_decode_step.cu), allocated at its first use */
     float** step_kvc;        /* device [n_layers]: this slot's cache buffers */
     float* step_part;        /* attention partials */
-    uint32_t* step_state;    /* barrier count, error word, arrival counters */
+    uint32_t* step_state;    /* barrier count, error word */
     int32_t* h_step;         /* page-locked copy of the error word */
 } Slot;
 
@@ -781,7 +781,7 @@ static int step_on(void) {
 static int run_step(TGFwdModel* m, Slot* s, uint32_t pos) {
     const TGFwdConfig* c = &m->c;
     void* st = s->stream;
-    const uint32_t state_n = 2 + m->nkv;
+    const uint32_t state_n = 2;
     if (!s->step_kvc) {
         float** h = (float**)malloc(c->n_layers * sizeof(float*));
         if (!h) { set_err("host allocation failed"); return 0; }
