@@ -43,7 +43,9 @@ def golden():
 
 
 @pytest.mark.parametrize("name", sorted(FM.CONFIGS))
-def test_forward_matches_engine(cuda, golden, name):
+def test_forward_matches_engine(cuda, golden, name, monkeypatch):
+    """Every token through the per-layer launches (five per layer)."""
+    monkeypatch.setenv("TGKV_FWD_STEP", "0")
     cfg = FM.CONFIGS[name]
     f = tgkv.Forward(cuda, fwd_config(cfg), FM.weights(cfg, FM.SEEDS[name]))
     try:
@@ -83,10 +85,7 @@ def test_long_prefill_and_decode_against_oracle(cuda, decode_path):
 def decode_path(request, monkeypatch):
     """Decode tokens through the per-layer launches, or through the
     one-launch decode step (all layers in one cooperative launch)."""
-    if request.param == "launches":
-        monkeypatch.delenv("TGKV_FWD_STEP", raising=False)
-    else:
-        monkeypatch.setenv("TGKV_FWD_STEP", "1")
+    monkeypatch.setenv("TGKV_FWD_STEP", "0" if request.param == "launches" else "1")
     return request.param
 
 

@@ -22,6 +22,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "tgkv_forward.h"
 
 namespace tgkvs {
@@ -50,28 +52,29 @@ __device__ __forceinline__ float silu_mul(float a, float b) { return (a / (1.0f 
 
 // Grid barrier over a counter that only grows within the launch: barrier b
 // completes when the counter reaches (b + 1) * gridDim.x.  Thread 0 of each
-// CTA makes the CTA's writes visible (fence) before it arrives and waits with
-// acquire loads; the result (1 = go on) is read by all threads of the CTA
-// from shared memory, so the CTA leaves together.
+// CTA arrives with a release reduction (the CTA's writes, ordered before it by
+// __syncthreads, become visible with it) and spins on acquire loads; the
+// result (1 = go on) is read by all threads of the CTA from shared memory, so
+// the CTA leaves together.
 __device__ __forceinline__ int grid_sync(uint32_t* bar, uint32_t& target, int* err, int* s_ok) {
     __syncthreads();
     if (threadIdx.x == 0) {
         target += gridDim.x;
-        __threadfence();
-        atomicAdd(bar, 1u);
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
         const long long t0 = clock64();
         int ok = 1;
-        while (true) {
+        for (uint32_t it = 0;; ++it) {
             uint32_t v;
             asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
             if (v >= target) break;
-            if (*(volatile int*)err) { ok = 0; break; }
-            if (clock64() - t0 > kSpinCycles) {
-                atomicExch(err, kErrBarrier);
-                ok = 0;
-                break;
+            if ((it & 63) == 63) {
+                if (*(volatile int*)err) { ok = 0; break; }
+                if (clock64() - t0 > kSpinCycles) {
+                    atomicExch(err, kErrBarrier);
+                    ok = 0;
+                    break;
+                }
             }
-            __nanosleep(64);
         }
         if (ok && *(volatile int*)err) ok = 0;
         *s_ok = ok;
@@ -459,11 +462,32 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
 
 namespace {
 
+// A step launch holds every SM for its whole duration, and two of them
+// resident at once could each wait at a barrier for CTAs the other one keeps
+// out.  Launches from different streams (forward slots) are therefore chained
+// on each device through one event: each waits for the previous one's end.
+constexpr int kMaxDevices = 64;
+std::mutex g_step_mu;
+cudaEvent_t g_step_done[kMaxDevices];
+
 template <int G>
 int launch_step(const TGFwdStepParams& p, size_t smem, uint32_t grid, cudaStream_t st) {
     void* args[] = {const_cast<TGFwdStepParams*>(&p)};
-    return (int)cudaLaunchCooperativeKernel((const void*)decode_step_kernel<G>, dim3(grid),
-                                            dim3(kThreads), args, smem, st);
+    int dev = 0;
+    cudaError_t e;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(g_step_mu);
+    cudaEvent_t& done = g_step_done[dev];
+    if (!done && (e = cudaEventCreateWithFlags(&done, cudaEventDisableTiming)) != cudaSuccess) {
+        done = nullptr;
+        return (int)e;
+    }
+    if ((e = cudaStreamWaitEvent(st, done, 0)) != cudaSuccess) return (int)e;
+    if ((e = cudaLaunchCooperativeKernel((const void*)decode_step_kernel<G>, dim3(grid),
+                                         dim3(kThreads), args, smem, st)) != cudaSuccess)
+        return (int)e;
+    return (int)cudaEventRecord(done, st);
 }
 
 template <int G>

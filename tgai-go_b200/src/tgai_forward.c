@@ -770,10 +770,11 @@ static int run_layer(TGFwdModel* m, Slot* s, uint32_t l, uint32_t seq, uint32_t 
 }
 
 /* One-token decode steps run as one cooperative launch over all layers
- * (tgkv_fwd_decode_step) with TGKV_FWD_STEP=1, where the model fits it. */
+ * (tgkv_fwd_decode_step) where the model fits it; TGKV_FWD_STEP=0 takes them
+ * through the per-layer launches instead. */
 static int step_on(void) {
     const char* e = getenv("TGKV_FWD_STEP");
-    return e && e[0] == '1';
+    return !(e && e[0] == '0');
 }
 
 /* All layers of one decode token at position pos (x holds its embedding);
