@@ -826,6 +826,9 @@ def run_fwd(args):
                        "experts": f"{cfg['n_experts']} top-{cfg['n_activated']}, d_ff {cfg['d_ff']}",
                        "vocab": cfg["vocab"], "context": f"{pos0}..{pos0 + args.steps}",
                        "parallelism": f"replicas x{world}",
+                       "decode_path": ("per-layer launches (TGKV_FWD_STEP=0)"
+                                       if os.environ.get("TGKV_FWD_STEP", "") == "0" else
+                                       "one cooperative launch per token over all layers"),
                        "l2": "weights read per token (3.4 GB) >> 126 MB L2"},
             "roofline": {"bound": "hbm", "kernel": "whole decode step", "achieved": achieved,
                          "peak": peak, "unit": "GB/s", "frac": achieved / peak,

@@ -754,7 +754,6 @@ static int run_layer(TGFwdModel* m, Slot* s, uint32_t l, uint32_t seq, uint32_t 
         return gemm(s, seq, d, dff, s->h, dff, L->w3, s->x, d, 1);
     }
     if (!gemm(s, seq, ne, d, s->ln, d, L->router, s->router, ne, 0)) return 0;
-    t_launches++;
     if (!tg_cuda_kv_memset(s->counts, 0, (size_t)ne * 4, st)) {
         set_err("memset: %s", tg_cuda_kv_last_error());
         return 0;
@@ -799,7 +798,6 @@ static int run_step(TGFwdModel* m, Slot* s, uint32_t pos) {
             return 0;
         }
     }
-    t_launches++;
     if (!tg_cuda_kv_memset(s->step_state, 0, state_n * 4, st)) {
         set_err("memset: %s", tg_cuda_kv_last_error());
         return 0;
@@ -850,7 +848,6 @@ static int run_forward(TGFwdModel* m, Slot* s, const int32_t* ids, uint32_t seq,
         tg_kv_advance(s->kv[l], pos);
     }
     memcpy(s->h_ids, ids, (size_t)seq * 4);
-    t_launches++;
     if (!tg_cuda_kv_h2d(s->ids, s->h_ids, (size_t)seq * 4, st)) {
         set_err("ids upload: %s", tg_cuda_kv_last_error());
         return 0;
@@ -872,7 +869,6 @@ static int run_forward(TGFwdModel* m, Slot* s, const int32_t* ids, uint32_t seq,
         CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, xl, m->fnorm, 1, d, d, d, 1e-6f, st));
         if (!gemm(s, 1, m->rows, d, s->ln, d, m->emb, s->logits, m->rows, 0)) return 0;
     }
-    t_launches++;
     if (!tg_cuda_kv_d2h(s->h_logits, s->logits, (size_t)m->rows * 4, st) || !tg_cuda_kv_sync(st)) {
         set_err("forward: %s", tg_cuda_kv_last_error());
         return 0;
