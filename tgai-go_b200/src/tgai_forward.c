@@ -675,11 +675,13 @@ static int decode_fits(uint32_t R, uint32_t K) {
  * NULL when the site is off. */
 static const float* pf(const float* w, int site) {
     static int mask = -1;
-    if (mask < 0) {
+    int v = __atomic_load_n(&mask, __ATOMIC_RELAXED);
+    if (v < 0) {
         const char* e = getenv("TGKV_PREFETCH");
-        mask = e && e[0] ? atoi(e) : 0;
+        v = e && e[0] ? atoi(e) & 15 : 0;
+        __atomic_store_n(&mask, v, __ATOMIC_RELAXED);
     }
-    return (mask & site) ? w : NULL;
+    return (v & site) ? w : NULL;
 }
 
 static int attn_half(TGFwdModel* m, Slot* s, const Layer* L, TGKvCache* kv, uint32_t seq,
