@@ -177,6 +177,18 @@ def lengths_for(wl, seed, rank):
     return rng.integers(wl["lmin"], wl["lmax"] + 1, wl["n_seq"]).astype(np.int64)
 
 
+def rank_lengths(wl, seed, rank, world, shard_seqs):
+    """Context lengths of this rank's sequences.  Weak scaling (default):
+    every rank serves its own set (values seeded per rank) with the 1-GPU
+    run's length profile, so per-GPU work is fixed as N grows.  shard_seqs
+    (strong scaling): the 1-GPU set split over the ranks by LPT on length."""
+    all_lens = lengths_for(wl, seed, 0)
+    if not shard_seqs:
+        return all_lens
+    import shard
+    return all_lens[shard.lpt_partition(all_lens, world)[rank]]
+
+
 def attn_bytes(lens_after, nh, nkv, hd, b=2):
     """Algorithmic bytes of one layer's decode call: K and V read once per KV
     head over L positions, the new row's append write, q read and out write."""
@@ -290,15 +302,7 @@ def run_ours(args):
     else:
         nkv, nh = wl["nkv"], wl["nh"]
     hd, layers = wl["hd"], wl["layers"]
-    if args.shard_seqs and not heads_sharded:
-        # strong scaling: the workload's sequences split over ranks by LPT
-        all_lens = lengths_for(wl, args.seed, 0)
-        mine = shard.lpt_partition(all_lens, world)[rank]
-        lens0 = all_lens[mine]
-    else:
-        # weak scaling: every rank serves its own 64 sequences (values seeded
-        # per rank) with the same length profile, so per-GPU work is fixed as N grows
-        lens0 = lengths_for(wl, args.seed, 0)
+    lens0 = rank_lengths(wl, args.seed, rank, world, args.shard_seqs and not heads_sharded)
     n_seq = len(lens0)
     kvd = nkv * hd
     e2e_steps = 0 if args.no_e2e else args.steps
