@@ -484,9 +484,13 @@ int launch_step(const TGFwdStepParams& p, size_t smem, uint32_t grid, cudaStream
         return (int)e;
     }
     if ((e = cudaStreamWaitEvent(st, done, 0)) != cudaSuccess) return (int)e;
-    if ((e = cudaLaunchCooperativeKernel((const void*)decode_step_kernel<G>, dim3(grid),
-                                         dim3(kThreads), args, smem, st)) != cudaSuccess)
-        return (int)e;
+    e = cudaLaunchCooperativeKernel((const void*)decode_step_kernel<G>, dim3(grid),
+                                    dim3(kThreads), args, smem, st);
+    if (e == cudaErrorCooperativeLaunchTooLarge) {
+        (void)cudaGetLastError();
+        return -1;                             // refused before anything ran
+    }
+    if (e != cudaSuccess) return (int)e;
     return (int)cudaEventRecord(done, st);
 }
 
@@ -499,7 +503,7 @@ int step_grid(size_t smem, uint32_t* grid) {
         return (int)e;
     if ((e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev)) != cudaSuccess)
         return (int)e;
-    if (!coop) return (int)cudaErrorNotSupported;
+    if (!coop) return -1;
     if (smem > 48 * 1024 &&
         (e = cudaFuncSetAttribute(decode_step_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)smem)) != cudaSuccess)
@@ -507,7 +511,7 @@ int step_grid(size_t smem, uint32_t* grid) {
     if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, decode_step_kernel<G>, kThreads,
                                                            smem)) != cudaSuccess)
         return (int)e;
-    if (per < 1) return (int)cudaErrorCooperativeLaunchTooLarge;
+    if (per < 1) return -1;
     *grid = (uint32_t)sms;                 // one CTA per SM
     return 0;
 }

@@ -111,6 +111,9 @@ int tgkv_fwd_step_supported(uint32_t d, uint32_t n_heads, uint32_t n_kv_heads, u
                             uint32_t dff, uint32_t ne, uint32_t na);
 size_t tgkv_fwd_step_smem(uint32_t d, uint32_t q_dim, uint32_t dff, uint32_t ne, uint32_t na);
 size_t tgkv_fwd_step_part_floats(uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim);
+/* 0 launched; -1 the device cannot hold the grid resident (no cooperative
+ * launch, or too few SMs for this process): nothing was queued; else a CUDA
+ * error code. */
 int tgkv_fwd_decode_step(const TGFwdStepParams* p, void* stream);
 
 /* Page-locked host memory (NULL on failure). */

@@ -146,6 +146,7 @@ struct TGFwdModel {
     Layer* L;
     float *emb, *fnorm, *cs, *sn;
     TGFwdStepLayer* step_layers;   /* device [n_layers], when the one-launch step fits */
+    int step_refused;              /* the device refused the step's grid: per-layer launches */
     uint64_t wbytes;
     pthread_mutex_t mu;
     Slot* slots;
@@ -779,7 +780,9 @@ static int step_on(void) {
 }
 
 /* All layers of one decode token at position pos (x holds its embedding);
- * the error word comes back with the logits. */
+ * the error word comes back with the logits.  1 queued, 0 failed, -1 the
+ * device refused the grid (nothing queued but a zeroing of the step state;
+ * the caller runs the per-layer launches). */
 static int run_step(TGFwdModel* m, Slot* s, uint32_t pos) {
     const TGFwdConfig* c = &m->c;
     void* st = s->stream;
@@ -828,7 +831,13 @@ static int run_step(TGFwdModel* m, Slot* s, uint32_t pos) {
     p.max_seq = c->max_seq_len;
     p.sx_floats = c->d_model > m->q_dim ? c->d_model : m->q_dim;
     p.scale = 1.0f / sqrtf((float)m->hd);
-    CHECK_LAUNCH(tgkv_fwd_decode_step(&p, st));
+    const int e = tgkv_fwd_decode_step(&p, st);
+    if (e < 0) {
+        __atomic_store_n(&m->step_refused, 1, __ATOMIC_RELAXED);
+        return -1;
+    }
+    t_launches++;
+    if (e) { set_err("decode step launch failed (CUDA error %d)", e); return 0; }
     for (uint32_t l = 0; l < c->n_layers; l++) tg_kv_advance(s->kv[l], 1);
     s->h_step[0] = -1;
     if (!tg_cuda_kv_d2h(s->h_step, s->step_state + 1, 4, st)) {
@@ -855,13 +864,16 @@ static int run_forward(TGFwdModel* m, Slot* s, const int32_t* ids, uint32_t seq,
         return 0;
     }
     CHECK_LAUNCH(tgkv_fwd_embed(s->x, m->emb, s->ids, seq, d, m->rows, c->unk_id, st));
-    const int step = seq == 1 && m->step_layers && step_on();
+    int step = seq == 1 && m->step_layers && step_on() &&
+               !__atomic_load_n(&m->step_refused, __ATOMIC_RELAXED);
     if (step) {
-        if (!run_step(m, s, pos)) return 0;
-    } else {
+        const int r = run_step(m, s, pos);
+        if (!r) return 0;
+        step = r > 0;
+    }
+    if (!step)
         for (uint32_t l = 0; l < c->n_layers; l++)
             if (!run_layer(m, s, l, seq, pos)) return 0;
-    }
     /* final norm of the last row, then the tied-embedding LM head */
     const float* xl = s->x + (uint64_t)(seq - 1) * d;
     if (decode_fits(1, d)) {
