@@ -799,6 +799,15 @@ static int run_step(TGFwdModel* m, Slot* s, uint32_t pos) {
         s->step_state = (uint32_t*)tg_cuda_kv_malloc(state_n * 4);
         s->h_step = (int32_t*)tgkv_fwd_host_alloc(16);
         if (!ok || !s->step_part || !s->step_state || !s->h_step) {
+            /* all or nothing: a later call allocates them again from scratch */
+            tg_cuda_kv_free(s->step_kvc);
+            tg_cuda_kv_free(s->step_part);
+            tg_cuda_kv_free(s->step_state);
+            tgkv_fwd_host_free(s->h_step);
+            s->step_kvc = NULL;
+            s->step_part = NULL;
+            s->step_state = NULL;
+            s->h_step = NULL;
             set_err("decode step buffers: allocation failed");
             return 0;
         }
