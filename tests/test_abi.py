@@ -98,3 +98,38 @@ def test_cuda_backend_without_device_reports_reason(lib):
     assert lib.tg_cuda_kv_last_error()
     assert lib.tg_gpu_backend_ready() == 0
     assert lib.tg_gpu_backend_name() == b"none"
+
+
+def test_static_attention_rejects_bad_arguments_before_any_device_call(lib):
+    """tg_kv_attention_static checks its arguments on the host first: each bad
+    call returns 0 with a reason and touches no device (so this runs without a
+    GPU).  Addresses are only compared for alignment, never dereferenced."""
+    kvc, q, out = 0x10000, 0x20000, 0x30000
+    cases = [
+        ((None, 0, 64, 2, 64, 8, q, out, 4, 1), b"null pointer"),
+        ((kvc, 0, 64, 2, 96, 8, q, out, 4, 1), b"no kernel for dtype 0 head_dim 96"),
+        ((kvc, 1, 64, 4, 64, 8, q, out, 6, 1), b"not a multiple"),
+        ((kvc, 0, 64, 2, 64, 8, q, out, 4, 9), b"need 1 <= n_q"),
+        ((kvc, 0, 64, 2, 64, 65, q, out, 4, 1), b"need 1 <= n_q"),
+        ((kvc, 0, 64, 2, 64, 8, q, out, 4, 0), b"need 1 <= n_q"),
+        ((kvc, 0, 4096, 2, 64, 2048, q, out, 4, 1025), b"above the limit of 1024"),
+        ((kvc + 8, 0, 64, 2, 64, 8, q, out, 4, 1), b"16-byte"),
+        ((kvc, 0, 64, 2, 64, 8, q + 4, out, 4, 1), b"8-byte"),
+    ]
+    for args, why in cases:
+        a = [C.c_void_p(x) if i in (0, 6, 7) else x for i, x in enumerate(args)]
+        assert lib.tg_kv_attention_static(*a, None) == 0, args
+        assert why in lib.tg_kv_last_error(), (args, lib.tg_kv_last_error())
+
+
+@pytest.mark.skipif(os.path.exists("/dev/nvidia0"), reason="CPU-only behaviour")
+def test_forward_create_fails_cleanly(lib):
+    import tgkv
+    assert not lib.tg_fwd_create(None, tgkv.WEIGHT_FN(lambda *a: None), None)
+    assert b"null argument" in lib.tg_fwd_last_error()
+    cfg = tgkv.TGFwdConfig(n_layers=1, d_model=64, n_heads=2, n_kv_heads=1, head_dim=0, d_ff=64,
+                           vocab_size=16, max_seq_len=8, n_experts=0, n_activated=0,
+                           rope_theta=10000.0, unk_id=0)
+    cb = tgkv.WEIGHT_FN(lambda *a: None)
+    assert not lib.tg_fwd_create(C.byref(cfg), cb, None)
+    assert lib.tg_fwd_last_error()
