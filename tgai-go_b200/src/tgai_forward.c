@@ -873,7 +873,12 @@ static int run_forward(TGFwdModel* m, Slot* s, const int32_t* ids, uint32_t seq,
         return 0;
     }
     CHECK_LAUNCH(tgkv_fwd_embed(s->x, m->emb, s->ids, seq, d, m->rows, c->unk_id, st));
+    /* The step's attention splits a KV head's context into at most
+     * kTgStepMaxTasks warp tasks; past 32 positions a task (4096 in all) the
+     * tasks grow long and few warps stream the cache, where the per-layer
+     * path's split attention kernel keeps HBM busy instead. */
     int step = seq == 1 && m->step_layers && step_on() &&
+               (uint64_t)pos + 1 <= (uint64_t)kTgStepMaxTasks * 32 &&
                !__atomic_load_n(&m->step_refused, __ATOMIC_RELAXED);
     if (step) {
         const int r = run_step(m, s, pos);
