@@ -139,10 +139,28 @@ int tg_kv_rope_tables(float theta, uint32_t head_dim, uint32_t pos0, uint32_t n_
  * function calls no cudaMalloc/cudaFree.  The first call on each device does a
  * one-time set-up (the array's device address) and should come before any
  * stream capture.  All calls share the array: calls that overlap on the GPU
- * (other streams, other threads) race; order them on one stream. */
+ * (other streams, other threads) race; order them on one stream.
+ *
+ * Its kernel's waits are bounded (about 2 s).  A wait that runs out leaves
+ * that call's output undefined and records a code in the array's error word,
+ * which later calls do not clear: read it with tg_kv_attention_static_error. */
 int tg_kv_attention_static(const void* kvc, int dtype, uint32_t max_seq, uint32_t n_kv_heads,
                            uint32_t head_dim, uint32_t kv_len, const float* q, float* out,
                            uint32_t n_heads, uint32_t n_q, void* stream);
+
+/* The error word of tg_kv_attention_static on the current device, after
+ * waiting for `stream`: 0 if every call since the last read finished its
+ * waits, else the code of a wait that ran out (1: a K/V stage never arrived,
+ * 2: a stage was never released); the word is cleared once returned.  -1 if
+ * the word could not be read (reason in tg_kv_last_error()).  Allocates
+ * nothing.  No counterpart in the reference. */
+int tg_kv_attention_static_error(void* stream);
+
+/* Failure injection for tests: the next n_calls calls of
+ * tg_kv_attention_static launch with their K/V loads held back, so their
+ * waits run out (about 2 s each) and report through
+ * tg_kv_attention_static_error.  0 cancels.  No counterpart in the reference. */
+void tg_kv_attention_static_inject_stall(int n_calls);
 
 /* ---- Batched decode over many caches (one layer of many sequences) ------- */
 

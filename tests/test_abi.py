@@ -123,6 +123,14 @@ def test_static_attention_rejects_bad_arguments_before_any_device_call(lib):
 
 
 @pytest.mark.skipif(os.path.exists("/dev/nvidia0"), reason="CPU-only behaviour")
+def test_static_error_reader_without_a_call(lib):
+    """The static entry's error reader answers 0 where no static call was ever
+    made (here: no device at all), and the stall hook only arms a counter."""
+    lib.tg_kv_attention_static_inject_stall(0)
+    assert lib.tg_kv_attention_static_error(None) == 0
+
+
+@pytest.mark.skipif(os.path.exists("/dev/nvidia0"), reason="CPU-only behaviour")
 def test_forward_create_fails_cleanly(lib):
     import tgkv
     assert not lib.tg_fwd_create(None, tgkv.WEIGHT_FN(lambda *a: None), None)

@@ -380,9 +380,11 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
         }
         // ---------------- producer: one tiled TMA box of K and one of V per
         // stage (32 rows of this KV head; rows past max_seq arrive as 0)
-        if (lane == 0) {
-            prefetch_tmap(cd.tmap);
+        if (lane == 0 && !p.stall_loads) {
+            const uint64_t tmap = cd.tmap ? cd.tmap : reinterpret_cast<uint64_t>(&p.tmap0);
+            prefetch_tmap(tmap);
             const int x = (int)(ck.kvh * HD);
+            int issued = 0;
             for (int t = 0; t < ntiles; ++t) {
                 const int s = t % C::NSTAGE;
                 if (t >= C::NSTAGE && !mbar_wait(&empty[s], ((t / C::NSTAGE) - 1) & 1)) {
@@ -393,9 +395,17 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
                 const int row0 = (int)(ck.pos0 + (uint32_t)t * kTile);
                 unsigned char* st = smem + s * C::STAGE;
                 mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * kTile * C::RB));
-                tma_load_3d(st, cd.tmap, x, row0, 0, &full[s]);
-                tma_load_3d(st + kTile * C::RB, cd.tmap, x, row0, 1, &full[s]);
+                tma_load_3d(st, tmap, x, row0, 0, &full[s]);
+                tma_load_3d(st + kTile * C::RB, tmap, x, row0, 1, &full[s]);
+                ++issued;
             }
+            // Keep the CTA alive until its last stages have landed, so that
+            // consumers that gave up early never leave copies in flight into
+            // shared memory.  No later tile reuses these stages, so each
+            // barrier stays in the phase its last copy completed.
+            for (int t = issued > C::NSTAGE ? issued - C::NSTAGE : 0; t < issued; ++t)
+                if (!mbar_wait(&full[t % C::NSTAGE], (t / C::NSTAGE) & 1))
+                    atomicExch(p.err, kErrFullTimeout);
         }
         return;
     }
@@ -428,7 +438,9 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
 
     for (int t = 0; t < ntiles; ++t) {
         const int s = t % C::NSTAGE;
-        if (!mbar_wait(&full[s], (t / C::NSTAGE) & 1)) {
+        // the warp leaves together: a lane that saw the stage complete while
+        // another gave up must not go on to the shuffles below alone
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (t / C::NSTAGE) & 1))) {
             if (lane == 0) { atomicExch(p.err, kErrFullTimeout); sm_flag[0] = 1; }
             break;
         }
@@ -848,17 +860,17 @@ extern "C" int tgkv_launch_rope_append(const TGKvRopeParams* p, void* stream) {
 // not allocate device memory -- code running where cudaMalloc is off limits
 // (inside a host allocator hook, a real-time decode thread with a fixed memory
 // budget, or an engine that hands this library only its own buffers).  Its
-// scratch (the CTA partials, the arrival counters, the cache's TMA tensor map
-// and an error word) lives in the file-scope device array below: 4 MiB that
-// every GPU which loads this library holds until the process exits.
+// scratch (the CTA partials, the arrival counters and an error word) lives in
+// the file-scope device array below: 4 MiB that every GPU which loads this
+// library holds until the process exits.  The cache's TMA tensor map travels
+// in the kernel's parameter block, so a call copies nothing from the host.
 extern "C" void tgkv_set_last_error(const char* msg);   // tgai_kv_cache.c
 
 namespace tgkv {
 namespace staticmem {
 
 constexpr size_t kBytes = 4u << 20;
-constexpr size_t kOffTmap = 0;        // 128-byte CUtensorMap
-constexpr size_t kOffErr = 128;       // bounded-wait error word
+constexpr size_t kOffErr = 0;         // bounded-wait error word, kept until read
 constexpr size_t kOffCounters = 256;  // arrival counters, then partials
 constexpr int kMaxDevices = 64;
 
@@ -873,6 +885,15 @@ std::mutex g_mu;
 unsigned char* g_addr[kMaxDevices];   // device address of g_scratch, per device
 int g_sms[kMaxDevices];
 EncodeTiledFn g_encode = nullptr;
+int g_stall_calls = 0;                // failure injection: calls left to stall
+
+// 1 if this call is to launch with its loads stalled (failure injection).
+uint32_t take_stall() {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_stall_calls <= 0) return 0;
+    --g_stall_calls;
+    return 1;
+}
 
 int fail(const char* fmt, ...) {
     char msg[256];
@@ -970,16 +991,17 @@ extern "C" __attribute__((visibility("default"))) int tg_kv_attention_static(
                     (unsigned long long)need, (unsigned long long)kBytes);
     const uint32_t grid = (uint32_t)n_chunks;
 
-    // The cache's tensor map goes into the static array on the stream, ahead
-    // of the kernel; the counters and the error word are cleared the same way
-    // (the previous call's contents are still there).
-    CUtensorMap tm;
+    // The cache's tensor map travels in the kernel's parameter block (tmap0);
+    // only the arrival counters are cleared on the stream, since the
+    // previous call's contents are still in the array.  The error word is
+    // left alone: it keeps a failed call's code until
+    // tg_kv_attention_static_error() has returned it.
     cuuint64_t dims[3] = {kv_dim, max_seq, 2};
     cuuint64_t strides[2] = {kv_dim * es, (uint64_t)max_seq * kv_dim * es};
     cuuint32_t box[3] = {head_dim, TGKV_TILE, 1};
     cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = g_encode(&tm, dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+    CUresult r = g_encode(&p.tmap0, dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                           3, const_cast<void*>(kvc), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -987,15 +1009,15 @@ extern "C" __attribute__((visibility("default"))) int tg_kv_attention_static(
         return fail("tg_kv_attention_static: cuTensorMapEncodeTiled failed (%d)", (int)r);
     unsigned char* base = g_addr[dev];
     cudaStream_t st = (cudaStream_t)stream;
-    cudaError_t e = cudaMemcpyAsync(base + kOffTmap, &tm, sizeof(tm), cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess) e = cudaMemsetAsync(base + kOffErr, 0, kOffCounters - kOffErr + counters, st);
+    cudaError_t e = cudaMemsetAsync(base + kOffCounters, 0, counters, st);
     if (e != cudaSuccess)
-        return fail("tg_kv_attention_static: staging failed: %s", cudaGetErrorString(e));
+        return fail("tg_kv_attention_static: clearing the counters failed: %s",
+                    cudaGetErrorString(e));
 
     p.caches = nullptr;
     p.cache0.base = (uint64_t)(uintptr_t)kvc;
     p.cache0.max_seq = max_seq;
-    p.cache0.tmap = (uint64_t)(uintptr_t)(base + kOffTmap);
+    p.cache0.tmap = 0;                     // the kernel uses p.tmap0
     p.q = q;
     p.out = out;
     p.counters = reinterpret_cast<uint32_t*>(base + kOffCounters);
@@ -1010,9 +1032,44 @@ extern "C" __attribute__((visibility("default"))) int tg_kv_attention_static(
     p.chunk = (uint32_t)chunk;
     p.qscale = (1.0f / sqrtf((float)head_dim)) * 1.4426950408889634f;
     p.item_base = 0;
+    p.stall_loads = take_stall();
     const int rc = tgkv_launch_attention(&p, dtype, head_dim, gt, grid, stream);
     if (rc != 0)
         return fail("tg_kv_attention_static: launch failed: %s",
                     cudaGetErrorString((cudaError_t)rc));
     return 1;
+}
+
+// The error word of the static array on the current device: 0 when every
+// call so far finished its waits, else the code of a wait that ran out.
+// Waits for `stream` first; clears the word once it has been returned.
+extern "C" __attribute__((visibility("default"))) int tg_kv_attention_static_error(void* stream) {
+    using namespace tgkv::staticmem;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+    unsigned char* base;
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        base = g_addr[dev];
+    }
+    if (!base) return 0;                  // no call was made on this device
+    cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+    int32_t v = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&v, base + kOffErr, sizeof(v), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && v) e = cudaMemset(base + kOffErr, 0, sizeof(v));
+    if (e != cudaSuccess) {
+        fail("tg_kv_attention_static_error: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return v;
+}
+
+// Failure injection for tests: the next n_calls calls of
+// tg_kv_attention_static launch with the producer issuing no loads, so each
+// of their waits runs out after its bound (about 2 s) and records its code.
+extern "C" __attribute__((visibility("default"))) void tg_kv_attention_static_inject_stall(
+    int n_calls) {
+    using namespace tgkv::staticmem;
+    std::lock_guard<std::mutex> lock(g_mu);
+    g_stall_calls = n_calls > 0 ? n_calls : 0;
 }

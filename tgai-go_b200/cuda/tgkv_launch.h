@@ -74,6 +74,12 @@ typedef struct {
     uint32_t* gather_flag[TGKV_MAX_RANKS];
     uint64_t  gather_base;
     uint32_t  gather_world;
+    /* Failure injection for tests: nonzero makes the producer issue no loads,
+     * so every wait of the launch runs out and reports through err. */
+    uint32_t  stall_loads;
+    /* Used when cache0.tmap is 0 (the no-allocation entry): the cache's tensor
+     * map travels in the parameter block itself. */
+    CUtensorMap tmap0;
     uint32_t n_pos[TGKV_MAX_ITEMS];
     uint32_t chunk_prefix[TGKV_MAX_ITEMS + 1];
 } TGKvAttnParams;

@@ -14,6 +14,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <strings.h>
 
 static _Thread_local char t_err[256] = "dispatch: no error";
 static char g_reason[256] = "not initialized";
@@ -29,13 +30,32 @@ static void set_err(const char* fmt, ...) {
 
 const char* tg_gpu_kv_error(void) { return t_err; }
 
+/* TG_BACKEND as the reference reads it (src/tgai_gpu_dispatch.c:467-492,
+ * case-insensitive): unset, "auto" or "cuda" bring the CUDA path up; "cpu"
+ * and "vulkan" are refused with a reason (this build has neither, and the
+ * KV-cache path never falls back); any other value is refused as unknown.
+ * A backend the caller already selected with tg_be_select is kept. */
 int tg_gpu_backend_init(void) {
     TGBackend* b = tg_be_current();
-    if (!b && !tg_be_select(NULL)) {
-        snprintf(g_reason, sizeof(g_reason), "no backend: %s", tg_cuda_kv_last_error());
-        return 0;
+    if (!b) {
+        const char* env = getenv("TG_BACKEND");
+        if (env && env[0] && strcasecmp(env, "auto") != 0 && strcasecmp(env, "cuda") != 0) {
+            if (strcasecmp(env, "cpu") == 0 || strcasecmp(env, "vulkan") == 0)
+                snprintf(g_reason, sizeof(g_reason),
+                         "TG_BACKEND=%s refused: this build routes the KV-cache path to CUDA "
+                         "only (no %s path, no fallback)", env, env);
+            else
+                snprintf(g_reason, sizeof(g_reason),
+                         "TG_BACKEND=%s not recognised (auto or cuda; cpu and vulkan are "
+                         "refused)", env);
+            return 0;
+        }
+        if (!tg_be_select("cuda")) {
+            snprintf(g_reason, sizeof(g_reason), "cuda: %s", tg_cuda_kv_last_error());
+            return 0;
+        }
+        b = tg_be_current();
     }
-    b = tg_be_current();
     if (b != &tg_backend_cuda) {
         snprintf(g_reason, sizeof(g_reason), "backend %s is not cuda", b ? b->name : "(none)");
         return 0;

@@ -91,6 +91,8 @@ PROTOS = {
     "tg_kv_bytes": (u64, [vp]),
     "tg_kv_download": (i32, [vp, vp]),
     "tg_kv_attention_static": (i32, [vp, i32, u32, u32, u32, u32, vp, vp, u32, u32, vp]),
+    "tg_kv_attention_static_error": (i32, [vp]),
+    "tg_kv_attention_static_inject_stall": (None, [i32]),
     "tg_kv_rope_tables": (i32, [fp, u32, u32, u32, u32, u32, PF, PF, PF]),
     "tg_kv_set_attn_mscale": (None, [vp, fp]),
     "tg_kv_batch_create": (vp, [C.POINTER(vp), u32, u32]),
