@@ -1,26 +1,28 @@
 """Benchmark of the KV-cache decode path (append + GQA decode attention).
 
-Default workload ("cfg4"): per GPU, 64 independent
-sequences with context lengths U[1k, 32k], 32 layers, 32 query / 8 KV heads,
-head_dim 128, bf16 caches.  One step = for every layer, one batched decode call
-(append of each sequence's new K/V row + split-sequence attention of its new
-query over the whole cache).  The metric is decode tokens/s (one token per
-sequence per step, all layers) and achieved HBM GB/s of the attention launches.
+Default workload ("cfg4"): 64 independent sequences
+with context lengths U[1k, 32k], 32 layers, 32 query / 8 KV heads, head_dim
+128, bf16 caches.  One step = for every layer, one batched decode call (append
+of each sequence's new K/V row + split-sequence attention of its new query
+over the whole cache).  The metric is decode tokens/s (one token per sequence
+per step, all layers) and achieved HBM GB/s of the attention launches.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload cfg4|cfg5|cfg2]
+                  [--workload cfg4|cfg5|cfg2|cfg3|fwd]
 
-N > 1 runs under torchrun, one rank per GPU.  cfg4 shards by sequences (each
-rank owns its own 64 with the length profile of the 1-GPU run; weak scaling,
-no collective on the data path).  cfg5
-(one 131072-token sequence) shards KV-head groups and all-gathers the per-head
-outputs with NCCL after every layer (strong scaling).
+N > 1 runs under torchrun, one rank per GPU.  The cfg4 headline shards the one
+set of 64 sequences over the ranks by longest-processing-time on length
+(strong scaling, no collective on the data path).  Beside it the same line
+carries `weak` (N > 1: every rank its own 64 sequences) and `cfg5`
+(configs[4]: one 131072-token sequence; at N > 1 its KV-head groups are split
+over the ranks and the attention kernel gathers the per-head outputs over
+NVLink).  `--workload cfg5|cfg2` runs those alone.
 
 Inputs are synthetic (seeded normal values; the reference names no dataset)
 and larger than L2 (126 MB) between timed iterations.  `--impl reference`
 times the reference algorithm's CPU path (the engine-order restatement of
 src/tgai_engine.c:3943-4011 in oracle/, all host threads) on a bounded sample
-of the same workload.
+of the same workload, extrapolated to the full step, with the same config.
 """
 import argparse
 import ctypes as C
@@ -42,7 +44,7 @@ METRIC = "decode attn+KV-append tokens/s & HBM GB/s vs ~8 TB/s peak at 1/2/4/8 B
 WORKLOADS = {
     # name: sequences per rank, layers, q heads, kv heads, head_dim, length range
     "cfg4": dict(n_seq=64, layers=32, nh=32, nkv=8, hd=128, lmin=1024, lmax=32768,
-                 desc="configs[3]: 64 seqs/GPU, L~U[1k,32k], 32 layers, 32q/8kv, hd128, bf16"),
+                 desc="configs[3]: 64 seqs, L~U[1k,32k], 32 layers, 32q/8kv, hd128, bf16"),
     "cfg5": dict(n_seq=1, layers=32, nh=32, nkv=8, hd=128, lmin=131072, lmax=131072,
                  desc="configs[4]: 1 seq, L=131072, 32 layers, 32q/8kv, hd128, bf16"),
     "cfg2": dict(n_seq=1, layers=24, nh=16, nkv=4, hd=128, lmin=4096, lmax=4096,
@@ -206,17 +208,23 @@ def dist_setup(args):
 
 
 def make_cpu_sample(wl, lens, seed, max_bytes=1.5e9):
-    """Shortest-first whole sequences of one layer as fp32 caches (the
-    reference has no bf16 cache), within max_bytes of host memory."""
+    """Whole sequences of one layer as fp32 caches (the reference has no bf16
+    cache), within max_bytes of host memory, taken at evenly spaced ranks of
+    the sorted lengths so that short and long contexts are both timed."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     nh, nkv, hd = wl["nh"], wl["nkv"], wl["hd"]
+    order = np.argsort(lens, kind="stable")
+    per_pos = 2 * nkv * hd * 4
+    mean_b = float(np.mean(lens)) * per_pos
+    k = int(max(1, min(len(lens), max_bytes // max(mean_b, 1.0))))
+    picks = order[np.unique(np.round(np.linspace(0, len(lens) - 1, k)).astype(int))]
     items, used = [], 0
-    for idx in np.argsort(lens):
+    for idx in picks:
         L = int(lens[idx])
-        b = 2 * L * nkv * hd * 4
+        b = L * per_pos
         if items and used + b > max_bytes:
-            break
+            continue
         items.append((O.normal(2 * L * nkv * hd, seed, int(idx), 9),
                       O.normal(nh * hd, seed, int(idx), 10), L))
         used += b
@@ -227,11 +235,11 @@ def time_cpu_sample(wl, lens, items, threads, budget_s):
     """Reference-order CPU decode (oracle/: the engine loop of
     src/tgai_engine.c:3943-4011, one query per sequence) over the sample until
     budget_s of CPU work; extrapolated by positions x layers to the full step.
-    Returns (tokens/s, description)."""
+    Returns (tokens/s, description, seconds timed)."""
     import oracle as O
     nh, nkv, hd = wl["nh"], wl["nkv"], wl["hd"]
     done, spent, n = 0, 0.0, 0
-    while spent < budget_s:
+    while spent < budget_s or n < len(items):
         kvc, q, L = items[n % len(items)]
         t0 = time.perf_counter()
         O.decode_batch([kvc], [q], [L], nh, nkv, hd, threads=threads)
@@ -239,35 +247,93 @@ def time_cpu_sample(wl, lens, items, threads, budget_s):
         done += L
         n += 1
     step_s = spent * float(np.sum(lens)) * wl["layers"] / done
-    desc = (f"{n} single-layer sequence decodes (L={items[0][2]}..{items[-1][2]}, the shortest "
-            f"{len(items)} of {len(lens)}), fp32 cache, {spent:.1f}s of CPU work, scaled by "
-            f"positions x {wl['layers']} layers to the full step")
-    return wl["n_seq"] / step_s, desc
+    ls = sorted(it[2] for it in items)
+    desc = (f"extrapolated: {n} single-layer sequence decodes over {len(items)} of the "
+            f"{len(lens)} sequences (L={ls[0]}..{ls[-1]}, evenly spaced ranks of the sorted "
+            f"lengths), fp32 cache, {spent:.1f}s of CPU work, scaled by positions x "
+            f"{wl['layers']} layers to the full step")
+    return len(lens) / step_s, desc, spent
+
+
+def workload(args, name):
+    wl = dict(WORKLOADS[name])
+    if args.seqs:
+        wl["n_seq"] = args.seqs
+    if args.layers:
+        wl["layers"] = args.layers
+    return wl
+
+
+def decode_mode(name, world, weak):
+    """How a decode workload spreads over `world` ranks: 'own' (every rank
+    its own copy of the set: weak scaling), 'lpt' (the one set of sequences
+    split by longest-processing-time: strong) or 'heads' (the KV heads of
+    the set split into groups, outputs gathered: strong)."""
+    if world == 1:
+        return "own"
+    if name == "cfg4":
+        return "own" if weak else "lpt"
+    return "heads"
+
+
+def job_lengths(wl, seed, world, mode):
+    """Context lengths of every sequence of the whole job (all ranks)."""
+    one = lengths_for(wl, seed, 0)
+    return np.tile(one, world) if mode == "own" else one
+
+
+def decode_config(args, name, world, mode):
+    """The `config` of a decode line: a function of the arguments only, so
+    the reference arm prints the same one."""
+    wl = workload(args, name)
+    lens = job_lengths(wl, args.seed, world, mode)
+    if mode == "heads":
+        par = f"kv-head groups x{world} + " + ("in-kernel NVLink gather" if args.gather == "fused"
+                                                else "NCCL all-gather")
+    elif mode == "lpt":
+        par = f"sequences x{world} (LPT split of one set), no collective"
+    else:
+        par = (f"sequences x{world} (own set per GPU), no collective" if world > 1 else
+               "one GPU")
+    return {"workload": name, "desc": wl["desc"], "layers": wl["layers"],
+            "sequences": int(len(lens)),
+            "kv_heads_per_gpu": wl["nkv"] // world if mode == "heads" else wl["nkv"],
+            "context_mean": float(np.mean(lens)),
+            "l2": "inputs larger than L2 (K/V read per step >> 126 MB)",
+            "parallelism": par}
 
 
 def run_reference(args):
-    """--impl reference: the reference algorithm's CPU path, all host threads."""
+    """--impl reference: the reference algorithm's CPU path, all host threads,
+    on the same workload and config as this arm."""
     world, rank, _ = dist_setup(args)
     if rank != 0:
         return
-    wl = WORKLOADS[args.workload]
-    lens = lengths_for(wl, args.seed, 0)
+    name = args.workload
+    wl = workload(args, name)
+    mode = decode_mode(name, world, args.weak)
+    lens = lengths_for(wl, args.seed, 0)     # the job repeats this set under 'own'
     threads = os.cpu_count() or 1
     items = make_cpu_sample(wl, lens, args.seed)
     budget = max(0.5, args.cpu_total_s / max(1, args.steps + args.warmup))
-    vals = []
+    vals, secs = [], []
     for i in range(args.warmup + args.steps):
-        tok, desc = time_cpu_sample(wl, lens, items, threads, budget)
+        tok, desc, spent = time_cpu_sample(wl, lens, items, threads, budget)
         if i >= args.warmup:
             vals.append(tok)
+            secs.append(spent)
     v = float(np.median(vals))
+    njob = len(job_lengths(wl, args.seed, world, mode))
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * wl["n_seq"] / float(np.median(vals)),
-        "higher_is_better": True, "scaling": "weak" if args.workload == "cfg4" else "strong",
+        # what each timed step took: a bounded sample of the workload
+        "ms_per_step": 1000.0 * float(np.median(secs)),
+        "full_step_ms_extrapolated": 1000.0 * njob / v,
+        "extrapolated": True,
+        "higher_is_better": True, "scaling": "weak" if mode == "own" and world > 1 else "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "desc": wl["desc"]},
+        "config": decode_config(args, name, world, mode),
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": desc},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -276,33 +342,22 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args):
+def decode_run(args, lib, name, world, rank, local, mode, cpu=False):
+    """One decode workload: fill the caches, time `steps` decode steps on the
+    device and again through host buffers, free everything.  Every rank
+    returns the same summary (times are the max over ranks)."""
     import torch
     import torch.distributed as dist
     import tgkv
-
-    world, rank, local = dist_setup(args)
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-    lib = tgkv.load()
-    tgkv.check(lib.tg_cuda_kv_set_device(local), lib, "set_device")
-    tgkv.check(lib.tg_be_select(b"cuda"), lib, "tg_be_select")
-    wl = dict(WORKLOADS[args.workload])
-    if args.seqs:
-        wl["n_seq"] = args.seqs
-    if args.layers:
-        wl["layers"] = args.layers
     import shard
-    heads_sharded = args.workload != "cfg4" and world > 1
-    if heads_sharded:
+    wl = workload(args, name)
+    if mode == "heads":
         kv0, kv1, q0, q1 = shard.kv_head_shard(wl["nh"], wl["nkv"], world, rank)
         nkv, nh = kv1 - kv0, q1 - q0
     else:
         nkv, nh = wl["nkv"], wl["nh"]
     hd, layers = wl["hd"], wl["layers"]
-    lens0 = rank_lengths(wl, args.seed, rank, world, args.shard_seqs and not heads_sharded)
+    lens0 = rank_lengths(wl, args.seed, rank, world, mode == "lpt")
     n_seq = len(lens0)
     kvd = nkv * hd
     e2e_steps = 0 if args.no_e2e else args.steps
@@ -338,22 +393,22 @@ def run_ours(args):
     kn = [torch.randn(n_seq, kvd, device="cuda", generator=gen) for _ in range(layers)]
     vn = [torch.randn(n_seq, kvd, device="cuda", generator=gen) for _ in range(layers)]
     out = [torch.empty(n_seq, nh, hd, device="cuda") for _ in range(layers)]
+    heads = mode == "heads"
     gathered = ([torch.empty(world, n_seq, nh, hd, device="cuda") for _ in range(layers)]
-                if heads_sharded else None)
+                if heads else None)
     # in-kernel gather over NVLink: every rank's attention stores its heads'
-    # outputs into every rank's gathered buffer (CUDA IPC peer memory)
-    fused = heads_sharded and args.gather == "fused"
-    gathers = []
+    # outputs into every rank's gathered buffer (CUDA IPC peer memory); one
+    # gather object serves every layer and step
+    fused = heads and args.gather == "fused"
+    gather = None
     if fused:
-        for l in range(layers):
-            g = lib.tg_kv_gather_create(world, rank, n_seq * nh * hd)
-            tgkv.check(g, lib, "tg_kv_gather_create")
-            h = (C.c_uint8 * 64)()
-            tgkv.check(lib.tg_kv_gather_export(g, h), lib, "tg_kv_gather_export")
-            allh = [None] * world
-            dist.all_gather_object(allh, bytes(h))
-            tgkv.check(lib.tg_kv_gather_import(g, b"".join(allh)), lib, "tg_kv_gather_import")
-            gathers.append(g)
+        gather = lib.tg_kv_gather_create(world, rank, n_seq * nh * hd)
+        tgkv.check(gather, lib, "tg_kv_gather_create")
+        h = (C.c_uint8 * 64)()
+        tgkv.check(lib.tg_kv_gather_export(gather, h), lib, "tg_kv_gather_export")
+        allh = [None] * world
+        dist.all_gather_object(allh, bytes(h))
+        tgkv.check(lib.tg_kv_gather_import(gather, b"".join(allh)), lib, "tg_kv_gather_import")
     launches = [0]
 
     def step(events=None):
@@ -363,7 +418,7 @@ def run_ours(args):
             if fused:
                 ok = lib.tg_kv_batch_decode_gather(plans[l], q[l].data_ptr(), kn[l].data_ptr(),
                                                    vn[l].data_ptr(), out[l].data_ptr(),
-                                                   gathers[l], sh)
+                                                   gather, sh)
             else:
                 ok = lib.tg_kv_batch_decode(plans[l], q[l].data_ptr(), kn[l].data_ptr(),
                                             vn[l].data_ptr(), out[l].data_ptr(), sh)
@@ -372,7 +427,7 @@ def run_ours(args):
             launches[0] += lib.tg_kv_batch_last_launches(plans[l])
             if events is not None:
                 events[l][1].record(stream)
-            if heads_sharded and not fused:
+            if heads and not fused:
                 dist.all_gather_into_tensor(gathered[l], out[l])
 
     def barrier():
@@ -390,7 +445,7 @@ def run_ours(args):
     clocks.start()
     ev = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
           for _ in range(layers * args.steps)]
-    lens_step = [np.array([lib.tg_kv_len(caches[0][i]) for i in range(n_seq)]) + 1]
+    lens_step = np.array([lib.tg_kv_len(caches[0][i]) for i in range(n_seq)]) + 1
     launches[0] = 0
     barrier()
     t0 = torch.cuda.Event(enable_timing=True)
@@ -399,7 +454,7 @@ def run_ours(args):
     # step is nothing but the per-layer attention launches, back to back, and
     # events between them would break their programmatic-dependent overlap
     # (a 13 us cfg2 call measured 21 us with them).
-    per_call_events = heads_sharded and not fused
+    per_call_events = heads and not fused
     t0.record(stream)
     for s_ in range(args.steps):
         step(ev[s_ * layers:(s_ + 1) * layers] if per_call_events else None)
@@ -408,16 +463,20 @@ def run_ours(args):
     clock = clocks.stop()
     timed_launches = launches[0]
     kid = lib.tg_cuda_kv_attn_last_kernel()
-    kfam = {1: "attention_kernel (CUDA cores)", 3: "attention_tc_kernel (tcgen05)"}.get(kid, "?")
     ms = t0.elapsed_time(t1) / args.steps
     ms_max = max_over_ranks(ms)
-    algo = sum(attn_bytes(lens_step[0] + s_, nh, nkv, hd) for s_ in range(args.steps)) * layers
+    algo = sum(attn_bytes(lens_step + s_, nh, nkv, hd) for s_ in range(args.steps)) * layers
     if per_call_events:
         call_ms = sum(a.elapsed_time(b) for a, b in ev)
     else:
         call_ms = ms * args.steps                      # the timed region is the calls
     kernel_gbs = algo / (call_ms / 1000.0) / 1e9
+    # the slowest rank's achieved bandwidth and the least-loaded rank's
+    gbs_min = -max_over_ranks(-kernel_gbs)
     per_launch_bytes = algo / (args.steps * layers)
+    # tokens per step over all ranks: the whole sequence set once (sharded
+    # heads or LPT-split sequences), else every rank's own sequences
+    tokens = n_seq * world if mode == "own" else wl["n_seq"]
 
     # ---- end to end: host buffers, copies inside the timed region
     e2e = None
@@ -434,14 +493,14 @@ def run_ours(args):
                 if fused:       # out_host receives every rank's outputs
                     ok = lib.tg_kv_batch_decode_gather_host(
                         plans[l], qh[l].data_ptr(), kh[l].data_ptr(), vh[l].data_ptr(),
-                        oh[l].data_ptr(), gathers[l], sh)
+                        oh[l].data_ptr(), gather, sh)
                 else:
                     ok = lib.tg_kv_batch_decode_host(plans[l], qh[l].data_ptr(),
                                                      kh[l].data_ptr(), vh[l].data_ptr(),
                                                      oh[l].data_ptr(), sh)
                 if not ok:
                     raise RuntimeError(lib.tg_kv_last_error().decode())
-                if heads_sharded and not fused:
+                if heads and not fused:
                     dist.all_gather_into_tensor(gathered[l], out[l])
 
         for _ in range(e2e_warm):
@@ -457,27 +516,24 @@ def run_ours(args):
         e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
         h2d = layers * (qh[0].numel() + 2 * kh[0].numel()) * 4
         d2h = layers * oh[0].numel() * 4
-        tokens = wl["n_seq"] if (heads_sharded or args.shard_seqs) else n_seq * world
         e2e = {"value": tokens / (e_ms / 1000.0), "unit": "tokens/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e_ms}
 
     err = lib.tg_cuda_kv_device_error()
-    if gathers:
-        barrier()                 # no rank still writes into a peer's buffer
-        for g in gathers:
-            lib.tg_kv_gather_destroy(g)
+    barrier()                     # no rank still writes into a peer's buffer
+    if gather:
+        lib.tg_kv_gather_destroy(gather)
     for b in plans:
         lib.tg_kv_batch_destroy(b)
     for row in caches:
         for c in row:
             lib.tg_kv_destroy(c)
+    del q, kn, vn, out, gathered
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
     if err:
         raise RuntimeError(f"kernel bounded wait expired (code {err})")
 
-    # tokens per step over all ranks: the whole sequence set once (sharded
-    # heads or LPT-split sequences), else every rank's own sequences
-    tokens = wl["n_seq"] if (heads_sharded or args.shard_seqs) else n_seq * world
-    value = tokens / (ms_max / 1000.0)
     peak, peak_kind = measured_peak()
     traffic = None
     tp = os.path.join(ROOT, "profiles", "attention_dram_ratio.json")
@@ -488,48 +544,91 @@ def run_ours(args):
             traffic = per_launch_bytes * float(json.load(open(tp))[key])
         except Exception:
             traffic = None
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    cpu_line = None
+    if cpu and rank == 0 and world == 1 and not args.no_cpu:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         items = make_cpu_sample(wl, lens0, args.seed)
-        tok, desc = time_cpu_sample(wl, lens0, items, 1, args.cpu_baseline_s)
-        cpu = {"value": tok, "unit": "tokens/s", "cores": 1, "kind": "port", "sample": desc}
+        tok, desc, _ = time_cpu_sample(wl, lens0, items, 1, args.cpu_baseline_s)
+        cpu_line = {"value": tok, "unit": "tokens/s", "cores": 1, "kind": "port",
+                    "sample": desc}
+    return {
+        "value": tokens / (ms_max / 1000.0), "ms_per_step": ms_max, "tokens_per_step": tokens,
+        "kernel_gbs": kernel_gbs, "algo": algo, "per_launch_bytes": per_launch_bytes,
+        "roofline": {"bound": "hbm", "achieved": kernel_gbs, "peak": peak, "unit": "GB/s",
+                     "frac": kernel_gbs / peak, "traffic": traffic, "peak_source": peak_kind,
+                     "min_rank_frac": gbs_min / peak,
+                     "kernel": ("tg_kv_batch_decode per layer (append fused into the "
+                                "split-sequence attention launch): CUDA events on the launch "
+                                "stream, " + ("around every call" if per_call_events else
+                                              "around the timed region, which holds only "
+                                              "these calls")),
+                     "algorithmic_bytes_per_launch": per_launch_bytes},
+        "hbm_gbs": algo / (ms * args.steps / 1000.0) / 1e9,
+        "gpu_launches": timed_launches, "clocks": clock, "e2e": e2e, "cpu_baseline": cpu_line,
+        "details": {"attention_kernel": {1: "attention_kernel (CUDA cores)",
+                                         3: "attention_tc_kernel (tcgen05)"}.get(kid, "?"),
+                    "sequences_per_gpu": n_seq, "query_heads_per_gpu": nh,
+                    "fill_s": round(t_fill, 1)},
+    }
+
+
+def sub_record(args, name, world, mode, r):
+    """A decode run beside the headline, in the same units."""
+    return {"workload": name, "value": r["value"], "unit": "tokens/s",
+            "ms_per_step": r["ms_per_step"],
+            "scaling": "weak" if mode == "own" and world > 1 else "strong",
+            "config": decode_config(args, name, world, mode),
+            "roofline": r["roofline"], "e2e": r["e2e"], "gpu_launches": r["gpu_launches"],
+            "clocks": r["clocks"], "details": r["details"]}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import tgkv
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    lib = tgkv.load()
+    tgkv.check(lib.tg_cuda_kv_set_device(local), lib, "set_device")
+    tgkv.check(lib.tg_be_select(b"cuda"), lib, "tg_be_select")
+    name = args.workload
+    mode = decode_mode(name, world, args.weak)
+    r = decode_run(args, lib, name, world, rank, local, mode, cpu=True)
+    extra = {}
+    if name == "cfg4" and not args.no_extra:
+        # beside the headline: every GPU with its own 64 sequences (weak
+        # scaling) at N > 1, and configs[4] (one 131072-token sequence; KV
+        # heads split over the GPUs at N > 1)
+        if world > 1 and mode != "own":
+            extra["weak"] = sub_record(args, "cfg4", world, "own",
+                                       decode_run(args, lib, "cfg4", world, rank, local, "own"))
+        m5 = decode_mode("cfg5", world, False)
+        extra["cfg5"] = sub_record(args, "cfg5", world, m5,
+                                   decode_run(args, lib, "cfg5", world, rank, local, m5))
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+            "metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
             "higher_is_better": True,
-            "scaling": "strong" if (heads_sharded or args.shard_seqs) else "weak",
+            "scaling": "weak" if mode == "own" and world > 1 else "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": args.workload, "desc": wl["desc"],
-                       "layers": layers,
-                       "sequences_per_gpu": n_seq,
-                       "kv_heads_per_gpu": nkv, "context_mean": float(lens0.mean()),
-                       "l2": "inputs larger than L2 (K/V read per step >> 126 MB)",
-                       "parallelism": (f"kv-head groups x{world} + "
-                                       + ("in-kernel NVLink gather" if fused else "NCCL all-gather")
-                                       if heads_sharded else
-                                       f"sequences x{world} ({'LPT split' if args.shard_seqs else 'own set per GPU'}), no collective"),
-                       "attention_kernel": kfam,
-                       "fill_s": round(t_fill, 1)},
-            "hbm_gbs": algo / (ms * args.steps / 1000.0) / 1e9,
-            "roofline": {"bound": "hbm", "achieved": kernel_gbs, "peak": peak, "unit": "GB/s",
-                         "frac": kernel_gbs / peak, "traffic": traffic,
-                         "peak_source": peak_kind,
-                         "kernel": ("tg_kv_batch_decode per layer (append fused into the "
-                                    "split-sequence attention launch): CUDA events on the launch "
-                                    "stream, " + ("around every call" if per_call_events else
-                                                  "around the timed region, which holds only "
-                                                  "these calls")),
-                         "algorithmic_bytes_per_launch": per_launch_bytes},
-            "gpu_launches": timed_launches,
-            "clocks": clock,
-            "e2e": e2e,
-            "cpu_baseline": cpu,
+            "config": decode_config(args, name, world, mode),
+            "hbm_gbs": r["hbm_gbs"],
+            "roofline": r["roofline"],
+            "gpu_launches": r["gpu_launches"],
+            "clocks": r["clocks"],
+            "e2e": r["e2e"],
+            "cpu_baseline": r["cpu_baseline"],
+            "details": r["details"],
         }
+        line.update(extra)
         print(json.dumps(line), flush=True)
     if world > 1:
-        barrier()
+        dist.barrier(device_ids=[local])
         dist.destroy_process_group()
 
 
@@ -599,6 +698,24 @@ def run_cfg3(args):
     tokens = sum(n for _, n in timed)
     # causal suffix attention FLOPs (QK^T + PV) over all layers
     flops = sum(4.0 * nh * hd * sum(l + j + 1 for j in range(n)) for l, n in timed) * layers
+
+    # The appends alone: the same turns' truncate + append of every layer, no
+    # attention, timed as one region (the append launches back to back).
+    a0 = torch.cuda.Event(enable_timing=True)
+    a1 = torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for lcp, n in timed:
+        for l in range(layers):
+            c = caches[l]
+            tgkv.check(lib.tg_kv_truncate(c, min(lcp, lib.tg_kv_len(c))), lib, "truncate")
+            tgkv.check(lib.tg_kv_append_dev(c, k[l].data_ptr(), v[l].data_ptr(), n, sh), lib,
+                       "append")
+    a1.record(stream)
+    torch.cuda.synchronize()
+    a_ms = a0.elapsed_time(a1)
+    rows = sum(n for _, n in timed) * layers
+    app_write = 2.0 * rows * kvd * 2          # K and V rows written, bf16
+    app_read = 2.0 * rows * kvd * 4           # K and V rows read, fp32
     for c in caches:
         lib.tg_kv_destroy(c)
     line = {"metric": METRIC, "value": tokens / (ms / 1000.0), "unit": "tokens/s", "n_gpus": 1,
@@ -607,7 +724,12 @@ def run_cfg3(args):
             "data": "synthetic",
             "config": {"workload": "cfg3", "desc": wl["desc"], "turns": timed,
                        "attention_kernel": kernel},
-            "attention_tflops": flops / (ms / 1000.0) / 1e12}
+            "attention_tflops": flops / (ms / 1000.0) / 1e12,
+            "append": {"ms_per_turn": a_ms / len(timed),
+                       "write_gbs": app_write / (a_ms / 1000.0) / 1e9,
+                       "read_write_gbs": (app_write + app_read) / (a_ms / 1000.0) / 1e9,
+                       "launches_per_turn": layers,
+                       "bytes": "write: 2 x rows x kv_dim x 2 B (bf16); read: the fp32 rows"}}
     print(json.dumps(line), flush=True)
 
 
@@ -725,6 +847,8 @@ def run_fwd(args):
     needs), after a 512-token prefill."""
     world, rank, _ = dist_setup(args)
     cfg = dict(FWD)
+    if args.layers:                  # a cut-down model for small profiling captures
+        cfg["n_layers"] = args.layers
     prefill = 512
     threads = os.cpu_count() or 1
     if args.impl == "reference":
@@ -862,9 +986,11 @@ def main():
                     help="sequences per GPU (default: the workload's); for small profiling cases")
     ap.add_argument("--layers", type=int, default=0,
                     help="layers (default: the workload's); for small profiling cases")
-    ap.add_argument("--shard-seqs", action="store_true",
-                    help="cfg4: split the workload's sequences over ranks (LPT, strong scaling) "
-                         "instead of a full set per GPU (weak scaling)")
+    ap.add_argument("--weak", action="store_true",
+                    help="cfg4 at N > 1: every GPU its own set of sequences (weak scaling) as "
+                         "the headline, instead of the one set split over the GPUs (strong)")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="cfg4: only the headline (no weak-scaling or cfg5 record beside it)")
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
                     help="KV heads split over ranks (cfg5/cfg2 at N>1): outputs gathered by the "
                          "attention kernel over NVLink (fused) or by an NCCL all-gather")

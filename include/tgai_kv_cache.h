@@ -203,8 +203,9 @@ uint32_t tg_kv_batch_last_launches(const TGKvBatch* b);
 typedef struct TGKvGather TGKvGather;
 
 /* This rank's side of a gather among `world` ranks (<= 8): one device
- * allocation holding the gathered outputs [world][elems] fp32 (rank r's at
- * [r*elems, (r+1)*elems)) and an arrival counter.  NULL on failure. */
+ * allocation holding two buffers of gathered outputs [world][elems] fp32
+ * (rank r's at [r*elems, (r+1)*elems)), used by alternate calls, and an
+ * arrival counter for each.  NULL on failure. */
 TGKvGather* tg_kv_gather_create(uint32_t world, uint32_t rank, uint64_t elems);
 /* Closes the peers' buffers and frees this rank's.  Call on every rank after
  * all ranks have finished their last gathered step (a barrier). */
@@ -215,13 +216,21 @@ int tg_kv_gather_export(const TGKvGather* g, void* handle64);
  * order (this rank's own entry is not opened).  Every rank exports before any
  * rank imports. */
 int tg_kv_gather_import(TGKvGather* g, const void* handles);
-/* Device address of this rank's gathered outputs [world][elems]. */
+/* Device address of the gathered outputs [world][elems] of the last call on
+ * this object (the first buffer before any call). */
 float* tg_kv_gather_buffer(const TGKvGather* g);
 
 /* tg_kv_batch_decode whose outputs also land in every rank's gathered buffer
  * (this rank's slice: elems = n * n_heads * head_dim), followed by a wait on
  * `stream` until every rank's outputs of this step have arrived here.  All
- * ranks make the same sequence of calls with plans of the same shape. */
+ * ranks make the same sequence of calls with plans of the same shape.
+ *
+ * One gather object can serve every layer and step.  A call's gathered
+ * outputs (tg_kv_gather_buffer right after it) stay valid until the call after
+ * next on the object, on every rank: queue their consumers on `stream` before
+ * this rank's next call on the object (or order them before it with an
+ * event); the next call's stores then go to the other buffer, and no rank's
+ * call after that starts storing before this rank's next call has run. */
 int tg_kv_batch_decode_gather(TGKvBatch* b, const float* q, const float* k_new,
                               const float* v_new, float* out, TGKvGather* g, void* stream);
 /* The same from host buffers; out_host receives the whole gathered

@@ -428,14 +428,25 @@ uint32_t tg_kv_batch_last_launches(const TGKvBatch* b) { return b ? b->last_laun
 
 #define TGKV_GATHER_MAX 8
 
+/* Two halves of [world][elems] gathered outputs and one arrival counter per
+ * half, used by alternate calls.  A call's outputs stay in their half until
+ * the call after next: before any rank's call n+2 stores into a peer's half,
+ * that rank has waited for every rank's call n+1 arrivals, and a rank's call
+ * n+1 kernel runs only after the work it queued on its stream before that call
+ * -- the consumers of call n's outputs -- has finished.  The counters are
+ * separate for the same reason: no arrival of call n+2 can reach a counter
+ * before its owner has finished waiting for call n. */
 struct TGKvGather {
     uint32_t world, rank;
     uint64_t elems;                   /* outputs of one rank */
-    uint64_t flag_off;                /* byte offset of the arrival counter */
+    uint64_t half_bytes;              /* one half: [world][elems] fp32, 256-byte multiple */
+    uint64_t flag_off;                /* byte offset of the two arrival counters (128 B apart) */
     unsigned char* mem;               /* this rank's allocation */
     unsigned char* peer[TGKV_GATHER_MAX];   /* every rank's allocation (own at [rank]) */
     int imported;
-    uint32_t target;                  /* arrivals expected after the last step */
+    uint64_t calls;                   /* gathered calls so far; call n uses half n & 1 */
+    uint32_t last_half;               /* half of the last call */
+    uint32_t target[2];               /* arrivals expected per half after the last call */
 };
 
 TGKvGather* tg_kv_gather_create(uint32_t world, uint32_t rank, uint64_t elems) {
@@ -449,7 +460,8 @@ TGKvGather* tg_kv_gather_create(uint32_t world, uint32_t rank, uint64_t elems) {
     g->world = world;
     g->rank = rank;
     g->elems = elems;
-    g->flag_off = ((uint64_t)world * elems * 4 + 255) / 256 * 256;
+    g->half_bytes = ((uint64_t)world * elems * 4 + 255) / 256 * 256;
+    g->flag_off = 2 * g->half_bytes;
     g->mem = (unsigned char*)tg_cuda_kv_malloc((size_t)(g->flag_off + 256));   /* zeroed */
     if (!g->mem) {
         set_err("gather: %s", tg_cuda_kv_last_error());
@@ -489,7 +501,9 @@ int tg_kv_gather_import(TGKvGather* g, const void* handles) {
     return 1;
 }
 
-float* tg_kv_gather_buffer(const TGKvGather* g) { return g ? (float*)g->mem : NULL; }
+float* tg_kv_gather_buffer(const TGKvGather* g) {
+    return g ? (float*)(g->mem + (uint64_t)g->last_half * g->half_bytes) : NULL;
+}
 
 /* One decode step of the plan; with g, the outputs also go to every rank's
  * gathered buffer and the stream then waits for all ranks' outputs. */
@@ -527,12 +541,13 @@ static int batch_decode(TGKvBatch* b, const float* q, const float* k_new, const 
     call.counters = b->counters;
     call.k_new = k_new;               /* the append runs inside the attention launch */
     call.v_new = v_new;
+    const uint32_t half = g ? (uint32_t)(g->calls & 1u) : 0;
     if (g) {
         call.gather_world = g->world;
         call.gather_base = (uint64_t)g->rank * g->elems;
         for (uint32_t r = 0; r < g->world; r++) {
-            call.gather_out[r] = (float*)g->peer[r];
-            call.gather_flag[r] = (uint32_t*)(g->peer[r] + g->flag_off);
+            call.gather_out[r] = (float*)(g->peer[r] + (uint64_t)half * g->half_bytes);
+            call.gather_flag[r] = (uint32_t*)(g->peer[r] + g->flag_off + 128u * half);
         }
     }
     if (tg_be_current() != &tg_backend_cuda) {
@@ -548,8 +563,11 @@ static int batch_decode(TGKvBatch* b, const float* q, const float* k_new, const 
     if (g) {
         /* every rank finishes the same number of segments and signals each
          * rank once per segment */
-        g->target += g->world * (uint32_t)tg_cuda_kv_attn_segments(&call);
-        if (!tg_cuda_kv_gather_wait((const uint32_t*)(g->mem + g->flag_off), g->target, stream)) {
+        g->target[half] += g->world * (uint32_t)tg_cuda_kv_attn_segments(&call);
+        g->calls++;
+        g->last_half = half;
+        if (!tg_cuda_kv_gather_wait((const uint32_t*)(g->mem + g->flag_off + 128u * half),
+                                    g->target[half], stream)) {
             set_err("%s", tg_cuda_kv_last_error());
             return 0;
         }
@@ -613,7 +631,7 @@ static int batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_h
     if (!ok) { set_err("%s", tg_cuda_kv_last_error()); return 0; }
     float* direct = g ? NULL : (float*)tg_cuda_kv_host_device_ptr(out_host);
     if (!batch_decode(b, q, k, v, direct ? direct : o, g, stream)) return 0;
-    const void* src = g ? (const void*)g->mem : (const void*)o;
+    const void* src = g ? (const void*)tg_kv_gather_buffer(g) : (const void*)o;
     const uint64_t ob = g ? (uint64_t)g->world * g->elems * 4 : qb;
     if ((!direct && !tg_cuda_kv_d2h(out_host, src, ob, stream)) ||
         !tg_cuda_kv_event_record(b->slot_free[s], stream)) {
