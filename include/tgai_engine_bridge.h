@@ -124,6 +124,18 @@ int      tg_fwd_slot_last_pos(const TGFwdModel* m, const void* key);
 uint64_t tg_fwd_weight_bytes(const TGFwdModel* m);
 /* Kernel launches and GEMM calls issued by the last forward of this thread. */
 uint32_t tg_fwd_last_launches(void);
+
+/* The fp32 GEMM the forward's prefill runs, as a standalone call on device
+ * buffers: out[M][N] (row stride ldo) = x[M][K] . w[N][K]^T (row strides ldx,
+ * ldw), or += with accumulate, on the sm_100a tensor cores at fp32-product
+ * accuracy (each operand split into its tf32 part and exact remainder, three
+ * products summed).  K, ldx and ldw multiples of 4.  Allocates the split
+ * operands for the call and waits for `stream`.  1 = done, 0 = failed (reason
+ * in tg_fwd_last_error).  Replaces the reference bridge's gemm_f32 /
+ * cublasSgemm (cuda/tgai_cuda.cu:473-479). */
+int tg_fwd_gemm_f32(uint32_t M, uint32_t N, uint32_t K, const float* x, uint32_t ldx,
+                    const float* w, uint32_t ldw, float* out, uint32_t ldo, int accumulate,
+                    void* stream);
 const char* tg_fwd_last_error(void);
 
 #ifdef __cplusplus

@@ -348,6 +348,8 @@ int tg_cuda_kv_sync(void* stream) {
     return cuda_ok(cudaStreamSynchronize((cudaStream_t)stream), "stream sync");
 }
 
+__attribute__((visibility("hidden"))) int32_t* tgkv_bridge_err_word(void) { return g_err_word; }
+
 int tg_cuda_kv_device_error(void) {
     if (!g_ready) return 0;
     int32_t v = 0;

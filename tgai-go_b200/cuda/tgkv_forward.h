@@ -6,6 +6,7 @@
 
 #include <stddef.h>
 #include <stdint.h>
+#include <cuda.h>                 /* CUtensorMap */
 
 #ifdef __cplusplus
 extern "C" {
@@ -115,6 +116,38 @@ size_t tgkv_fwd_step_part_floats(uint32_t n_heads, uint32_t n_kv_heads, uint32_t
  * launch, or too few SMs for this process): nothing was queued; else a CUDA
  * error code. */
 int tgkv_fwd_decode_step(const TGFwdStepParams* p, void* stream);
+
+/* fp32 GEMM on the tensor cores (tgkv_gemm.cu): out[M][N] (row stride ldo)
+ * = A[M][K] . W[N][K]^T, or += with accumulate, at fp32-product accuracy.
+ * Each operand is given as its tf32-rounded part and the exact remainder
+ * (tgkv_split_tf32); the kernel sums A_big.W_big + A_big.W_small +
+ * A_small.W_big.  K, lda and ldw multiples of 4 (16-byte rows for TMA). */
+typedef struct {
+    CUtensorMap a_big, a_small;     /* [M][K], box 32 x 128, 128-byte swizzle */
+    CUtensorMap w_big, w_small;     /* [N][K], box 32 x BN */
+    float* out;
+    uint64_t ldo;
+    uint32_t M, N, K;
+    int accumulate;
+    int32_t* err;                   /* device error word: set when a bounded wait runs out */
+} TGGemmParams;
+/* Fill p (host only; 0 on unsupported shapes or a failed tensor-map encode). */
+int tgkv_gemm_encode(TGGemmParams* p, const float* a_big, const float* a_small, uint64_t lda,
+                     const float* w_big, const float* w_small, uint64_t ldw, float* out,
+                     uint64_t ldo, uint32_t M, uint32_t N, uint32_t K, int accumulate,
+                     int32_t* err);
+/* Output tile width the launch uses for an M x N product (64 or 128). */
+uint32_t tgkv_gemm_bn(uint32_t M, uint32_t N);
+int tgkv_gemm_launch(const TGGemmParams* p, void* stream);
+/* big = x rounded to tf32 (nearest, ties away), small = x - big (exact), for
+ * rows x cols (row strides ldx, ldo in elements). */
+int tgkv_split_tf32(const float* x, uint64_t ldx, float* big, float* small, uint64_t ldo,
+                    uint32_t rows, uint32_t cols, void* stream);
+
+/* The bridge's device error word (tgai_cuda_bridge.c), which
+ * tg_cuda_kv_device_error reads: kernels outside the bridge record their
+ * bounded-wait expiries there too. */
+int32_t* tgkv_bridge_err_word(void);
 
 /* Page-locked host memory (NULL on failure). */
 void* tgkv_fwd_host_alloc(size_t bytes);

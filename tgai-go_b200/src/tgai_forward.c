@@ -17,8 +17,9 @@
  * The device side is one stream per sequence ("slot", keyed by the caller's
  * pointer as cuda/tgai_cuda.cu:1656-1672 keys them): our kernels
  * (tgkv_forward.cu), the KV path's RoPE+append and attention kernels, and
- * fp32 cuBLAS GEMMs for the projections, the router and the LM head (opened
- * with dlopen on first use, so the KV path alone never needs cuBLAS).  The
+ * for the prefill projections and the router our tensor-core GEMM
+ * (tgkv_gemm.cu) at fp32-product accuracy, where the reference bridge calls
+ * cublasSgemm (cuda/tgai_cuda.cu:473-479); no library GEMM is used.  The
  * only host synchronisation per forward is the final logits copy; the MoE
  * routing stays on the device (the reference bridge copies the top-k ids to
  * the host once per layer, cuda/tgai_cuda.cu:1532-1590).
@@ -38,7 +39,6 @@
 #include "tgai_kv_cache.h"
 #include "tgkv_forward.h"
 
-#include <cublas_v2.h>
 #include <dlfcn.h>
 #include <math.h>
 #include <pthread.h>
@@ -62,49 +62,6 @@ static void set_err(const char* fmt, ...) {
 const char* tg_fwd_last_error(void) { return t_err; }
 uint32_t tg_fwd_last_launches(void) { return t_launches; }
 
-/* ---- cuBLAS, opened on first use ----------------------------------------- */
-typedef cublasStatus_t (*blas_create_fn)(cublasHandle_t*);
-typedef cublasStatus_t (*blas_destroy_fn)(cublasHandle_t);
-typedef cublasStatus_t (*blas_stream_fn)(cublasHandle_t, cudaStream_t);
-typedef cublasStatus_t (*blas_sgemm_fn)(cublasHandle_t, cublasOperation_t, cublasOperation_t,
-                                        int, int, int, const float*, const float*, int,
-                                        const float*, int, const float*, float*, int);
-static struct {
-    int ok;
-    char why[200];
-    blas_create_fn create;
-    blas_destroy_fn destroy;
-    blas_stream_fn set_stream;
-    blas_sgemm_fn sgemm;
-} g_blas;
-static pthread_once_t g_blas_once = PTHREAD_ONCE_INIT;
-
-static void blas_open(void) {
-    static const char* names[] = {"libcublas.so.12", "libcublas.so"};
-    void* h = NULL;
-    for (size_t i = 0; i < sizeof(names) / sizeof(names[0]) && !h; i++)
-        h = dlopen(names[i], RTLD_NOW | RTLD_LOCAL);
-    if (!h) {
-        snprintf(g_blas.why, sizeof(g_blas.why), "cuBLAS not loadable: %s", dlerror());
-        return;
-    }
-    g_blas.create = (blas_create_fn)dlsym(h, "cublasCreate_v2");
-    g_blas.destroy = (blas_destroy_fn)dlsym(h, "cublasDestroy_v2");
-    g_blas.set_stream = (blas_stream_fn)dlsym(h, "cublasSetStream_v2");
-    g_blas.sgemm = (blas_sgemm_fn)dlsym(h, "cublasSgemm_v2");
-    if (!g_blas.create || !g_blas.destroy || !g_blas.set_stream || !g_blas.sgemm) {
-        snprintf(g_blas.why, sizeof(g_blas.why), "cuBLAS lacks the v2 GEMM entry points");
-        return;
-    }
-    g_blas.ok = 1;
-}
-
-static int blas_ready(void) {
-    pthread_once(&g_blas_once, blas_open);
-    if (!g_blas.ok) set_err("%s", g_blas.why);
-    return g_blas.ok;
-}
-
 /* ---- model and slots ------------------------------------------------------ */
 typedef struct {
     float* ln1;        /* [d] */
@@ -116,6 +73,10 @@ typedef struct {
     float* w3;         /* dense [d][dff];   MoE [ne][d][dff] */
     float* router;     /* [ne][d] */
     float* qb;         /* [ne] or NULL */
+    /* the prefill GEMMs' operands: each weight as its tf32-rounded part and
+     * the exact remainder (tgkv_split_tf32), same shapes */
+    float *wqkv_b, *wqkv_s, *wo_b, *wo_s, *router_b, *router_s;
+    float *w12_b, *w12_s, *w3_b, *w3_s;   /* dense FFN only */
 } Layer;
 
 typedef struct Slot {
@@ -126,9 +87,9 @@ typedef struct Slot {
     int last_pos;            /* positions [0, last_pos) written by this slot; -1 none */
     int kv_hi;
     void* stream;
-    cublasHandle_t blas;
     uint32_t cap;            /* token rows the workspaces hold */
     float *x, *ln, *qkv, *q, *attn, *ab, *h, *router, *top_w, *y, *logits;
+    float *abig, *asmall;    /* a prefill GEMM's input rows, split (tgkv_split_tf32) */
     int32_t *top_ids, *ids;
     uint32_t *counts, *lists;
     int32_t* h_ids;          /* page-locked */
@@ -145,6 +106,7 @@ struct TGFwdModel {
     uint32_t hd, nkv, q_dim, kv_dim, qkv_dim, rows;
     Layer* L;
     float *emb, *fnorm, *cs, *sn;
+    float *emb_b, *emb_s;          /* split embedding, only where the LM head needs the GEMM */
     TGFwdStepLayer* step_layers;   /* device [n_layers], when the one-launch step fits */
     int step_refused;              /* the device refused the step's grid: per-layer launches */
     uint64_t wbytes;
@@ -153,6 +115,11 @@ struct TGFwdModel {
     uint32_t max_slots, live;
     long long rejects;
 };
+
+/* The fused decode kernels stage R token rows of K floats in shared memory. */
+static int decode_fits(uint32_t R, uint32_t K) {
+    return R <= tgkv_fwd_decode_rows() && (uint64_t)R * K * 4 + 1024 <= 200 * 1024;
+}
 
 /* Device copy of n floats from host (blocking). */
 static float* upload(TGFwdModel* m, const float* src, uint64_t n) {
@@ -165,6 +132,25 @@ static float* upload(TGFwdModel* m, const float* src, uint64_t n) {
     }
     m->wbytes += n * sizeof(float);
     return d;
+}
+
+/* The prefill GEMM's form of a device weight [rows][cols]: its tf32-rounded
+ * part and the exact remainder, in two new device buffers (queued on the
+ * default stream; creation synchronises before it returns). */
+static int split_weight(TGFwdModel* m, const float* w, uint64_t rows, uint64_t cols,
+                        float** big, float** small) {
+    const uint64_t n = rows * cols;
+    *big = (float*)tg_cuda_kv_malloc(n * sizeof(float));
+    *small = (float*)tg_cuda_kv_malloc(n * sizeof(float));
+    if (!*big || !*small) {
+        set_err("device allocation of %llu bytes failed", (unsigned long long)(2 * n * 4));
+        return 0;
+    }
+    const int e = tgkv_split_tf32(w, cols, *big, *small, cols, (uint32_t)rows, (uint32_t)cols,
+                                  NULL);
+    if (e) { set_err("weight split failed (CUDA error %d)", e); return 0; }
+    m->wbytes += 2 * n * sizeof(float);
+    return 1;
 }
 
 /* A tensor of exactly rows x cols elements (cols 1 for 1-D), or NULL. */
@@ -206,6 +192,9 @@ static void free_layer(Layer* l) {
     tg_cuda_kv_free(l->w3);
     tg_cuda_kv_free(l->router);
     tg_cuda_kv_free(l->qb);
+    float* sp[] = {l->wqkv_b, l->wqkv_s, l->wo_b, l->wo_s, l->router_b, l->router_s,
+                   l->w12_b, l->w12_s, l->w3_b, l->w3_s};
+    for (size_t i = 0; i < sizeof(sp) / sizeof(sp[0]); i++) tg_cuda_kv_free(sp[i]);
 }
 
 static void slot_release_mem(TGFwdModel* m, Slot* s);
@@ -220,6 +209,8 @@ void tg_fwd_destroy(TGFwdModel* m) {
         free(m->L);
     }
     tg_cuda_kv_free(m->emb);
+    tg_cuda_kv_free(m->emb_b);
+    tg_cuda_kv_free(m->emb_s);
     tg_cuda_kv_free(m->fnorm);
     tg_cuda_kv_free(m->cs);
     tg_cuda_kv_free(m->sn);
@@ -273,23 +264,29 @@ static int load_layer(TGFwdModel* m, uint32_t l, TGFwdWeightFn get, void* ctx) {
         }
         if (!(L->wqkv = upload_cat(m, w, nw, 3))) return 0;
         if (any_bias && !(L->bqkv = upload_cat(m, b, nb, 3))) return 0;
+        if (!split_weight(m, L->wqkv, m->qkv_dim, d, &L->wqkv_b, &L->wqkv_s)) return 0;
     }
     if (!(p = tensor(get, ctx, NAME("blocks.%u.attn.out_proj.weight", l), d, m->q_dim, 1)) ||
-        !(L->wo = upload(m, p, (uint64_t)d * m->q_dim)))
+        !(L->wo = upload(m, p, (uint64_t)d * m->q_dim)) ||
+        !split_weight(m, L->wo, d, m->q_dim, &L->wo_b, &L->wo_s))
         return 0;
     if (ne == 0) {
         const float* w[2];
         uint64_t nw[2] = {(uint64_t)dff * d, (uint64_t)dff * d};
         if (!(w[0] = tensor(get, ctx, NAME("blocks.%u.ffn.w1.weight", l), dff, d, 1))) return 0;
         if (!(w[1] = tensor(get, ctx, NAME("blocks.%u.ffn.w2.weight", l), dff, d, 1))) return 0;
-        if (!(L->w12 = upload_cat(m, w, nw, 2))) return 0;
+        if (!(L->w12 = upload_cat(m, w, nw, 2)) ||
+            !split_weight(m, L->w12, 2 * (uint64_t)dff, d, &L->w12_b, &L->w12_s))
+            return 0;
         if (!(p = tensor(get, ctx, NAME("blocks.%u.ffn.w3.weight", l), d, dff, 1)) ||
-            !(L->w3 = upload(m, p, (uint64_t)d * dff)))
+            !(L->w3 = upload(m, p, (uint64_t)d * dff)) ||
+            !split_weight(m, L->w3, d, dff, &L->w3_b, &L->w3_s))
             return 0;
         return 1;
     }
     if (!(p = tensor(get, ctx, NAME("blocks.%u.moe.router.weight", l), ne, d, 1)) ||
-        !(L->router = upload(m, p, (uint64_t)ne * d)))
+        !(L->router = upload(m, p, (uint64_t)ne * d)) ||
+        !split_weight(m, L->router, ne, d, &L->router_b, &L->router_s))
         return 0;
     p = optional(get, ctx, NAME("blocks.%u.moe._qb_bias", l), ne, 1, &bad);
     if (bad || (p && !(L->qb = upload(m, p, ne)))) return 0;
@@ -348,7 +345,6 @@ TGFwdModel* tg_fwd_create(const TGFwdConfig* cfg, TGFwdWeightFn get, void* ctx) 
         set_err("no CUDA device: %s", tg_gpu_backend_reason());
         return NULL;
     }
-    if (!blas_ready()) return NULL;
 
     TGFwdModel* m = (TGFwdModel*)calloc(1, sizeof(TGFwdModel));
     if (!m) { set_err("host allocation failed"); return NULL; }
@@ -383,6 +379,10 @@ TGFwdModel* tg_fwd_create(const TGFwdConfig* cfg, TGFwdWeightFn get, void* ctx) 
             goto fail;
         }
         if (!(m->emb = upload(m, e, (uint64_t)m->rows * c.d_model))) goto fail;
+        /* the LM head is a GEMV of the staged row where d fits; else the GEMM */
+        if (!decode_fits(1, c.d_model) &&
+            !split_weight(m, m->emb, m->rows, c.d_model, &m->emb_b, &m->emb_s))
+            goto fail;
         const float* f = tensor(get, ctx, "final_norm.weight", c.d_model, 1, 1);
         if (!f || !(m->fnorm = upload(m, f, c.d_model))) goto fail;
     }
@@ -417,6 +417,9 @@ TGFwdModel* tg_fwd_create(const TGFwdConfig* cfg, TGFwdWeightFn get, void* ctx) 
         free(t);
         if (!ok) { set_err("step layer table: %s", tg_cuda_kv_last_error()); goto fail; }
     }
+    /* the weight splits ran on the default stream; the slots' streams do not
+     * wait for it */
+    if (!tg_cuda_kv_sync(NULL)) { set_err("weight split: %s", tg_cuda_kv_last_error()); goto fail; }
     return m;
 fail:
     tg_fwd_destroy(m);
@@ -428,7 +431,7 @@ uint64_t tg_fwd_weight_bytes(const TGFwdModel* m) { return m ? m->wbytes : 0; }
 /* ---- slots ---------------------------------------------------------------- */
 static void slot_free_ws(Slot* s) {
     float** f[] = {&s->x, &s->ln, &s->qkv, &s->q, &s->attn, &s->ab, &s->h, &s->router,
-                   &s->top_w, &s->y};
+                   &s->top_w, &s->y, &s->abig, &s->asmall};
     for (size_t i = 0; i < sizeof(f) / sizeof(f[0]); i++) { tg_cuda_kv_free(*f[i]); *f[i] = NULL; }
     tg_cuda_kv_free(s->top_ids);
     tg_cuda_kv_free(s->ids);
@@ -461,8 +464,6 @@ static void slot_release_mem(TGFwdModel* m, Slot* s) {
     s->logits = NULL;
     tgkv_fwd_host_free(s->h_logits);
     s->h_logits = NULL;
-    if (s->blas) g_blas.destroy(s->blas);
-    s->blas = NULL;
     if (s->stream) tg_cuda_kv_stream_destroy(s->stream);
     s->stream = NULL;
     s->used = 0;
@@ -486,7 +487,12 @@ static int slot_reserve(TGFwdModel* m, Slot* s, uint32_t need) {
     s->h = (float*)tg_cuda_kv_malloc(pairs * dff * 4);
     s->ids = (int32_t*)tg_cuda_kv_malloc((uint64_t)cap * 4);
     s->h_ids = (int32_t*)tgkv_fwd_host_alloc((uint64_t)cap * 4);
-    int ok = s->x && s->ln && s->qkv && s->q && s->attn && s->h && s->ids && s->h_ids;
+    uint64_t kmax = d > m->q_dim ? d : m->q_dim;
+    if (dff > kmax) kmax = dff;
+    s->abig = (float*)tg_cuda_kv_malloc(cap * kmax * 4);
+    s->asmall = (float*)tg_cuda_kv_malloc(cap * kmax * 4);
+    int ok = s->x && s->ln && s->qkv && s->q && s->attn && s->h && s->ids && s->h_ids &&
+             s->abig && s->asmall;
     if (ne == 0) {
         s->ab = (float*)tg_cuda_kv_malloc(cap * 2 * dff * 4);
         ok = ok && s->ab;
@@ -511,15 +517,6 @@ static int slot_reserve(TGFwdModel* m, Slot* s, uint32_t need) {
 static int slot_init(TGFwdModel* m, Slot* s) {
     s->stream = tg_cuda_kv_stream_create();
     if (!s->stream) { set_err("stream: %s", tg_cuda_kv_last_error()); return 0; }
-    if (g_blas.create(&s->blas) != CUBLAS_STATUS_SUCCESS) {
-        s->blas = NULL;
-        set_err("cublasCreate failed");
-        return 0;
-    }
-    if (g_blas.set_stream(s->blas, (cudaStream_t)s->stream) != CUBLAS_STATUS_SUCCESS) {
-        set_err("cublasSetStream failed");
-        return 0;
-    }
     s->kv = (TGKvCache**)calloc(m->c.n_layers, sizeof(TGKvCache*));
     if (!s->kv) { set_err("host allocation failed"); return 0; }
     for (uint32_t l = 0; l < m->c.n_layers; l++) {
@@ -647,24 +644,21 @@ HIDDEN uint32_t tgkv_fwd_max_slots(const TGFwdModel* m) { return m ? m->max_slot
         if (_e) { set_err("%s failed (CUDA error %d)", #expr, _e); return 0; }  \
     } while (0)
 
-/* out[M][N] (row stride ldo) = x[M][K] (row stride ldx) . W[N][K]^T, or += */
+/* out[M][N] (row stride ldo) = x[M][K] (row stride ldx) . W[N][K]^T, or +=,
+ * on the tensor cores at fp32-product accuracy (tgkv_gemm.cu): x is split
+ * into its tf32 part and remainder in the slot's workspace, W comes split
+ * (wb, ws) from model creation. */
 static int gemm(Slot* s, uint32_t M, uint32_t N, uint32_t K, const float* x, uint32_t ldx,
-                const float* w, float* out, uint32_t ldo, int accumulate) {
-    const float one = 1.f, zero = 0.f;
-    t_launches++;
-    const cublasStatus_t st = g_blas.sgemm(s->blas, CUBLAS_OP_T, CUBLAS_OP_N, (int)N, (int)M,
-                                           (int)K, &one, w, (int)K, x, (int)ldx,
-                                           accumulate ? &one : &zero, out, (int)ldo);
-    if (st != CUBLAS_STATUS_SUCCESS) {
-        set_err("cublasSgemm(%u x %u x %u) failed with status %d", M, N, K, (int)st);
+                const float* wb, const float* ws, float* out, uint32_t ldo, int accumulate) {
+    CHECK_LAUNCH(tgkv_split_tf32(x, ldx, s->abig, s->asmall, K, M, K, s->stream));
+    TGGemmParams p;
+    if (!tgkv_gemm_encode(&p, s->abig, s->asmall, K, wb, ws, K, out, ldo, M, N, K, accumulate,
+                          tgkv_bridge_err_word())) {
+        set_err("GEMM %u x %u x %u: unsupported shape or tensor map", M, N, K);
         return 0;
     }
+    CHECK_LAUNCH(tgkv_gemm_launch(&p, s->stream));
     return 1;
-}
-
-/* The fused decode kernels stage R token rows of K floats in shared memory. */
-static int decode_fits(uint32_t R, uint32_t K) {
-    return R <= tgkv_fwd_decode_rows() && (uint64_t)R * K * 4 + 1024 <= 200 * 1024;
 }
 
 /* Attention half of a layer: q/k/v, RoPE + KV append, attention.  Leaves the
@@ -699,7 +693,7 @@ static int attn_half(TGFwdModel* m, Slot* s, const Layer* L, TGKvCache* kv, uint
                                            (uint64_t)d * m->q_dim, st));
     } else {
         CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, s->x, L->ln1, seq, d, d, d, 1e-6f, st));
-        if (!gemm(s, seq, m->qkv_dim, d, s->ln, d, L->wqkv, s->qkv, m->qkv_dim, 0)) return 0;
+        if (!gemm(s, seq, m->qkv_dim, d, s->ln, d, L->wqkv_b, L->wqkv_s, s->qkv, m->qkv_dim, 0)) return 0;
         if (L->bqkv) CHECK_LAUNCH(tgkv_fwd_bias(s->qkv, L->bqkv, seq, m->qkv_dim, st));
         t_launches++;
         if (!tg_cuda_kv_rope_append(TG_KV_F32, s->qkv, m->cs, m->sn, tg_kv_device_handle(kv),
@@ -749,14 +743,14 @@ static int run_layer(TGFwdModel* m, Slot* s, uint32_t l, uint32_t seq, uint32_t 
                                              ne, na, next_qkv, next_qkv_n, st));
         return 1;
     }
-    if (!gemm(s, seq, d, m->q_dim, s->attn, m->q_dim, L->wo, s->x, d, 1)) return 0;
+    if (!gemm(s, seq, d, m->q_dim, s->attn, m->q_dim, L->wo_b, L->wo_s, s->x, d, 1)) return 0;
     CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, s->x, L->ln2, seq, d, d, d, 1e-6f, st));
     if (ne == 0) {
-        if (!gemm(s, seq, 2 * dff, d, s->ln, d, L->w12, s->ab, 2 * dff, 0)) return 0;
+        if (!gemm(s, seq, 2 * dff, d, s->ln, d, L->w12_b, L->w12_s, s->ab, 2 * dff, 0)) return 0;
         CHECK_LAUNCH(tgkv_fwd_silu_mul(s->h, s->ab, seq, dff, 1, st));
-        return gemm(s, seq, d, dff, s->h, dff, L->w3, s->x, d, 1);
+        return gemm(s, seq, d, dff, s->h, dff, L->w3_b, L->w3_s, s->x, d, 1);
     }
-    if (!gemm(s, seq, ne, d, s->ln, d, L->router, s->router, ne, 0)) return 0;
+    if (!gemm(s, seq, ne, d, s->ln, d, L->router_b, L->router_s, s->router, ne, 0)) return 0;
     if (!tg_cuda_kv_memset(s->counts, 0, (size_t)ne * 4, st)) {
         set_err("memset: %s", tg_cuda_kv_last_error());
         return 0;
@@ -895,7 +889,7 @@ static int run_forward(TGFwdModel* m, Slot* s, const int32_t* ids, uint32_t seq,
                                        m->rows, d, 0, NULL, 0, st));
     } else {
         CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, xl, m->fnorm, 1, d, d, d, 1e-6f, st));
-        if (!gemm(s, 1, m->rows, d, s->ln, d, m->emb, s->logits, m->rows, 0)) return 0;
+        if (!gemm(s, 1, m->rows, d, s->ln, d, m->emb_b, m->emb_s, s->logits, m->rows, 0)) return 0;
     }
     if (!tg_cuda_kv_d2h(s->h_logits, s->logits, (size_t)m->rows * 4, st) || !tg_cuda_kv_sync(st)) {
         set_err("forward: %s", tg_cuda_kv_last_error());
@@ -926,4 +920,47 @@ const float* tg_fwd_forward(TGFwdModel* m, const void* key, const int32_t* ids,
         return NULL;
     }
     return s->h_logits;
+}
+
+int tg_fwd_gemm_f32(uint32_t M, uint32_t N, uint32_t K, const float* x, uint32_t ldx,
+                    const float* w, uint32_t ldw, float* out, uint32_t ldo, int accumulate,
+                    void* stream) {
+    t_launches = 0;
+    if (!x || !w || !out || !M || !N || !K) { set_err("null argument or empty shape"); return 0; }
+    if (K % 4 || ldx % 4 || ldw % 4 || ldx < K || ldw < K || ldo < N) {
+        set_err("K, ldx and ldw must be multiples of 4, ldx, ldw >= K and ldo >= N");
+        return 0;
+    }
+    if (!tg_cuda_kv_init()) { set_err("no CUDA device: %s", tg_cuda_kv_last_error()); return 0; }
+    float* buf[4] = {NULL, NULL, NULL, NULL};
+    const uint64_t na = (uint64_t)M * K, nw = (uint64_t)N * K;
+    buf[0] = (float*)tg_cuda_kv_malloc(na * 4);
+    buf[1] = (float*)tg_cuda_kv_malloc(na * 4);
+    buf[2] = (float*)tg_cuda_kv_malloc(nw * 4);
+    buf[3] = (float*)tg_cuda_kv_malloc(nw * 4);
+    int ok = buf[0] && buf[1] && buf[2] && buf[3];
+    if (!ok) set_err("split operands: device allocation failed");
+    int e = 0;
+    if (ok && ((e = tgkv_split_tf32(x, ldx, buf[0], buf[1], K, M, K, stream)) ||
+               (e = tgkv_split_tf32(w, ldw, buf[2], buf[3], K, N, K, stream)))) {
+        set_err("split failed (CUDA error %d)", e);
+        ok = 0;
+    }
+    TGGemmParams p;
+    if (ok && !tgkv_gemm_encode(&p, buf[0], buf[1], K, buf[2], buf[3], K, out, ldo, M, N, K,
+                                accumulate, tgkv_bridge_err_word())) {
+        set_err("GEMM %u x %u x %u: tensor map encode failed", M, N, K);
+        ok = 0;
+    }
+    if (ok && (e = tgkv_gemm_launch(&p, stream))) {
+        set_err("GEMM launch failed (CUDA error %d)", e);
+        ok = 0;
+    }
+    t_launches = ok ? 3 : 0;
+    if (!tg_cuda_kv_sync(stream) && ok) {
+        set_err("GEMM: %s", tg_cuda_kv_last_error());
+        ok = 0;
+    }
+    for (int i = 0; i < 4; i++) tg_cuda_kv_free(buf[i]);
+    return ok;
 }
