@@ -204,6 +204,7 @@ PROTOS = {
     "tg_fwd_weight_bytes": (u64, [vp]),
     "tg_fwd_last_launches": (u32, []),
     "tg_fwd_last_error": (cp, []),
+    "tg_fwd_gemm_f32": (i32, [u32, u32, u32, vp, u32, vp, u32, vp, u32, i32, vp]),
 }
 
 _lib = None
