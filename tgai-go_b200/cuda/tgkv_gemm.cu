@@ -9,9 +9,14 @@
 // The product is A_big.W_big + A_big.W_small + A_small.W_big; the dropped
 // A_small.W_small term is below 2^-22 of |a||w|, and the tf32 rounding the
 // tensor core applies to `small` costs about as much, so every product is
-// good to about 2^-21 -- the accuracy class of an fp32 SGEMM over these K.
-// The three products are one K-concatenated pipeline: k-block kb of segment
-// 0, 1, 2 loads (A_big, W_big), (A_big, W_small), (A_small, W_big).
+// good to about 2^-21.  The three products are one K-concatenated pipeline:
+// k-block kb of segment 0, 1, 2 loads (A_small, W_big), (A_big, W_small),
+// (A_big, W_big).  The tensor core's fp32 accumulation truncates at every
+// step, relative to the accumulator's magnitude, so the two small terms go
+// first (while the accumulator is ~2^-11 of its final size) and the k-blocks
+// are dealt round-robin over all of TMEM (512 / BN accumulators), which the
+// epilogue adds in IEEE fp32: every accumulator sees a fraction of the steps
+// at a fraction of the magnitude.
 //
 // One CTA (128 threads) per 128 x BN output tile.  Lane 0 of warp 0 moves
 // 128x32 (A) and BNx32 (W) fp32 tiles with 128-byte-swizzled tiled TMA into
@@ -47,7 +52,8 @@ struct Cfg {
     static constexpr int NStage = (196608 / Stage) > 8 ? 8 : (196608 / Stage);
     static constexpr int OffBar = NStage * Stage;
     static constexpr int Smem = OffBar + (2 * NStage + 2) * 8 + 16 + 1024;   // + alignment slack
-    static constexpr uint32_t TmemCols = BN < 32 ? 32 : BN;
+    static constexpr int NAcc = 512 / BN;              // accumulators: all 512 TMEM columns
+    static constexpr uint32_t TmemCols = 512;
 };
 
 // Instruction descriptor, kind::tf32: D f32 (bits 4-5 = 1), A and B tf32
@@ -130,7 +136,7 @@ __global__ void __launch_bounds__(128, 1) gemm_tf32x3_kernel(const __grid_consta
             const int kx = (kb - seg * nkb) * kBK;
             unsigned char* st = smem + s * C::Stage;
             mbar_arrive_expect_tx(&full[s], (uint32_t)C::Stage);
-            tma_load_2d(st, seg == 2 ? &p.a_small : &p.a_big, kx, (int)m0, &full[s]);
+            tma_load_2d(st, seg == 0 ? &p.a_small : &p.a_big, kx, (int)m0, &full[s]);
             tma_load_2d(st + kABytes, seg == 1 ? &p.w_small : &p.w_big, kx, (int)n0, &full[s]);
             ++issued;
         }
@@ -151,10 +157,12 @@ __global__ void __launch_bounds__(128, 1) gemm_tf32x3_kernel(const __grid_consta
             tc_fence_after();
             const uint32_t a = smem_addr(smem + s * C::Stage);
             const uint32_t b = a + kABytes;
+            const uint32_t acc = tmem + (uint32_t)((kb % C::NAcc) * BN);
 #pragma unroll
             for (int k = 0; k < kBK / 8; ++k)          // K = 8 tf32 = 32 bytes per MMA
-                umma_tf32(tmem, umma_desc_sw128(a + 32 * k, 16, 1024),
-                          umma_desc_sw128(b + 32 * k, 16, 1024), idesc, (kb | k) != 0);
+                umma_tf32(acc, umma_desc_sw128(a + 32 * k, 16, 1024),
+                          umma_desc_sw128(b + 32 * k, 16, 1024), idesc,
+                          (kb >= C::NAcc) || (k > 0));
             umma_commit(&empty[s]);                    // the stage is free once these are done
         }
         umma_commit(done);                             // every MMA issued so far is done
@@ -171,13 +179,24 @@ __global__ void __launch_bounds__(128, 1) gemm_tf32x3_kernel(const __grid_consta
     const uint32_t row = m0 + 32 * warp + lane;
     float* orow = p.out + (uint64_t)row * p.ldo;
     const bool vec = (p.ldo % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0);
+    const int n_acc = total < C::NAcc ? total : C::NAcc;   // accumulators written
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
         const uint32_t col0 = n0 + 32 * c;
         if (col0 >= p.N) break;                        // warp-uniform
         uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + 32 * c, r);
+        const uint32_t t = tmem + ((uint32_t)(32 * warp) << 16) + 32 * c;
+        tmem_ld32(t, r);
         tmem_wait_ld(r);
+#pragma unroll 1
+        for (int a = 1; a < n_acc; ++a) {
+            uint32_t q[32];
+            tmem_ld32(t + (uint32_t)(a * BN), q);
+            tmem_wait_ld(q);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q[j]));
+        }
         if (!store || row >= p.M) continue;
         if (vec && col0 + 32 <= p.N) {
 #pragma unroll
