@@ -942,6 +942,56 @@ def run_fwd(args):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         dt = float(tt[0])
         dist.destroy_process_group()
+    # several sequences at once, one thread each, as a server runs them: the
+    # one-token forwards in flight together run as batches over the weights
+    multi = None
+    if not args.no_extra:
+        import threading
+        n_thr, mp = 8, 64
+        keys = [C.c_void_p(1000 + i) for i in range(n_thr)]
+        mids = np.random.default_rng([args.seed, rank, 7]).integers(
+            0, cfg["vocab"], (n_thr, mp + args.warmup + args.steps)).astype(np.int32)
+        go = threading.Barrier(n_thr + 1)
+        fail = []
+
+        def seq(i):
+            try:
+                def one(a, pos):
+                    if not lib.tg_fwd_forward(m, keys[i], a.ctypes.data_as(C.POINTER(C.c_int32)),
+                                              len(a), pos):
+                        raise RuntimeError(lib.tg_fwd_last_error().decode())
+                one(mids[i, :mp], 0)
+                for t in range(args.warmup):
+                    one(mids[i, mp + t:mp + t + 1], mp + t)
+                go.wait()
+                for t in range(args.warmup, args.warmup + args.steps):
+                    one(mids[i, mp + t:mp + t + 1], mp + t)
+                go.wait()
+            except Exception as e:
+                fail.append(repr(e))
+                go.abort()
+
+        tok0, bat0 = C.c_uint64(), C.c_uint64()
+        lib.tg_fwd_batch_stats(m, C.byref(tok0), C.byref(bat0))
+        th = [threading.Thread(target=seq, args=(i,)) for i in range(n_thr)]
+        for t in th:
+            t.start()
+        go.wait()
+        t0m = time.perf_counter()
+        go.wait()
+        dtm = time.perf_counter() - t0m
+        for t in th:
+            t.join()
+        if fail:
+            raise SystemExit("multi-sequence decode: " + fail[0])
+        tok1, bat1 = C.c_uint64(), C.c_uint64()
+        lib.tg_fwd_batch_stats(m, C.byref(tok1), C.byref(bat1))
+        nb = bat1.value - bat0.value
+        multi = {"sequences": n_thr, "tokens_per_s": n_thr * args.steps / dtm,
+                 "ms_per_round": 1000.0 * dtm / args.steps,
+                 "mean_batch": (tok1.value - tok0.value) / nb if nb else 1.0,
+                 "how": f"{n_thr} threads, each its own sequence (a {mp}-token prefill, then "
+                        f"one-token forwards): host clock over {args.steps} tokens per thread"}
     lib.tg_fwd_destroy(m)
     if rank != 0:
         return
@@ -969,6 +1019,7 @@ def run_fwd(args):
                          "peak_source": src, "traffic": None,
                          "bytes_per_token": bpt},
             "gpu_launches": launches * args.steps,
+            "multi_sequence": multi,
             "prefill": {"tokens": prefill, "ms": 1000.0 * pf_s, "tokens_per_s": prefill / pf_s,
                         "launches": pf_launches,
                         "how": "host clock around one synchronous tg_fwd_forward of the "

@@ -125,6 +125,14 @@ uint64_t tg_fwd_weight_bytes(const TGFwdModel* m);
 /* Kernel launches and GEMM calls issued by the last forward of this thread. */
 uint32_t tg_fwd_last_launches(void);
 
+/* One-token forwards of different sequences that are in flight at the same
+ * time (from several threads) run as one pass over the weights, up to 4 at a
+ * time: the reference bridge's per-slot streams (cuda/tgai_cuda_bridge.c:
+ * 147-162) each read every weight.  Tokens decoded in such batches of two or
+ * more so far, and the number of those batches.  TGKV_FWD_BATCH=0 turns the
+ * batching off. */
+void tg_fwd_batch_stats(const TGFwdModel* m, uint64_t* tokens, uint64_t* batches);
+
 /* The fp32 GEMM the forward's prefill runs, as a standalone call on device
  * buffers: out[M][N] (row stride ldo) = x[M][K] . w[N][K]^T (row strides ldx,
  * ldw), or += with accumulate, on the sm_100a tensor cores at fp32-product

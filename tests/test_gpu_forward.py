@@ -5,8 +5,9 @@ tests/golden/forward.npz holds tg_forward's logits (CPU engine,
 src/tgai_engine.c built in oracle/_ref) for the seeded MoE and dense models of
 tests/fwd_model.py over their scripts: prefill, decode, a second sequence on
 its own KV, LCP truncate + re-append.  The CUDA forward computes in fp32
-(cuBLAS SGEMM, fp32 KV cache) in a different summation order, so the bar is
-a relative error (max |diff| / max |logit|) of 1e-4.
+(tensor-core GEMMs at fp32-product accuracy, fp32 KV cache) in a different
+summation order, so the bar is a relative error (max |diff| / max |logit|)
+of 1e-4.
 """
 import ctypes as C
 import os
@@ -277,3 +278,55 @@ def test_engine_seam(cuda, golden, tmp_path, monkeypatch):
         for c in caches.values():
             eng.tg_kvcache_free(c)
         eng.tg_free(m)
+
+
+@pytest.mark.parametrize("name", sorted(FM.CONFIGS))
+def test_concurrent_sequences_batch_across_slots(cuda, name):
+    """Eight sequences decoded at once from eight threads, as a server does:
+    one-token forwards that are in flight together run as batches over the
+    weights (tg_fwd_batch_stats counts them), and every sequence's logits, at
+    every step, match the float64 oracle at the forward's tolerance."""
+    import threading
+    cfg = dict(FM.CONFIGS[name])
+    w = FM.weights(cfg, 91)
+    f = tgkv.Forward(cuda, fwd_config(cfg), w)
+    n_seq, prefill, steps = 8, 12, 20
+    rng = np.random.default_rng(13)
+    ids = rng.integers(0, cfg["vocab"], (n_seq, prefill + steps)).astype(np.int32)
+    for i in range(n_seq):
+        f.key(f"t{i}")                      # keys registered before the threads start
+    out = [[None] * (steps + 1) for _ in range(n_seq)]
+    errors = []
+    start = threading.Barrier(n_seq)
+
+    def worker(i):
+        try:
+            out[i][0] = f.forward(f"t{i}", ids[i, :prefill], 0)
+            start.wait()
+            for t in range(steps):
+                out[i][t + 1] = f.forward(f"t{i}", ids[i, prefill + t:prefill + t + 1],
+                                          prefill + t)
+        except Exception as e:              # reported below, on the test's thread
+            errors.append(f"{i}: {e!r}")
+
+    tokens, batches = C.c_uint64(), C.c_uint64()
+    try:
+        th = [threading.Thread(target=worker, args=(i,)) for i in range(n_seq)]
+        for t in th:
+            t.start()
+        for t in th:
+            t.join()
+        assert not errors, errors
+        cuda.tg_fwd_batch_stats(f.m, C.byref(tokens), C.byref(batches))
+    finally:
+        f.close()
+    assert batches.value > 0 and tokens.value >= 2 * batches.value, (tokens.value, batches.value)
+    for i in range(n_seq):
+        o = fwd_oracle.Forward(cfg, w)
+        e = rel(out[i][0], o.forward("s", ids[i, :prefill], 0))
+        assert e < FWD_TOL, (i, "prefill", e)
+        for t in range(steps):
+            ref = o.forward("s", ids[i, prefill + t:prefill + t + 1], prefill + t)
+            e = rel(out[i][t + 1], ref)
+            assert e < FWD_TOL, (i, t, e)
+    assert cuda.tg_cuda_kv_device_error() == 0

@@ -150,6 +150,27 @@ __device__ __forceinline__ void dots(const float* const (&w)[NW], const float* c
     for (int n = 0; n < NW; ++n) acc[n] = warp_sum(acc[n]);
 }
 
+// Bulk prefetch of `bytes` (multiple of 16, 16-byte aligned) into L2: one
+// instruction, no registers held, nothing waits for it.
+__device__ __forceinline__ void prefetch_l2(const void* ptr, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(bytes) : "memory");
+}
+
+// The rows this warp will read in a coming phase, into L2: rows
+// first + k * step (< limit) of `base` (row stride `stride` floats, `bytes`
+// per row), one per lane and pass.  `skip` leading rows are left out (a
+// phase's first row, which its own loads start at once).
+__device__ __forceinline__ void prefetch_rows(const float* base, uint64_t stride, uint32_t bytes,
+                                              uint32_t first, uint32_t step, uint32_t limit,
+                                              uint32_t skip = 0) {
+    const uint32_t lane = threadIdx.x & 31;
+    for (uint32_t k = skip + lane;; k += 32) {
+        const uint64_t r = (uint64_t)first + (uint64_t)k * step;
+        if (r >= limit) break;
+        prefetch_l2(base + r * stride, bytes);
+    }
+}
+
 }  // namespace tgkvs
 
 using namespace tgkvs;
@@ -343,13 +364,30 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
     const uint32_t ch = ((L + n_tasks - 1) / n_tasks + kSub - 1) / kSub * kSub;
     n_tasks = (L + ch - 1) / ch;
     const uint32_t half = hd >> 1;
+    const uint32_t npair = (q_dim + 2 * kv_dim) / 2;
+    // Each phase's weight rows go to L2 one phase ahead (the routed experts'
+    // as soon as the router has chosen), so HBM keeps streaming while the
+    // grid waits at a barrier.  Every warp prefetches exactly the rows it
+    // will read itself.
+    if (p.prefetch) prefetch_rows(p.layers[0].wqkv, 2 * (uint64_t)d, 8 * d, gw, tw, npair);
 
     for (uint32_t l = 0; l < p.n_layers; ++l) {
         const TGFwdStepLayer W = p.layers[l];
         float* kvc = p.kvc[l];
+        if (p.prefetch) {
+            // P3's out-projection rows and P2's K/V ranges
+            prefetch_rows(W.wo, q_dim, 4 * q_dim, gw, tw, d);
+            for (uint32_t t = gw; t < nkv * n_tasks; t += tw) {
+                const uint32_t kvh = t / n_tasks, pb = (t % n_tasks) * ch;
+                const uint32_t pe = pb + ch < L ? pb + ch : L;
+                for (uint32_t j = pb + lane; j < pe; j += 32) {
+                    prefetch_l2(kvc + (uint64_t)j * kv_dim + kvh * hd, 4 * hd);
+                    prefetch_l2(kvc + ((uint64_t)p.max_seq + j) * kv_dim + kvh * hd, 4 * hd);
+                }
+            }
+        }
         // ---- P1: norm, Q/K/V row pairs, bias, RoPE at pos, K/V append
         stage(sx, p.x, W.ln1, d, red);
-        const uint32_t npair = (q_dim + 2 * kv_dim) / 2;
         for (uint32_t mp = gw; mp < npair; mp += tw) {
             const uint32_t n0 = 2 * mp;
             float a[2];
@@ -385,6 +423,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
         }
         if (!grid_sync(bar, target, err, &s_ok)) return;
         // ---- P3: every CTA merges all heads into sx, then out projection + residual
+        if (p.prefetch && !ne) {          // the dense FFN's W1 and W2 rows of P4
+            prefetch_rows(W.w12, d, 4 * d, gw, tw, dff);
+            prefetch_rows(W.w12 + (uint64_t)dff * d, d, 4 * d, gw, tw, dff);
+        }
         for (uint32_t h = warp; h < nkv * G; h += kWarps) attn_merge_head<G>(p, h, n_tasks, sx + h * hd);
         __syncthreads();
         for (uint32_t n = gw; n < d; n += tw) {
@@ -404,6 +446,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
             __syncthreads();
             if (warp == 0) top_k_warp(slog, ne, na, s_ids, s_w);
             __syncthreads();
+            if (p.prefetch) {
+                // this warp's later W1/W2 rows of the routed experts, then
+                // their W3 rows of P5
+                for (uint32_t k = 0; k < na; ++k) {
+                    const int e = s_ids[k];
+                    if (e < 0 || (uint32_t)e >= ne) continue;
+                    const float* w1 = W.w12 + (uint64_t)e * 2 * dff * d;
+                    // task t = k * dff + j: the first of this warp's tasks is skipped
+                    const uint32_t t0 = gw, lo = k * dff, hi = lo + dff;
+                    uint32_t first = t0 >= lo ? t0 : t0 + ((lo - t0 + tw - 1) / tw) * tw;
+                    if (first == t0) first += tw;
+                    if (first < hi) {
+                        prefetch_rows(w1, d, 4 * d, first - lo, tw, dff);
+                        prefetch_rows(w1 + (uint64_t)dff * d, d, 4 * d, first - lo, tw, dff);
+                    }
+                    prefetch_rows(W.w3 + (uint64_t)e * d * dff, dff, 4 * dff, gw, tw, d);
+                }
+            }
             for (uint32_t t = gw; t < na * dff; t += tw) {
                 const uint32_t k = t / dff, j = t % dff;
                 const int e = s_ids[k];
@@ -417,6 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
                 if (lane == 0) p.h[(uint64_t)k * dff + j] = hv;
             }
         } else {
+            if (p.prefetch) prefetch_rows(W.w3, dff, 4 * dff, gw, tw, d);
             for (uint32_t j = gw; j < dff; j += tw) {
                 float a[2];
                 dots<2, 12>({W.w12 + (uint64_t)j * d, W.w12 + (uint64_t)(dff + j) * d}, {sx, sx}, d, a);
@@ -425,6 +486,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
         }
         if (!grid_sync(bar, target, err, &s_ok)) return;
         // ---- P5: W3 rows, k-ordered weighted sum (or dense W3) + residual
+        if (p.prefetch && l + 1 < p.n_layers)
+            prefetch_rows(p.layers[l + 1].wqkv, 2 * (uint64_t)d, 8 * d, gw, tw, npair);
         stage(sh, p.h, nullptr, (ne ? na : 1) * dff, red);
         for (uint32_t i = gw; i < d; i += tw) {
             float ot = 0.f;

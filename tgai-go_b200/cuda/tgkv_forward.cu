@@ -422,7 +422,8 @@ __global__ void __launch_bounds__(384, 1) dec_qkv_rope_kernel(const float* __res
                                                            uint32_t q_dim, uint32_t kv_dim,
                                                            uint32_t hd, uint32_t pos0,
                                                            uint32_t max_seq, const float* pf,
-                                                           uint64_t pf_n) {
+                                                           uint64_t pf_n, const uint32_t* pos_rows,
+                                                           float* k_out, float* v_out) {
     extern __shared__ __align__(16) float dsm[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t npair = (q_dim + 2 * kv_dim) / 2;
@@ -439,11 +440,14 @@ __global__ void __launch_bounds__(384, 1) dec_qkv_rope_kernel(const float* __res
         const bool rot = n0 < q_dim + kv_dim;
         const uint32_t half = hd >> 1, col = n0 < q_dim ? n0 : n0 - q_dim;
         float b0 = 0.f, b1 = 0.f, c = 0.f, sn_ = 0.f;
+        // row r's position: consecutive from pos0 (one sequence), or its own
+        // (rows of different sequences)
+        const uint64_t pos = lane < R ? (pos_rows ? pos_rows[lane] : pos0 + lane) : 0;
         if (lane < R) {
             if (bias) { b0 = bias[n0]; b1 = bias[n0 + 1]; }
             if (rot) {
-                c = cs[(uint64_t)(pos0 + lane) * half + (col % hd) / 2];
-                sn_ = sn[(uint64_t)(pos0 + lane) * half + (col % hd) / 2];
+                c = cs[pos * half + (col % hd) / 2];
+                sn_ = sn[pos * half + (col % hd) / 2];
             }
         }
         float ab[2][kDecRows];
@@ -451,16 +455,18 @@ __global__ void __launch_bounds__(384, 1) dec_qkv_rope_kernel(const float* __res
         float v0 = pick_row(ab[0]), v1 = pick_row(ab[1]);
         if (lane < R) {
             if (bias) { v0 += b0; v1 += b1; }
-            const uint64_t pos = pos0 + lane;
             if (rot) {
                 const float r0 = __fmaf_rn(v0, c, -__fmul_rn(v1, sn_));
                 const float r1 = __fmaf_rn(v0, sn_, __fmul_rn(v1, c));
                 float* dst = n0 < q_dim ? q_out + (uint64_t)lane * q_dim + col
-                                        : kvc + pos * kv_dim + col;
+                             : kvc      ? kvc + pos * kv_dim + col
+                                        : k_out + (uint64_t)lane * kv_dim + col;
                 dst[0] = r0;
                 dst[1] = r1;
             } else {
-                float* dst = kvc + ((uint64_t)max_seq + pos) * kv_dim + (n0 - q_dim - kv_dim);
+                const uint32_t vc = n0 - q_dim - kv_dim;
+                float* dst = kvc ? kvc + ((uint64_t)max_seq + pos) * kv_dim + vc
+                                 : v_out + (uint64_t)lane * kv_dim + vc;
                 dst[0] = v0;
                 dst[1] = v1;
             }
@@ -778,7 +784,26 @@ extern "C" int tgkv_fwd_dec_qkv_rope(const float* w, const float* x, const float
     const uint32_t npair = (q_dim + 2 * kv_dim) / 2, nw = warps_for(npair, sm_count());
     return launch_pdl_n(dec_qkv_rope_kernel, dim3(blocks_for(npair, nw)), nw * 32, sm, stream, w,
                         x, g, bias, cs, sn, q_out, kvc, R, d, q_dim, kv_dim, hd, pos0, max_seq,
-                        pf, pf_n);
+                        pf, pf_n, (const uint32_t*)nullptr, (float*)nullptr, (float*)nullptr);
+}
+
+extern "C" int tgkv_fwd_dec_qkv_rows(const float* w, const float* x, const float* g,
+                                     const float* bias, const float* cs, const float* sn,
+                                     float* q_out, float* k_out, float* v_out, uint32_t R,
+                                     uint32_t d, uint32_t q_dim, uint32_t kv_dim, uint32_t hd,
+                                     const uint32_t* pos_rows, uint32_t max_seq, const float* pf,
+                                     uint64_t pf_n, void* stream) {
+    if (R == 0 || R > kDecRows || d % 4 || hd % 2 || q_dim % hd || kv_dim % hd || !pos_rows ||
+        !k_out || !v_out)
+        return (int)cudaErrorInvalidValue;
+    const size_t sm = dec_smem(R, d);
+    if (sm > 200 * 1024) return (int)cudaErrorInvalidValue;
+    int e;
+    if ((e = set_smem(dec_qkv_rope_kernel, sm))) return e;
+    const uint32_t npair = (q_dim + 2 * kv_dim) / 2, nw = warps_for(npair, sm_count());
+    return launch_pdl_n(dec_qkv_rope_kernel, dim3(blocks_for(npair, nw)), nw * 32, sm, stream, w,
+                        x, g, bias, cs, sn, q_out, (float*)nullptr, R, d, q_dim, kv_dim, hd, 0u,
+                        max_seq, pf, pf_n, pos_rows, k_out, v_out);
 }
 
 extern "C" int tgkv_fwd_dec_w3_combine(const float* w3, const float* h, const int32_t* top_ids,

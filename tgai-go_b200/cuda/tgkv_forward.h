@@ -73,6 +73,14 @@ int tgkv_fwd_dec_qkv_rope(const float* w, const float* x, const float* g, const 
                           const float* cs, const float* sn, float* q_out, float* kvc, uint32_t R,
                           uint32_t d, uint32_t q_dim, uint32_t kv_dim, uint32_t hd, uint32_t pos0,
                           uint32_t max_seq, const float* pf, uint64_t pf_n, void* stream);
+/* The same for R token rows of different sequences: row r at position
+ * pos_rows[r] (device [R]); the rotated K rows and the V rows go to k_out /
+ * v_out [R][kv_dim] (for the batched attention, which appends them). */
+int tgkv_fwd_dec_qkv_rows(const float* w, const float* x, const float* g, const float* bias,
+                          const float* cs, const float* sn, float* q_out, float* k_out,
+                          float* v_out, uint32_t R, uint32_t d, uint32_t q_dim, uint32_t kv_dim,
+                          uint32_t hd, const uint32_t* pos_rows, uint32_t max_seq,
+                          const float* pf, uint64_t pf_n, void* stream);
 /* Router and experts W1/W2 in one launch: for every pair p = (r, k),
  * ln = rmsnorm(x[r], g), the router's top-na of ln . router^T (+ bias) with
  * softmax weights, and h[p] = silu(W1[e_k] ln) * (W2[e_k] ln); top_ids /
@@ -107,6 +115,7 @@ typedef struct {
     uint32_t n_layers, d, n_heads, n_kv_heads, head_dim, dff, ne, na, pos, max_seq;
     uint32_t sx_floats;             /* max(d, q_dim) */
     float scale;                    /* score scale: 1/sqrt(head_dim) times the YaRN mscale */
+    uint32_t prefetch;              /* 1: each phase's weight rows go to L2 a phase ahead */
 } TGFwdStepParams;
 int tgkv_fwd_step_supported(uint32_t d, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
                             uint32_t dff, uint32_t ne, uint32_t na);

@@ -114,7 +114,81 @@ struct TGFwdModel {
     Slot* slots;
     uint32_t max_slots, live;
     long long rejects;
+    /* one-token decodes of different slots gathered into one pass (below) */
+    pthread_mutex_t bmu;           /* the request queue and the leader flag */
+    pthread_cond_t bcv;
+    struct BatchReq* bq_head;
+    struct BatchReq* bq_tail;
+    int b_leader;                  /* a thread is running a batch */
+    pthread_mutex_t pmu;           /* the batch workspace and plans, held while a batch runs */
+    Slot bs;                       /* the batch's stream and workspaces (no KV) */
+    float *b_knew, *b_vnew;        /* [rows][kv_dim]: K/V rows for the fused append */
+    uint32_t *b_pos, *bh_pos;      /* positions, device and page-locked [rows] */
+    float *b_logits, *bh_logits;   /* [rows][vocab], device and page-locked */
+    struct BatchPlan* plans;       /* [kPlanCache] */
+    uint64_t plan_clock;
+    long long batched_tokens, batches;
 };
+
+/* ---- batched decode across slots: types ----------------------------------- */
+enum { kPlanCache = 16 };
+/* One batch composition (slot ids in ascending order) and, per layer, a
+ * batch plan over those slots' caches of that layer. */
+struct BatchPlan {
+    uint32_t n;
+    int ids[8];
+    TGKvBatch** b;                 /* [n_layers], NULL when the entry is empty */
+    uint64_t used;
+};
+/* A one-token decode waiting in the queue, run by whichever thread leads. */
+typedef struct BatchReq {
+    Slot* s;
+    int32_t id;
+    uint32_t pos;
+    int state;                     /* 0 queued, 1 taken, 2 done */
+    int ok;
+    uint32_t launches;
+    char err[256];
+    struct BatchReq* next;
+} BatchReq;
+
+static void plan_drop(TGFwdModel* m, struct BatchPlan* bp) {
+    if (bp->b) {
+        for (uint32_t l = 0; l < m->c.n_layers; l++) tg_kv_batch_destroy(bp->b[l]);
+        free(bp->b);
+    }
+    memset(bp, 0, sizeof(*bp));
+}
+
+/* Plans that hold slot `id`'s caches (all plans for id < 0). */
+static void plans_drop_slot(TGFwdModel* m, int id) {
+    if (!m->plans) return;
+    for (int i = 0; i < kPlanCache; i++) {
+        struct BatchPlan* bp = &m->plans[i];
+        if (!bp->b) continue;
+        int hit = id < 0;
+        for (uint32_t j = 0; j < bp->n && !hit; j++) hit = bp->ids[j] == id;
+        if (hit) plan_drop(m, bp);
+    }
+}
+
+static void slot_release_mem(TGFwdModel* m, Slot* s);
+
+static void batch_release(TGFwdModel* m) {
+    plans_drop_slot(m, -1);
+    free(m->plans);
+    m->plans = NULL;
+    slot_release_mem(m, &m->bs);
+    tg_cuda_kv_free(m->b_knew);
+    tg_cuda_kv_free(m->b_vnew);
+    tg_cuda_kv_free(m->b_pos);
+    tg_cuda_kv_free(m->b_logits);
+    tgkv_fwd_host_free(m->bh_pos);
+    tgkv_fwd_host_free(m->bh_logits);
+    m->b_knew = m->b_vnew = m->b_logits = m->bh_logits = NULL;
+    m->b_pos = m->bh_pos = NULL;
+}
+
 
 /* The fused decode kernels stage R token rows of K floats in shared memory. */
 static int decode_fits(uint32_t R, uint32_t K) {
@@ -201,6 +275,7 @@ static void slot_release_mem(TGFwdModel* m, Slot* s);
 
 void tg_fwd_destroy(TGFwdModel* m) {
     if (!m) return;
+    batch_release(m);
     if (m->slots)
         for (uint32_t i = 0; i < m->max_slots; i++) slot_release_mem(m, &m->slots[i]);
     free(m->slots);
@@ -216,6 +291,9 @@ void tg_fwd_destroy(TGFwdModel* m) {
     tg_cuda_kv_free(m->sn);
     tg_cuda_kv_free(m->step_layers);
     pthread_mutex_destroy(&m->mu);
+    pthread_mutex_destroy(&m->bmu);
+    pthread_mutex_destroy(&m->pmu);
+    pthread_cond_destroy(&m->bcv);
     free(m);
 }
 
@@ -349,6 +427,9 @@ TGFwdModel* tg_fwd_create(const TGFwdConfig* cfg, TGFwdWeightFn get, void* ctx) 
     TGFwdModel* m = (TGFwdModel*)calloc(1, sizeof(TGFwdModel));
     if (!m) { set_err("host allocation failed"); return NULL; }
     pthread_mutex_init(&m->mu, NULL);
+    pthread_mutex_init(&m->bmu, NULL);
+    pthread_mutex_init(&m->pmu, NULL);
+    pthread_cond_init(&m->bcv, NULL);
     m->c = c;
     m->hd = c.head_dim;
     m->nkv = c.n_kv_heads;
@@ -594,13 +675,16 @@ int tg_fwd_reset_slot(TGFwdModel* m, const void* key) {
 
 int tg_fwd_free_slot(TGFwdModel* m, const void* key) {
     if (!m) return 0;
+    pthread_mutex_lock(&m->pmu);        /* no batch is running over its caches */
     pthread_mutex_lock(&m->mu);
     Slot* s = find_slot(m, key);
     if (s) {
+        plans_drop_slot(m, s->id);
         slot_release_mem(m, s);
         m->live--;
     }
     pthread_mutex_unlock(&m->mu);
+    pthread_mutex_unlock(&m->pmu);
     return s != NULL;
 }
 
@@ -712,6 +796,36 @@ static int attn_half(TGFwdModel* m, Slot* s, const Layer* L, TGKvCache* kv, uint
     return 1;
 }
 
+/* The rest of a decode layer after the attention (attention output in
+ * s->attn, R token rows): out projection + residual, then the FFN, each with
+ * its norm fused; each launch prefetches the weights of a later one (the
+ * routed experts' W3 once the router has chosen; the next layer's Q/K/V). */
+static int decode_tail(TGFwdModel* m, Slot* s, uint32_t l, uint32_t R) {
+    const Layer* L = &m->L[l];
+    const TGFwdConfig* c = &m->c;
+    const uint32_t d = c->d_model, dff = c->d_ff, ne = c->n_experts, na = c->n_activated;
+    void* st = s->stream;
+    const Layer* Ln = l + 1 < c->n_layers ? &m->L[l + 1] : NULL;
+    const float* next_qkv = Ln ? pf(Ln->wqkv, 4) : NULL;
+    const uint64_t next_qkv_n = (uint64_t)m->qkv_dim * d;
+    if (ne == 0) {
+        CHECK_LAUNCH(tgkv_fwd_dec_gemv(1, L->wo, s->attn, m->q_dim, NULL, NULL, s->x, d, R, d,
+                                       m->q_dim, 0, pf(L->w12, 8), (uint64_t)2 * dff * d, st));
+        CHECK_LAUNCH(tgkv_fwd_dec_gemv(2, L->w12, s->x, d, L->ln2, NULL, s->h, dff, R, dff,
+                                       d, 1, pf(L->w3, 8), (uint64_t)d * dff, st));
+        CHECK_LAUNCH(tgkv_fwd_dec_gemv(1, L->w3, s->h, dff, NULL, NULL, s->x, d, R, d, dff,
+                                       0, next_qkv, next_qkv_n, st));
+        return 1;
+    }
+    CHECK_LAUNCH(tgkv_fwd_dec_gemv(1, L->wo, s->attn, m->q_dim, NULL, NULL, s->x, d, R, d,
+                                   m->q_dim, 0, NULL, 0, st));
+    CHECK_LAUNCH(tgkv_fwd_dec_moe_w12(s->x, L->ln2, L->router, L->qb, L->w12, s->top_ids,
+                                      s->top_w, s->h, R, d, dff, ne, na, pf(L->w3, 2), st));
+    CHECK_LAUNCH(tgkv_fwd_dec_w3_combine(L->w3, s->h, s->top_ids, s->top_w, s->x, R, d, dff,
+                                         ne, na, next_qkv, next_qkv_n, st));
+    return 1;
+}
+
 static int run_layer(TGFwdModel* m, Slot* s, uint32_t l, uint32_t seq, uint32_t pos) {
     const Layer* L = &m->L[l];
     const TGFwdConfig* c = &m->c;
@@ -719,30 +833,7 @@ static int run_layer(TGFwdModel* m, Slot* s, uint32_t l, uint32_t seq, uint32_t 
     void* st = s->stream;
     const int decode = decode_fits(seq, d) && decode_fits(seq, m->q_dim) && decode_fits(seq, dff);
     if (!attn_half(m, s, L, s->kv[l], seq, pos, decode)) return 0;
-    if (decode) {
-        /* out projection + residual, then the FFN, each with its norm fused;
-         * each launch prefetches the weights of a later one (the routed
-         * experts' W3 once the router has chosen; the next layer's Q/K/V) */
-        const Layer* Ln = l + 1 < c->n_layers ? &m->L[l + 1] : NULL;
-        const float* next_qkv = Ln ? pf(Ln->wqkv, 4) : NULL;
-        const uint64_t next_qkv_n = (uint64_t)m->qkv_dim * d;
-        if (ne == 0) {
-            CHECK_LAUNCH(tgkv_fwd_dec_gemv(1, L->wo, s->attn, m->q_dim, NULL, NULL, s->x, d, seq, d,
-                                           m->q_dim, 0, pf(L->w12, 8), (uint64_t)2 * dff * d, st));
-            CHECK_LAUNCH(tgkv_fwd_dec_gemv(2, L->w12, s->x, d, L->ln2, NULL, s->h, dff, seq, dff,
-                                           d, 1, pf(L->w3, 8), (uint64_t)d * dff, st));
-            CHECK_LAUNCH(tgkv_fwd_dec_gemv(1, L->w3, s->h, dff, NULL, NULL, s->x, d, seq, d, dff,
-                                           0, next_qkv, next_qkv_n, st));
-            return 1;
-        }
-        CHECK_LAUNCH(tgkv_fwd_dec_gemv(1, L->wo, s->attn, m->q_dim, NULL, NULL, s->x, d, seq, d,
-                                       m->q_dim, 0, NULL, 0, st));
-        CHECK_LAUNCH(tgkv_fwd_dec_moe_w12(s->x, L->ln2, L->router, L->qb, L->w12, s->top_ids,
-                                          s->top_w, s->h, seq, d, dff, ne, na, pf(L->w3, 2), st));
-        CHECK_LAUNCH(tgkv_fwd_dec_w3_combine(L->w3, s->h, s->top_ids, s->top_w, s->x, seq, d, dff,
-                                             ne, na, next_qkv, next_qkv_n, st));
-        return 1;
-    }
+    if (decode) return decode_tail(m, s, l, seq);
     if (!gemm(s, seq, d, m->q_dim, s->attn, m->q_dim, L->wo_b, L->wo_s, s->x, d, 1)) return 0;
     CHECK_LAUNCH(tgkv_fwd_rmsnorm(s->ln, s->x, L->ln2, seq, d, d, d, 1e-6f, st));
     if (ne == 0) {
@@ -834,6 +925,10 @@ static int run_step(TGFwdModel* m, Slot* s, uint32_t pos) {
     p.max_seq = c->max_seq_len;
     p.sx_floats = c->d_model > m->q_dim ? c->d_model : m->q_dim;
     p.scale = 1.0f / sqrtf((float)m->hd);
+    {   /* L2 prefetch of the next phase's weights; TGKV_STEP_PREFETCH=0 turns it off */
+        const char* pe = getenv("TGKV_STEP_PREFETCH");
+        p.prefetch = !(pe && pe[0] == '0');
+    }
     const int e = tgkv_fwd_decode_step(&p, st);
     if (e < 0) {
         __atomic_store_n(&m->step_refused, 1, __ATOMIC_RELAXED);
@@ -904,6 +999,234 @@ static int run_forward(TGFwdModel* m, Slot* s, const int32_t* ids, uint32_t seq,
     return 1;
 }
 
+/* ---- batched decode across slots -------------------------------------------
+ * The reference bridge runs every slot on its own stream with no lock on
+ * forward (cuda/tgai_cuda_bridge.c:147-162), so sequences served from
+ * several threads decode side by side, each reading all the weights.  Here a
+ * one-token forward joins a queue; the first thread to find no batch running
+ * leads: it takes up to tgkv_fwd_decode_rows() queued requests of different
+ * slots and runs them as ONE pass over the weights -- R token rows through
+ * the per-layer decode kernels, the attention as one ragged launch over the
+ * slots' caches with the K/V append fused in -- then wakes their threads.
+ * A request that finds itself alone takes the single-sequence path (the
+ * one-launch decode step).  Requests that arrive while a batch runs form the
+ * next one, so a busy server batches by itself and an idle one adds no wait.
+ * TGKV_FWD_BATCH=0 turns it off (every request runs alone, as before). */
+static int batch_on(const TGFwdModel* m) {
+    static int v = -1;
+    int on = __atomic_load_n(&v, __ATOMIC_RELAXED);
+    if (on < 0) {
+        const char* e = getenv("TGKV_FWD_BATCH");
+        on = !(e && e[0] == '0');
+        __atomic_store_n(&v, on, __ATOMIC_RELAXED);
+    }
+    const uint32_t R = tgkv_fwd_decode_rows();
+    return on && R >= 2 && decode_fits(R, m->c.d_model) && decode_fits(R, m->q_dim) &&
+           decode_fits(R, m->c.d_ff);
+}
+
+/* The batch workspace, made by the first batch (caller holds pmu). */
+static int batch_ready(TGFwdModel* m) {
+    if (m->plans) return 1;
+    const uint32_t R = tgkv_fwd_decode_rows();
+    Slot* b = &m->bs;
+    if (!b->stream && !(b->stream = tg_cuda_kv_stream_create())) {
+        set_err("batch stream: %s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    if (!slot_reserve(m, b, R)) return 0;
+    m->b_knew = (float*)tg_cuda_kv_malloc((uint64_t)R * m->kv_dim * 4);
+    m->b_vnew = (float*)tg_cuda_kv_malloc((uint64_t)R * m->kv_dim * 4);
+    m->b_pos = (uint32_t*)tg_cuda_kv_malloc((uint64_t)R * 4);
+    m->b_logits = (float*)tg_cuda_kv_malloc((uint64_t)R * m->rows * 4);
+    m->bh_pos = (uint32_t*)tgkv_fwd_host_alloc((uint64_t)R * 4);
+    m->bh_logits = (float*)tgkv_fwd_host_alloc((uint64_t)R * m->rows * 4);
+    struct BatchPlan* plans = (struct BatchPlan*)calloc(kPlanCache, sizeof(struct BatchPlan));
+    if (!m->b_knew || !m->b_vnew || !m->b_pos || !m->b_logits || !m->bh_pos || !m->bh_logits ||
+        !plans) {
+        free(plans);
+        set_err("batch workspace: allocation failed");
+        return 0;
+    }
+    m->plans = plans;
+    return 1;
+}
+
+/* The per-layer plans over the caches of slots rq[0..n) (ascending ids),
+ * from the cache or made now (caller holds pmu). */
+static TGKvBatch** batch_plans(TGFwdModel* m, BatchReq** rq, uint32_t n) {
+    struct BatchPlan* lru = &m->plans[0];
+    for (int i = 0; i < kPlanCache; i++) {
+        struct BatchPlan* bp = &m->plans[i];
+        if (bp->b && bp->n == n) {
+            uint32_t j = 0;
+            while (j < n && bp->ids[j] == rq[j]->s->id) j++;
+            if (j == n) {
+                bp->used = ++m->plan_clock;
+                return bp->b;
+            }
+        }
+        if (!bp->b || (lru->b && bp->used < lru->used)) lru = bp;
+    }
+    plan_drop(m, lru);
+    lru->b = (TGKvBatch**)calloc(m->c.n_layers, sizeof(TGKvBatch*));
+    if (!lru->b) { set_err("host allocation failed"); return NULL; }
+    TGKvCache* cs[8];
+    for (uint32_t l = 0; l < m->c.n_layers; l++) {
+        for (uint32_t j = 0; j < n; j++) cs[j] = rq[j]->s->kv[l];
+        if (!(lru->b[l] = tg_kv_batch_create(cs, n, m->c.n_heads))) {
+            set_err("batch plan: %s", tg_kv_last_error());
+            plan_drop(m, lru);
+            return NULL;
+        }
+    }
+    lru->n = n;
+    for (uint32_t j = 0; j < n; j++) lru->ids[j] = rq[j]->s->id;
+    lru->used = ++m->plan_clock;
+    return lru->b;
+}
+
+/* One token of each of the n >= 2 requests (distinct slots, ascending ids)
+ * through every layer in one pass; each slot's h_logits receives its row.
+ * Caller holds pmu. */
+static int run_batch(TGFwdModel* m, BatchReq** rq, uint32_t n) {
+    const TGFwdConfig* c = &m->c;
+    const uint32_t d = c->d_model;
+    if (!batch_ready(m)) return 0;
+    Slot* b = &m->bs;
+    void* st = b->stream;
+    for (uint32_t j = 0; j < n; j++) {
+        Slot* s = rq[j]->s;
+        const uint32_t pos = rq[j]->pos;
+        /* each sequence's gap rule and LCP, as run_forward applies them */
+        if (s->kv_hi > 0 && (int)pos > s->last_pos &&
+            !(slot_clear(m, s) && tg_cuda_kv_sync(s->stream)))
+            return 0;
+        for (uint32_t l = 0; l < c->n_layers; l++) {
+            tg_kv_reset(s->kv[l]);
+            tg_kv_advance(s->kv[l], pos);
+        }
+        b->h_ids[j] = rq[j]->id;
+        m->bh_pos[j] = pos;
+    }
+    TGKvBatch** plan = batch_plans(m, rq, n);
+    if (!plan) return 0;
+    if (!tg_cuda_kv_h2d(b->ids, b->h_ids, (size_t)n * 4, st) ||
+        !tg_cuda_kv_h2d(m->b_pos, m->bh_pos, (size_t)n * 4, st)) {
+        set_err("batch upload: %s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    CHECK_LAUNCH(tgkv_fwd_embed(b->x, m->emb, b->ids, n, d, m->rows, c->unk_id, st));
+    for (uint32_t l = 0; l < c->n_layers; l++) {
+        const Layer* L = &m->L[l];
+        /* norm + Q/K/V rows + bias + RoPE at each row's position; K/V rows
+         * for the attention launch, which appends them to each slot's cache */
+        CHECK_LAUNCH(tgkv_fwd_dec_qkv_rows(L->wqkv, b->x, L->ln1, L->bqkv, m->cs, m->sn, b->q,
+                                           m->b_knew, m->b_vnew, n, d, m->q_dim, m->kv_dim, m->hd,
+                                           m->b_pos, c->max_seq_len, pf(L->wo, 1),
+                                           (uint64_t)d * m->q_dim, st));
+        if (!tg_kv_batch_decode(plan[l], b->q, m->b_knew, m->b_vnew, b->attn, st)) {
+            set_err("batch attention: %s", tg_kv_last_error());
+            return 0;
+        }
+        t_launches += tg_kv_batch_last_launches(plan[l]);
+        if (!decode_tail(m, b, l, n)) return 0;
+    }
+    CHECK_LAUNCH(tgkv_fwd_dec_gemv(0, m->emb, b->x, d, m->fnorm, NULL, m->b_logits, m->rows, n,
+                                   m->rows, d, 0, NULL, 0, st));
+    if (!tg_cuda_kv_d2h(m->bh_logits, m->b_logits, (size_t)n * m->rows * 4, st) ||
+        !tg_cuda_kv_sync(st)) {
+        set_err("batch: %s", tg_cuda_kv_last_error());
+        return 0;
+    }
+    for (uint32_t j = 0; j < n; j++) {
+        Slot* s = rq[j]->s;
+        memcpy(s->h_logits, m->bh_logits + (uint64_t)j * m->rows, (size_t)m->rows * 4);
+        s->last_pos = (int)(rq[j]->pos + 1);
+        if (s->last_pos > s->kv_hi) s->kv_hi = s->last_pos;
+    }
+    m->batched_tokens += n;
+    m->batches++;
+    return 1;
+}
+
+/* Run the taken requests: alone through run_forward, else as one batch. */
+static void run_taken(TGFwdModel* m, BatchReq** rq, uint32_t n) {
+    int ok;
+    t_launches = 0;
+    if (n == 1) {
+        ok = run_forward(m, rq[0]->s, &rq[0]->id, 1, rq[0]->pos);
+        if (!ok) tg_cuda_kv_sync(rq[0]->s->stream);
+    } else {
+        /* ascending slot ids: one plan per set of slots */
+        for (uint32_t i = 1; i < n; i++)
+            for (uint32_t j = i; j > 0 && rq[j - 1]->s->id > rq[j]->s->id; j--) {
+                BatchReq* t = rq[j];
+                rq[j] = rq[j - 1];
+                rq[j - 1] = t;
+            }
+        pthread_mutex_lock(&m->pmu);
+        ok = run_batch(m, rq, n);
+        pthread_mutex_unlock(&m->pmu);
+        if (!ok) tg_cuda_kv_sync(m->bs.stream);
+    }
+    for (uint32_t j = 0; j < n; j++) {
+        rq[j]->ok = ok;
+        rq[j]->launches = t_launches;
+        if (!ok) snprintf(rq[j]->err, sizeof(rq[j]->err), "%s", t_err);
+    }
+}
+
+static const float* forward_one(TGFwdModel* m, Slot* s, int32_t id, uint32_t pos) {
+    BatchReq r;
+    memset(&r, 0, sizeof(r));
+    r.s = s;
+    r.id = id;
+    r.pos = pos;
+    const uint32_t R = tgkv_fwd_decode_rows();
+    pthread_mutex_lock(&m->bmu);
+    for (BatchReq* q = m->bq_head; q; q = q->next)
+        if (q->s == s) {
+            pthread_mutex_unlock(&m->bmu);
+            set_err("slot %d already has a forward in flight", s->id);
+            return NULL;
+        }
+    if (m->bq_tail) m->bq_tail->next = &r;
+    else m->bq_head = &r;
+    m->bq_tail = &r;
+    while (r.state != 2) {
+        if (!m->b_leader && m->bq_head) {
+            /* lead: take up to R requests from the head of the queue */
+            m->b_leader = 1;
+            BatchReq* take[8];
+            uint32_t n = 0;
+            while (m->bq_head && n < R && n < 8) {
+                BatchReq* q = m->bq_head;
+                m->bq_head = q->next;
+                if (!m->bq_head) m->bq_tail = NULL;
+                q->next = NULL;
+                q->state = 1;
+                take[n++] = q;
+            }
+            pthread_mutex_unlock(&m->bmu);
+            run_taken(m, take, n);
+            pthread_mutex_lock(&m->bmu);
+            for (uint32_t j = 0; j < n; j++) take[j]->state = 2;
+            m->b_leader = 0;
+            pthread_cond_broadcast(&m->bcv);
+            continue;
+        }
+        pthread_cond_wait(&m->bcv, &m->bmu);
+    }
+    pthread_mutex_unlock(&m->bmu);
+    t_launches = r.launches;
+    if (!r.ok) {
+        set_err("%s", r.err);
+        return NULL;
+    }
+    return s->h_logits;
+}
+
 const float* tg_fwd_forward(TGFwdModel* m, const void* key, const int32_t* ids,
                             uint32_t seq_len, uint32_t cache_pos) {
     t_launches = 0;
@@ -915,11 +1238,19 @@ const float* tg_fwd_forward(TGFwdModel* m, const void* key, const int32_t* ids,
     }
     Slot* s = slot_get(m, key);
     if (!s) return NULL;
+    if (seq_len == 1 && batch_on(m)) return forward_one(m, s, ids[0], cache_pos);
     if (!run_forward(m, s, ids, seq_len, cache_pos)) {
         tg_cuda_kv_sync(s->stream);
         return NULL;
     }
     return s->h_logits;
+}
+
+/* Tokens decoded in batches of two or more, and the number of those batches
+ * (a report for tests and the bench). */
+void tg_fwd_batch_stats(const TGFwdModel* m, uint64_t* tokens, uint64_t* batches) {
+    if (tokens) *tokens = m ? (uint64_t)m->batched_tokens : 0;
+    if (batches) *batches = m ? (uint64_t)m->batches : 0;
 }
 
 int tg_fwd_gemm_f32(uint32_t M, uint32_t N, uint32_t K, const float* x, uint32_t ldx,

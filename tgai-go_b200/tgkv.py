@@ -205,6 +205,7 @@ PROTOS = {
     "tg_fwd_last_launches": (u32, []),
     "tg_fwd_last_error": (cp, []),
     "tg_fwd_gemm_f32": (i32, [u32, u32, u32, vp, u32, vp, u32, vp, u32, i32, vp]),
+    "tg_fwd_batch_stats": (None, [vp, C.POINTER(u64), C.POINTER(u64)]),
 }
 
 _lib = None
