@@ -39,6 +39,10 @@ int         tg_cuda_kv_sm_count(void);
 void* tg_cuda_kv_malloc(size_t bytes);          /* zero-filled; NULL on failure */
 void  tg_cuda_kv_free(void* p);
 int   tg_cuda_kv_h2d(void* dst, const void* src, size_t bytes, void* stream);
+/* Host to device on `stream`, asynchronous also when stream is NULL (the
+ * legacy default stream), where tg_cuda_kv_h2d copies synchronously.  A
+ * pageable source may be reused as soon as this returns. */
+int   tg_cuda_kv_h2d_async(void* dst, const void* src, size_t bytes, void* stream);
 int   tg_cuda_kv_d2h(void* dst, const void* src, size_t bytes, void* stream);
 int   tg_cuda_kv_memset(void* dst, int value, size_t bytes, void* stream);
 /* The h2d/d2h/memset calls block when stream is NULL; otherwise they are

@@ -330,6 +330,12 @@ int tg_cuda_kv_h2d(void* dst, const void* src, size_t bytes, void* stream) {
                    "h2d async");
 }
 
+int tg_cuda_kv_h2d_async(void* dst, const void* src, size_t bytes, void* stream) {
+    if (!bytes) return 1;
+    return cuda_ok(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, (cudaStream_t)stream),
+                   "h2d async");
+}
+
 int tg_cuda_kv_d2h(void* dst, const void* src, size_t bytes, void* stream) {
     if (!bytes) return 1;
     if (!stream) return cuda_ok(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost), "d2h");
