@@ -43,6 +43,10 @@ METRIC = "decode attn+KV-append tokens/s & HBM GB/s vs ~8 TB/s peak at 1/2/4/8 B
 
 WORKLOADS = {
     # name: sequences per rank, layers, q heads, kv heads, head_dim, length range
+    # (caches bf16 unless the entry says dtype "f32")
+    "cfg1": dict(n_seq=1, layers=4, nh=8, nkv=8, hd=64, lmin=512, lmax=512, dtype="f32",
+                 desc="configs[0] at its largest context: 1 seq, L=512, 4 layers, 8q/8kv, hd64, "
+                      "fp32"),
     "cfg4": dict(n_seq=64, layers=32, nh=32, nkv=8, hd=128, lmin=1024, lmax=32768,
                  desc="configs[3]: 64 seqs, L~U[1k,32k], 32 layers, 32q/8kv, hd128, bf16"),
     "cfg5": dict(n_seq=1, layers=32, nh=32, nkv=8, hd=128, lmin=131072, lmax=131072,
@@ -189,6 +193,10 @@ def rank_lengths(wl, seed, rank, world, shard_seqs):
         return all_lens
     import shard
     return all_lens[shard.lpt_partition(all_lens, world)[rank]]
+
+
+def cache_esize(wl):
+    return 4 if wl.get("dtype") == "f32" else 2
 
 
 def attn_bytes(lens_after, nh, nkv, hd, b=2):
@@ -374,7 +382,8 @@ def decode_run(args, lib, name, world, rank, local, mode, cpu=False):
     for i in range(n_seq):
         L = int(lens0[i])
         for l in range(layers):
-            c = lib.tg_kv_create_ex(L + total_steps, nkv, hd, tgkv.TG_KV_BF16)
+            c = lib.tg_kv_create_ex(L + total_steps, nkv, hd,
+                                    tgkv.TG_KV_F32 if cache_esize(wl) == 4 else tgkv.TG_KV_BF16)
             tgkv.check(c, lib, "tg_kv_create_ex")
             k = torch.randn(L, kvd, device="cuda", generator=gen)
             v = torch.randn(L, kvd, device="cuda", generator=gen)
@@ -465,7 +474,8 @@ def decode_run(args, lib, name, world, rank, local, mode, cpu=False):
     kid = lib.tg_cuda_kv_attn_last_kernel()
     ms = t0.elapsed_time(t1) / args.steps
     ms_max = max_over_ranks(ms)
-    algo = sum(attn_bytes(lens_step + s_, nh, nkv, hd) for s_ in range(args.steps)) * layers
+    algo = sum(attn_bytes(lens_step + s_, nh, nkv, hd, cache_esize(wl))
+               for s_ in range(args.steps)) * layers
     if per_call_events:
         call_ms = sum(a.elapsed_time(b) for a, b in ev)
     else:
@@ -615,7 +625,8 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
             "higher_is_better": True,
             "scaling": "weak" if mode == "own" and world > 1 else "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "vs_baseline": None, "dtype": "f32" if cache_esize(WORKLOADS[name]) == 4 else "bf16",
+            "data": "synthetic",
             "config": decode_config(args, name, world, mode),
             "hbm_gbs": r["hbm_gbs"],
             "roofline": r["roofline"],

@@ -348,7 +348,8 @@ __device__ __forceinline__ void row_dots_n(const float* const (&w)[NW],
 #pragma unroll
     for (int n = 0; n < NW; ++n)
 #pragma unroll
-        for (int r = 0; r < kDecRows; ++r) acc[n][r] = warp_sum(acc[n][r]);
+        for (int r = 0; r < kDecRows; ++r)
+            if ((uint32_t)r < R) acc[n][r] = warp_sum(acc[n][r]);    // R is warp-uniform
 }
 
 // Lane r < R picks row r's sum.
