@@ -43,6 +43,13 @@ int   tg_cuda_kv_h2d(void* dst, const void* src, size_t bytes, void* stream);
  * legacy default stream), where tg_cuda_kv_h2d copies synchronously.  A
  * pageable source may be reused as soon as this returns. */
 int   tg_cuda_kv_h2d_async(void* dst, const void* src, size_t bytes, void* stream);
+/* dst (device) = a | b | c, read by one small kernel from page-locked host
+ * memory (a, b, c: device pointers of such memory, tg_cuda_kv_host_device_ptr;
+ * sizes and addresses multiples of 16 bytes).  Queued as a programmatic
+ * dependent: it overlaps the previous kernel on `stream` and completes after
+ * it. */
+int   tg_cuda_kv_stage_host(void* dst, const void* a, size_t na, const void* b, size_t nb,
+                            const void* c, size_t nc, void* stream);
 int   tg_cuda_kv_d2h(void* dst, const void* src, size_t bytes, void* stream);
 int   tg_cuda_kv_memset(void* dst, int value, size_t bytes, void* stream);
 /* The h2d/d2h/memset calls block when stream is NULL; otherwise they are

@@ -336,6 +336,15 @@ int tg_cuda_kv_h2d_async(void* dst, const void* src, size_t bytes, void* stream)
                    "h2d async");
 }
 
+int tg_cuda_kv_stage_host(void* dst, const void* a, size_t na, const void* b, size_t nb,
+                          const void* c, size_t nc, void* stream) {
+    if ((na | nb | nc) % 16 || (((uintptr_t)dst | (uintptr_t)a | (uintptr_t)b | (uintptr_t)c) & 15)) {
+        set_err("stage: sizes and addresses must be multiples of 16 bytes");
+        return 0;
+    }
+    return launch_rc(tgkv_launch_stage_host(a, na, b, nb, c, nc, dst, stream), "host staging");
+}
+
 int tg_cuda_kv_d2h(void* dst, const void* src, size_t bytes, void* stream) {
     if (!bytes) return 1;
     if (!stream) return cuda_ok(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost), "d2h");

@@ -365,10 +365,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
     n_tasks = (L + ch - 1) / ch;
     const uint32_t half = hd >> 1;
     const uint32_t npair = (q_dim + 2 * kv_dim) / 2;
-    // Each phase's weight rows go to L2 one phase ahead (the routed experts'
-    // as soon as the router has chosen), so HBM keeps streaming while the
-    // grid waits at a barrier.  Every warp prefetches exactly the rows it
-    // will read itself.
+    // With p.prefetch, each phase's weight rows go to L2 one phase ahead (the
+    // routed experts' as soon as the router has chosen), so HBM keeps
+    // streaming while the grid waits at a barrier; every warp prefetches
+    // exactly the rows it will read itself.  Off by default: it measured
+    // slower, the early streams queueing ahead of the current phase's loads.
     if (p.prefetch) prefetch_rows(p.layers[0].wqkv, 2 * (uint64_t)d, 8 * d, gw, tw, npair);
 
     for (uint32_t l = 0; l < p.n_layers; ++l) {

@@ -844,6 +844,69 @@ extern "C" int tgkv_launch_gather_wait(const uint32_t* flag, uint32_t target, in
     return (int)cudaGetLastError();
 }
 
+namespace tgkv {
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("TGKV_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// Up to three page-locked host arrays (device-mapped pointers) copied into
+// one device buffer back to back.  Every thread issues all its loads before
+// any store, so the PCIe round trip is paid once.  Launched as a programmatic
+// dependent that waits for nothing before its copies (the inputs are host
+// data), it overlaps the previous kernel's tail; it waits for that kernel at
+// its end, so a kernel waiting for this one also follows the previous one.
+__global__ void __launch_bounds__(256) stage_host_kernel(const float4* __restrict__ a,
+                                                         uint32_t na, const float4* __restrict__ b,
+                                                         uint32_t nb, const float4* __restrict__ c,
+                                                         uint32_t nc, float4* dst) {
+    constexpr int kPer = 8;
+    const uint32_t n = na + nb + nc;
+    for (uint32_t base = blockIdx.x * 256u * kPer; base < n; base += gridDim.x * 256u * kPer) {
+        float4 v[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const uint32_t i = base + u * 256u + threadIdx.x;
+            v[u] = i < na ? a[i] : i < na + nb ? b[i - na] : i < n ? c[i - na - nb]
+                                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const uint32_t i = base + u * 256u + threadIdx.x;
+            if (i < n) dst[i] = v[u];
+        }
+    }
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+}  // namespace tgkv
+
+extern "C" int tgkv_launch_stage_host(const void* a, uint64_t na, const void* b, uint64_t nb,
+                                      const void* c, uint64_t nc, void* dst, void* stream) {
+    const uint64_t n4 = (na + nb + nc) / 16;
+    if (!n4) return 0;
+    uint64_t blocks = (n4 + 256 * 8 - 1) / (256 * 8);
+    if (blocks > 148) blocks = 148;
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.blockDim = dim3(256);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = tgkv::pdl_enabled() ? 1 : 0;
+    return (int)cudaLaunchKernelEx(&cfg, tgkv::stage_host_kernel,
+                                   static_cast<const float4*>(a), (uint32_t)(na / 16),
+                                   static_cast<const float4*>(b), (uint32_t)(nb / 16),
+                                   static_cast<const float4*>(c), (uint32_t)(nc / 16),
+                                   static_cast<float4*>(dst));
+}
+
 extern "C" int tgkv_launch_rope_append(const TGKvRopeParams* p, void* stream) {
     const uint64_t total = (uint64_t)p->n_tokens * p->n_heads * (p->head_dim / 2);
     if (total == 0) return 0;

@@ -147,6 +147,11 @@ int tgkv_launch_append(const TGKvAppendParams* p, int dtype, void* stream);
  * until *flag has reached target (wrap-safe). */
 int tgkv_launch_gather_wait(const uint32_t* flag, uint32_t target, int32_t* err, void* stream);
 int tgkv_launch_rope_append(const TGKvRopeParams* p, void* stream);
+/* dst (device) = a | b | c: device-mapped pointers of page-locked host
+ * memory, byte counts multiples of 16, all 16-byte aligned.  A programmatic
+ * dependent that overlaps the previous kernel and completes after it. */
+int tgkv_launch_stage_host(const void* a, uint64_t na, const void* b, uint64_t nb,
+                           const void* c, uint64_t nc, void* dst, void* stream);
 /* Chunk length the planner uses for a launch of total_positions (bridge). */
 uint32_t tgkv_pick_chunk(const uint32_t* n_pos, uint32_t n_items, uint32_t mult, uint32_t sm_count);
 /* The same with `slots` resident CTAs per wave and chunks a multiple of tile. */

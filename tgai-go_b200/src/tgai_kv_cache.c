@@ -343,7 +343,11 @@ struct TGKvBatch {
     int slot_used[2];
     uint32_t slot;
     uint32_t last_launches;
-    void* pack;                       /* small inputs: q|k|v packed on the host (pageable) */
+    /* small page-locked inputs: two device slots the staging kernel fills in
+     * turn, and the device pointers of the last host buffers seen */
+    float* small_io[2];
+    uint64_t small_bytes;
+    uint32_t small_slot;
 };
 
 TGKvBatch* tg_kv_batch_create(TGKvCache* const* caches, uint32_t n, uint32_t n_heads) {
@@ -418,7 +422,9 @@ void tg_kv_batch_destroy(TGKvBatch* b) {
         tg_cuda_kv_event_destroy(b->slot_free[i]);
     }
     tg_cuda_kv_stream_destroy(b->copy_stream);
-    free(b->pack);
+    if (b->be && b->be->free)
+        for (int i = 0; i < 2; i++)
+            if (b->small_io[i]) b->be->free(b->small_io[i]);
     free(b->caches);
     free(b->npos);
     free(b);
@@ -596,9 +602,10 @@ int tg_kv_batch_decode_gather(TGKvBatch* b, const float* q, const float* k_new,
  * them straight from the kernel (no copy; the stores overlap the streaming),
  * else they are copied back on `stream` -- with g, the whole gathered buffer
  * is copied.  Synchronising `stream` covers the results either way. */
-/* Inputs of at most this many bytes per call go up as one packed copy on the
- * launch stream: for a few KB the side stream's events and three copies cost
- * more host time than the kernel takes. */
+/* Page-locked inputs of at most this many bytes per call are staged by one
+ * small kernel on the launch stream instead of three copies on the plan's
+ * copy stream ordered by events: for a few KB those CUDA calls cost more host
+ * time than the decode kernel takes. */
 #define TGKV_SMALL_UPLOAD (256u << 10)
 
 static int batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_host,
@@ -607,40 +614,37 @@ static int batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_h
     const uint64_t qb = (uint64_t)b->n * b->n_heads * b->head_dim * 4;
     const uint64_t kb = (uint64_t)b->n * b->kv_dim * 4;
     const uint64_t need = 2 * qb + 2 * kb + 64;
-    if (!g && qb + 2 * kb <= TGKV_SMALL_UPLOAD) {
-        /* q|k|v packed in pageable host memory, one copy on `stream` (the
-         * driver stages a pageable source before the call returns, so the
-         * pack is free again at once), the kernel right behind it on the same
-         * stream: two CUDA calls per decode call */
-        if (!b->pack && !(b->pack = malloc((size_t)(qb + 2 * kb)))) {
-            set_err("out of host memory");
-            return 0;
+    if (!g && qb + 2 * kb <= TGKV_SMALL_UPLOAD && !(qb % 16) && !(kb % 16)) {
+        void* dq = tg_cuda_kv_host_device_ptr(q_host);
+        void* dk = tg_cuda_kv_host_device_ptr(k_host);
+        void* dv = tg_cuda_kv_host_device_ptr(v_host);
+        if (dq && dk && dv && !(((uintptr_t)dq | (uintptr_t)dk | (uintptr_t)dv) & 15)) {
+            if (b->small_bytes < need) {
+                for (int i = 0; i < 2; i++) {
+                    if (b->small_io[i]) b->be->free(b->small_io[i]);   /* waits for readers */
+                    b->small_io[i] = (float*)b->be->alloc((size_t)need);
+                }
+                b->small_bytes = b->small_io[0] && b->small_io[1] ? need : 0;
+                if (!b->small_bytes) { set_err("batch: staging allocation failed"); return 0; }
+            }
+            float* q = b->small_io[b->small_slot];
+            float* k = (float*)((char*)q + qb);
+            float* v = (float*)((char*)k + kb);
+            float* o = (float*)((char*)v + kb);
+            b->small_slot ^= 1u;
+            if (!tg_cuda_kv_stage_host(q, dq, qb, dk, kb, dv, kb, stream)) {
+                set_err("%s", tg_cuda_kv_last_error());
+                return 0;
+            }
+            float* direct = (float*)tg_cuda_kv_host_device_ptr(out_host);
+            if (!batch_decode(b, q, k, v, direct ? direct : o, NULL, stream)) return 0;
+            b->last_launches++;
+            if (!direct && !tg_cuda_kv_d2h(out_host, o, qb, stream)) {
+                set_err("%s", tg_cuda_kv_last_error());
+                return 0;
+            }
+            return 1;
         }
-        if (need > b->io_bytes[0]) {
-            if (b->io[0]) b->be->free(b->io[0]);      /* cudaFree waits for its readers */
-            b->io[0] = (float*)b->be->alloc((size_t)need);
-            b->io_bytes[0] = b->io[0] ? need : 0;
-            if (!b->io[0]) { set_err("batch: staging allocation failed"); return 0; }
-        }
-        unsigned char* pk = (unsigned char*)b->pack;
-        memcpy(pk, q_host, (size_t)qb);
-        memcpy(pk + qb, k_host, (size_t)kb);
-        memcpy(pk + qb + kb, v_host, (size_t)kb);
-        float* q = b->io[0];
-        float* k = (float*)((char*)q + qb);
-        float* v = (float*)((char*)k + kb);
-        float* o = (float*)((char*)v + kb);
-        if (!tg_cuda_kv_h2d_async(q, pk, qb + 2 * kb, stream)) {
-            set_err("%s", tg_cuda_kv_last_error());
-            return 0;
-        }
-        float* direct = (float*)tg_cuda_kv_host_device_ptr(out_host);
-        if (!batch_decode(b, q, k, v, direct ? direct : o, NULL, stream)) return 0;
-        if (!direct && !tg_cuda_kv_d2h(out_host, o, qb, stream)) {
-            set_err("%s", tg_cuda_kv_last_error());
-            return 0;
-        }
-        return 1;
     }
     if (!b->copy_stream) {
         b->copy_stream = tg_cuda_kv_stream_create();
