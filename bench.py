@@ -658,8 +658,9 @@ def turn_script(seed, n_turns, lmin, lmax, vocab=32000):
 
 def run_cfg3(args):
     """One step = one chat turn over all layers: truncate every layer's cache
-    to the turn's LCP, append the suffix's K/V, attend the suffix queries
-    causally.  tokens/s counts suffix tokens through all layers."""
+    to the turn's LCP, append the suffix's K/V and attend the suffix queries
+    causally (tg_kv_append_attention).  tokens/s counts suffix tokens through
+    all layers."""
     import torch
     import tgkv
     lib = tgkv.load()
@@ -684,18 +685,23 @@ def run_cfg3(args):
     v = [torch.randn(nmax, kvd, device="cuda", generator=gen) for _ in range(layers)]
     out = [torch.empty(nmax, nh, hd, device="cuda") for _ in range(layers)]
 
+    launches = [0]
+
     def turn(lcp, n):
+        # truncate to the LCP, then the suffix's append + causal attention in
+        # one call (one launch of the tensor-core suffix kernel where it applies)
         for l in range(layers):
             c = caches[l]
             tgkv.check(lib.tg_kv_truncate(c, min(lcp, lib.tg_kv_len(c))), lib, "truncate")
-            tgkv.check(lib.tg_kv_append_dev(c, k[l].data_ptr(), v[l].data_ptr(), n, sh), lib,
-                       "append")
-            tgkv.check(lib.tg_kv_attention(c, q[l].data_ptr(), out[l].data_ptr(), nh, n, sh), lib,
-                       "attention")
+            tgkv.check(lib.tg_kv_append_attention(c, k[l].data_ptr(), v[l].data_ptr(),
+                                                  q[l].data_ptr(), out[l].data_ptr(), nh, n, sh),
+                       lib, "append + attention")
+            launches[0] += lib.tg_cuda_kv_attn_last_launches()
 
     for lcp, n in turns[:args.warmup]:
         turn(lcp, n)
     torch.cuda.synchronize()
+    launches[0] = 0
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
@@ -736,6 +742,7 @@ def run_cfg3(args):
             "config": {"workload": "cfg3", "desc": wl["desc"], "turns": timed,
                        "attention_kernel": kernel},
             "attention_tflops": flops / (ms / 1000.0) / 1e12,
+            "gpu_launches": launches[0],
             "append": {"ms_per_turn": a_ms / len(timed),
                        "write_gbs": app_write / (a_ms / 1000.0) / 1e9,
                        "read_write_gbs": (app_write + app_read) / (a_ms / 1000.0) / 1e9,

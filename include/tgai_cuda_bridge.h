@@ -159,6 +159,9 @@ uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c);
 /* (item, KV head, head subset) segments of a split-sequence call: each is
  * finished once, so a gather receives this many arrivals per rank. */
 uint64_t tg_cuda_kv_attn_segments(const TGCudaAttnCall* c);
+/* 1 if the call (with k_new/v_new: a suffix's new rows) runs as one launch
+ * of the tensor-core suffix kernel with the append fused in. */
+int tg_cuda_kv_attn_fuses_suffix(const TGCudaAttnCall* c);
 /* Launches made by the last tg_cuda_kv_attention on this thread. */
 uint32_t tg_cuda_kv_attn_last_launches(void);
 /* Kernel family of this thread's last tg_cuda_kv_attention call:

@@ -578,7 +578,11 @@ static int use_prefill(const TGCudaAttnCall* c) {
     if (!c || !c->n_kv_heads || !c->n_heads || c->n_heads % c->n_kv_heads || !c->n_pos ||
         !c->n_items || c->n_pos[0] == 0)
         return 0;
-    if (c->dtype != 1 || c->head_dim != 128 || c->table_dev || !c->cache.tmap_sw || c->k_new)
+    if (c->dtype != 1 || c->head_dim != 128 || c->table_dev || !c->cache.tmap_sw) return 0;
+    /* new rows (the fused append): item i's row lands at position n_pos[i] - 1,
+     * consecutive like the items; 16-byte rows for the kernel's loads */
+    if (c->k_new && (!c->v_new || !c->cache.base ||
+                     (((uintptr_t)c->k_new | (uintptr_t)c->v_new) & 15u)))
         return 0;
     const uint32_t g = c->n_heads / c->n_kv_heads;
     if (!(g == 1 || g == 2 || g == 4 || g == 8)) return 0;
@@ -608,6 +612,8 @@ static uint32_t prefill_split(const TGCudaAttnCall* c, uint32_t pos0) {
     }
     return 1;
 }
+
+int tg_cuda_kv_attn_fuses_suffix(const TGCudaAttnCall* c) { return use_prefill(c); }
 
 /* Calls that go to the tensor-core kernel need no split scratch: one token
  * byte and one counter keep the caller's sizing logic uniform. */
@@ -687,6 +693,11 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
     }
     if (prefill) {
         TGKvPrefillParams pp;
+        memset(&pp, 0, sizeof(pp));
+        pp.k_new = c->k_new;
+        pp.v_new = c->v_new;
+        pp.kvc = (uint16_t*)(uintptr_t)c->cache.base;
+        pp.max_seq = c->cache.max_seq;
         pp.tmap_sw = c->cache.tmap_sw;
         pp.q = c->q;
         pp.out = c->out;

@@ -128,6 +128,15 @@ typedef struct {
     uint32_t pos0;
     float    qscale;             /* softmax scale * log2(e) */
     uint32_t n_split;
+    /* The turn's append fused in: NULL, or the n_q new rows [n_q][kv_dim]
+     * fp32 of K and V, stored (bf16, round to nearest even) at positions
+     * pos0 .. pos0 + n_q - 1 of kvc before they are read.  Each CTA stores
+     * the new rows of its own KV head and tile range; CTAs of different row
+     * blocks store the same bytes for the rows they share. */
+    const float* k_new;
+    const float* v_new;
+    uint16_t*    kvc;            /* the cache buffer [2][max_seq][kv_dim], bf16 */
+    uint32_t     max_seq;
 } TGKvPrefillParams;
 
 /* Launchers (tgkv_kernels.cu, tgkv_prefill.cu).  Return 0 on success, else a

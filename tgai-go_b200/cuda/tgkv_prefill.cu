@@ -267,6 +267,34 @@ prefill_kernel(const __grid_constant__ TGKvPrefillParams p) {
     // previous kernel on the stream; nothing below reads global memory
     // before that kernel has completed.
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (p.k_new && nt > 0) {
+        // The fused append: this CTA's new K/V rows -- KV head kvh, positions
+        // in [pos0, pmax] within its tiles -- go into the cache (bf16, the
+        // append kernel's rounding) before its TMA loads read them.
+        const uint32_t lo = max(p.pos0, (uint32_t)j0 * kPos);
+        const uint32_t hi = min(pmax + 1, (uint32_t)(j0 + nt) * kPos);
+        if (lo < hi) {
+            const uint32_t kv_dim = p.n_kv_heads * kHD;
+            const uint64_t vofs = (uint64_t)p.max_seq * kv_dim;
+#pragma unroll 1
+            for (uint32_t i = tid; i < (hi - lo) * 32; i += kThreads) {
+                const uint32_t row = lo + (i >> 5), part = i & 31, e = (part & 15) * 8;
+                const float* src = (part < 16 ? p.k_new : p.v_new) +
+                                   (uint64_t)(row - p.pos0) * kv_dim + kvh * kHD + e;
+                const float4 a = *reinterpret_cast<const float4*>(src);
+                const float4 b = *reinterpret_cast<const float4*>(src + 4);
+                uint4 w;
+                w.x = pack_bf16x2(a.x, a.y);
+                w.y = pack_bf16x2(a.z, a.w);
+                w.z = pack_bf16x2(b.x, b.y);
+                w.w = pack_bf16x2(b.z, b.w);
+                *reinterpret_cast<uint4*>(p.kvc + (part < 16 ? 0 : vofs) +
+                                          (uint64_t)row * kv_dim + kvh * kHD + e) = w;
+            }
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
+        __syncthreads();
+    }
     // Cluster barrier, first phase: a CTA arrives once its staging area is
     // free (q moved into TMEM) and waits before copying partials to peers.
     if (warp >= kSoftmaxWarps) cluster_arrive();

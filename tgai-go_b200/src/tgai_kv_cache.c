@@ -319,6 +319,59 @@ int tg_kv_attention(TGKvCache* c, const float* q_dev, float* out_dev, uint32_t n
     return 1;
 }
 
+int tg_kv_append_attention(TGKvCache* c, const float* k_dev, const float* v_dev,
+                           const float* q_dev, float* out_dev, uint32_t n_heads, uint32_t n,
+                           void* stream) {
+    if (!c || !k_dev || !v_dev || !q_dev || !out_dev) { set_err("null argument"); return 0; }
+    if (n == 0) { set_err("n must be at least 1"); return 0; }
+    if ((uint64_t)c->len + n > c->max_seq) { set_err("capacity exceeded"); return 0; }
+    if (n_heads == 0 || n_heads % c->n_kv_heads) {
+        set_err("n_heads %u is not a multiple of n_kv_heads %u", n_heads, c->n_kv_heads);
+        return 0;
+    }
+    if (n > c->npos_cap) {
+        uint32_t* np = (uint32_t*)realloc(c->npos, (size_t)n * sizeof(uint32_t));
+        if (!np) { set_err("realloc failed"); return 0; }
+        c->npos = np;
+        c->npos_cap = n;
+    }
+    for (uint32_t t = 0; t < n; t++) c->npos[t] = c->len + t + 1;
+    TGCudaAttnCall call;
+    memset(&call, 0, sizeof(call));
+    call.dtype = c->dtype;
+    call.n_heads = n_heads;
+    call.n_kv_heads = c->n_kv_heads;
+    call.head_dim = c->head_dim;
+    call.cache.base = (uint64_t)(uintptr_t)c->dev;
+    call.cache.max_seq = c->max_seq;
+    call.cache.tmap = (uint64_t)(uintptr_t)c->tmap;
+    call.cache.tmap_sw = (uint64_t)(uintptr_t)c->tmap_sw;
+    call.q = q_dev;
+    call.out = out_dev;
+    call.k_new = k_dev;
+    call.v_new = v_dev;
+    call.n_pos = c->npos;
+    call.n_items = n;
+    call.scale = score_scale(c);
+    if (tg_be_current() == &tg_backend_cuda && tg_cuda_kv_attn_fuses_suffix(&call)) {
+        /* one launch: the suffix kernel stores the rows, then attends them */
+        if (!ensure_attn_scratch(c->be, &call, &c->scratch, &c->scratch_bytes, &c->counters,
+                                 &c->counter_slots))
+            return 0;
+        call.scratch = c->scratch;
+        call.counters = c->counters;
+        if (!tg_cuda_kv_attention(&call, stream)) {
+            set_err("%s", tg_cuda_kv_last_error());
+            return 0;
+        }
+        c->len += n;
+        return 1;
+    }
+    /* any other geometry: the append launch, then the attention */
+    return tg_kv_append_dev(c, k_dev, v_dev, n, stream) &&
+           tg_kv_attention(c, q_dev, out_dev, n_heads, n, stream);
+}
+
 /* ---- batched decode ----------------------------------------------------- */
 struct TGKvBatch {
     uint32_t n, n_heads, n_kv_heads, head_dim, kv_dim;

@@ -91,6 +91,8 @@ PROTOS = {
     "tg_kv_bytes": (u64, [vp]),
     "tg_kv_download": (i32, [vp, vp]),
     "tg_kv_attention_static": (i32, [vp, i32, u32, u32, u32, u32, vp, vp, u32, u32, vp]),
+    "tg_kv_append_attention": (i32, [vp, vp, vp, vp, vp, u32, u32, vp]),
+    "tg_cuda_kv_attn_fuses_suffix": (i32, [vp]),
     "tg_kv_attention_static_error": (i32, [vp]),
     "tg_kv_attention_static_inject_stall": (None, [i32]),
     "tg_kv_rope_tables": (i32, [fp, u32, u32, u32, u32, u32, PF, PF, PF]),
