@@ -267,33 +267,52 @@ prefill_kernel(const __grid_constant__ TGKvPrefillParams p) {
     // previous kernel on the stream; nothing below reads global memory
     // before that kernel has completed.
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (p.k_new && nt > 0) {
-        // The fused append: this CTA's new K/V rows -- KV head kvh, positions
-        // in [pos0, pmax] within its tiles -- go into the cache (bf16, the
-        // append kernel's rounding) before its TMA loads read them.
-        const uint32_t lo = max(p.pos0, (uint32_t)j0 * kPos);
-        const uint32_t hi = min(pmax + 1, (uint32_t)(j0 + nt) * kPos);
-        if (lo < hi) {
-            const uint32_t kv_dim = p.n_kv_heads * kHD;
-            const uint64_t vofs = (uint64_t)p.max_seq * kv_dim;
+    if (p.k_new) {
+        // The fused append: the row block's new K/V rows -- KV head kvh,
+        // positions [pos0, pmax] -- go into the cache (bf16, the append
+        // kernel's rounding), shared out over the cluster's CTAs, every
+        // thread's loads in flight before its stores.  A cluster barrier then
+        // orders them before any CTA's TMA loads.  Other row blocks store the
+        // same bytes for the rows they share.
+        const uint32_t kv_dim = p.n_kv_heads * kHD;
+        const uint64_t vofs = (uint64_t)p.max_seq * kv_dim;
+        const uint32_t total = (pmax + 1 - p.pos0) * 32;      // 16-byte chunks of K and V rows
+        const uint32_t per = (total + ns - 1) / ns;
+        const uint32_t c0 = z * per, c1 = min(total, c0 + per);
+        constexpr int kU = 4;
 #pragma unroll 1
-            for (uint32_t i = tid; i < (hi - lo) * 32; i += kThreads) {
-                const uint32_t row = lo + (i >> 5), part = i & 31, e = (part & 15) * 8;
-                const float* src = (part < 16 ? p.k_new : p.v_new) +
-                                   (uint64_t)(row - p.pos0) * kv_dim + kvh * kHD + e;
-                const float4 a = *reinterpret_cast<const float4*>(src);
-                const float4 b = *reinterpret_cast<const float4*>(src + 4);
-                uint4 w;
-                w.x = pack_bf16x2(a.x, a.y);
-                w.y = pack_bf16x2(a.z, a.w);
-                w.z = pack_bf16x2(b.x, b.y);
-                w.w = pack_bf16x2(b.z, b.w);
-                *reinterpret_cast<uint4*>(p.kvc + (part < 16 ? 0 : vofs) +
-                                          (uint64_t)row * kv_dim + kvh * kHD + e) = w;
+        for (uint32_t i0 = c0 + tid; i0 < c1; i0 += kThreads * kU) {
+            float4 a[kU], b[kU];
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const uint32_t i = i0 + u * kThreads;
+                if (i < c1) {
+                    const uint32_t row = p.pos0 + (i >> 5), part = i & 31, e = (part & 15) * 8;
+                    const float* src = (part < 16 ? p.k_new : p.v_new) +
+                                       (uint64_t)(row - p.pos0) * kv_dim + kvh * kHD + e;
+                    a[u] = *reinterpret_cast<const float4*>(src);
+                    b[u] = *reinterpret_cast<const float4*>(src + 4);
+                }
             }
-            asm volatile("fence.proxy.async.global;" ::: "memory");
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const uint32_t i = i0 + u * kThreads;
+                if (i < c1) {
+                    const uint32_t row = p.pos0 + (i >> 5), part = i & 31, e = (part & 15) * 8;
+                    uint4 w;
+                    w.x = pack_bf16x2(a[u].x, a[u].y);
+                    w.y = pack_bf16x2(a[u].z, a[u].w);
+                    w.z = pack_bf16x2(b[u].x, b[u].y);
+                    w.w = pack_bf16x2(b[u].z, b[u].w);
+                    *reinterpret_cast<uint4*>(p.kvc + (part < 16 ? 0 : vofs) +
+                                              (uint64_t)row * kv_dim + kvh * kHD + e) = w;
+                }
+            }
         }
-        __syncthreads();
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __syncwarp();                 // the .aligned cluster barrier wants whole warps
+        cluster_sync();
+        asm volatile("fence.proxy.async.global;" ::: "memory");
     }
     // Cluster barrier, first phase: a CTA arrives once its staging area is
     // free (q moved into TMEM) and waits before copying partials to peers.
