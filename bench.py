@@ -686,6 +686,7 @@ def run_cfg3(args):
     out = [torch.empty(nmax, nh, hd, device="cuda") for _ in range(layers)]
 
     launches = [0]
+    fused = os.environ.get("TGKV_FUSE_SUFFIX", "") == "1"
 
     def turn(lcp, n):
         # truncate to the LCP, then the suffix's append + causal attention in
@@ -696,7 +697,8 @@ def run_cfg3(args):
             tgkv.check(lib.tg_kv_append_attention(c, k[l].data_ptr(), v[l].data_ptr(),
                                                   q[l].data_ptr(), out[l].data_ptr(), nh, n, sh),
                        lib, "append + attention")
-            launches[0] += lib.tg_cuda_kv_attn_last_launches()
+            # the attention's launches, and the append kernel's unless fused in
+            launches[0] += lib.tg_cuda_kv_attn_last_launches() + (0 if fused else 1)
 
     for lcp, n in turns[:args.warmup]:
         turn(lcp, n)

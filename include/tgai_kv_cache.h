@@ -126,11 +126,12 @@ int tg_kv_rope_tables(float theta, uint32_t head_dim, uint32_t pos0, uint32_t n_
 /* A turn's suffix in one call: append n rows of K and V (fp32 device
  * [n][kv_dim], as tg_kv_append_dev) at positions len .. len + n - 1, then
  * the causal attention of their n queries (as tg_kv_attention with n_q = n);
- * len grows by n.  On a bf16 head_dim-128 cache with at least 128 (row,
- * head) pairs and 16-byte aligned pointers this is ONE launch of the
- * tensor-core suffix kernel, which stores the new rows itself before it
- * reads them; otherwise the two launches.  The engine writes a turn's K/V
- * and then attends it (src/tgai_engine.c:3923-4011): the pair, fused.
+ * len grows by n.  The engine writes a turn's K/V and then attends it
+ * (src/tgai_engine.c:3923-4011): the pair in one call, the append kernel then
+ * the attention.  With TGKV_FUSE_SUFFIX=1, on a bf16 head_dim-128 cache with
+ * at least 128 (row, head) pairs and 16-byte aligned pointers, it is ONE
+ * launch of the tensor-core suffix kernel, which stores the new rows itself
+ * before it reads them (slower on the measured turn shapes, hence opt-in).
  * Returns 0 on capacity or argument errors (nothing launched). */
 int tg_kv_append_attention(TGKvCache* c, const float* k_dev, const float* v_dev,
                            const float* q_dev, float* out_dev, uint32_t n_heads, uint32_t n,

@@ -1,10 +1,11 @@
 """A chat turn's suffix in one call: tg_kv_append_attention.
 
 The engine writes a turn's K/V rows and then attends the turn's queries over
-the cache (src/tgai_engine.c:3923-4011).  On a bf16 head_dim-128 cache the
-library does both in one launch of the tensor-core suffix kernel, whose CTAs
-store the new rows they are about to read (each CTA its KV head and tile
-range; CTAs of different row blocks store the same bytes for shared rows).
+the cache (src/tgai_engine.c:3923-4011).  tg_kv_append_attention does both in
+one call: by default the append kernel then the attention; with
+TGKV_FUSE_SUFFIX=1, on a bf16 head_dim-128 cache, one launch of the
+tensor-core suffix kernel whose clusters store the new rows they are about to
+read (CTAs of different row blocks store the same bytes for shared rows).
 These tests run configs[2]'s turn script -- LCP truncate, /undo, /clear,
 64-512-token suffixes -- through the fused call and check:
   * the cache bytes equal, bit for bit, a cache built by the append kernel
@@ -12,7 +13,7 @@ These tests run configs[2]'s turn script -- LCP truncate, /undo, /clear,
   * the outputs meet the engine-order oracle on the cache as stored;
   * the fused route is one launch of the suffix kernel; geometries it does
     not take (fp32 caches, too few rows) run the two launches with the same
-    results.
+    results.  Both routes are run.
 """
 import numpy as np
 import pytest
@@ -42,9 +43,11 @@ def _turns(seed, n_turns):
     return out
 
 
+@pytest.mark.parametrize("fuse", ["1", "0"])     # in-kernel append, or the append kernel first
 @pytest.mark.parametrize("nh", [16, 32])          # groups of 4 and 8 query heads
-def test_fused_turns_match_separate_append_and_oracle(cuda, devbuf, nh):
+def test_fused_turns_match_separate_append_and_oracle(cuda, devbuf, nh, fuse, monkeypatch):
     lib = cuda
+    monkeypatch.setenv("TGKV_FUSE_SUFFIX", fuse)
     nkv, hd, ms, layer = 4, 128, 4096, 1
     kvd = nkv * hd
     fused = make_cache(lib, devbuf, ms, nkv, hd, 1, [], [])
@@ -63,6 +66,7 @@ def test_fused_turns_match_separate_append_and_oracle(cuda, devbuf, nh):
         assert lib.tg_cuda_kv_attn_last_kernel() == 2          # the tensor-core suffix kernel
         assert lib.tg_cuda_kv_attn_last_launches() == 1
         assert lib.tg_kv_len(fused) == len(hist)
+        monkeypatch.setenv("TGKV_FUSE_SUFFIX", "0")            # the reference side: two launches
         # ... and the append kernel + the attention on the other
         tgkv.check(lib.tg_kv_truncate(plain, lcp), lib)
         tgkv.check(lib.tg_kv_append_dev(plain, kd.ptr, vd.ptr, n, None), lib)
@@ -80,6 +84,7 @@ def test_fused_turns_match_separate_append_and_oracle(cuda, devbuf, nh):
                                  len(hist), ms)
         assert rel_head_err(got, eng) < TC_TOL, turn
         assert rel_head_err(got, op.get(np.float32, q.shape)) < TC_TOL, turn
+        monkeypatch.setenv("TGKV_FUSE_SUFFIX", fuse)
     assert lib.tg_cuda_kv_device_error() == 0
     lib.tg_kv_destroy(fused)
     lib.tg_kv_destroy(plain)

@@ -353,7 +353,14 @@ int tg_kv_append_attention(TGKvCache* c, const float* k_dev, const float* v_dev,
     call.n_pos = c->npos;
     call.n_items = n;
     call.scale = score_scale(c);
-    if (tg_be_current() == &tg_backend_cuda && tg_cuda_kv_attn_fuses_suffix(&call)) {
+    /* TGKV_FUSE_SUFFIX=1: one launch, the suffix kernel storing the rows
+     * itself before it reads them.  Off by default: on configs[2]'s turns it
+     * measured 0.506 ms per turn against 0.448 with the append kernel first
+     * (each row block's clusters store the rows they read, so the stores are
+     * repeated per row block and sit on every cluster's critical path). */
+    const char* fz = getenv("TGKV_FUSE_SUFFIX");
+    if (fz && fz[0] == '1' && tg_be_current() == &tg_backend_cuda &&
+        tg_cuda_kv_attn_fuses_suffix(&call)) {
         /* one launch: the suffix kernel stores the rows, then attends them */
         if (!ensure_attn_scratch(c->be, &call, &c->scratch, &c->scratch_bytes, &c->counters,
                                  &c->counter_slots))
@@ -367,7 +374,7 @@ int tg_kv_append_attention(TGKvCache* c, const float* k_dev, const float* v_dev,
         c->len += n;
         return 1;
     }
-    /* any other geometry: the append launch, then the attention */
+    /* the append launch, then the attention */
     return tg_kv_append_dev(c, k_dev, v_dev, n, stream) &&
            tg_kv_attention(c, q_dev, out_dev, n_heads, n, stream);
 }
