@@ -63,9 +63,13 @@ def test_forward_matches_engine(cuda, golden, name, monkeypatch):
     assert cuda.tg_cuda_kv_device_error() == 0
 
 
-def test_long_prefill_and_decode_against_oracle(cuda, decode_path):
+@pytest.mark.parametrize("experts", ["tensor-core GEMM", "CUDA-core kernels"])
+def test_long_prefill_and_decode_against_oracle(cuda, decode_path, experts, monkeypatch):
     """A 200-token prefill (longer than the workspaces' first size) and decode
-    steps near the capacity, checked against the float64 oracle."""
+    steps near the capacity, checked against the float64 oracle.  The
+    prefill's experts run as grouped tensor-core GEMMs (the default) or on the
+    CUDA-core expert kernels (TGKV_MOE_GEMM=0, read at model creation)."""
+    monkeypatch.setenv("TGKV_MOE_GEMM", "0" if experts == "CUDA-core kernels" else "1")
     cfg = dict(FM.CONFIGS["moe"])
     w = FM.weights(cfg, 77)
     f = tgkv.Forward(cuda, fwd_config(cfg), w)

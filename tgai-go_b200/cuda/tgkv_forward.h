@@ -139,12 +139,39 @@ typedef struct {
     uint32_t M, N, K;
     int accumulate;
     int32_t* err;                   /* device error word: set when a bounded wait runs out */
+    /* Grouped (one GEMM per MoE expert in one launch): group g multiplies
+     * A rows [group_off[g], + group_count[g]) (device arrays, read in the
+     * kernel) by W rows [g * N, (g + 1) * N); grid z = groups, y covers
+     * max_rows rows.  out_rows (or NULL): the output row of packed A row r. */
+    const uint32_t* group_count;
+    const uint32_t* group_off;
+    const uint32_t* out_rows;
+    uint32_t groups, max_rows;
 } TGGemmParams;
 /* Fill p (host only; 0 on unsupported shapes or a failed tensor-map encode). */
 int tgkv_gemm_encode(TGGemmParams* p, const float* a_big, const float* a_small, uint64_t lda,
                      const float* w_big, const float* w_small, uint64_t ldw, float* out,
                      uint64_t ldo, uint32_t M, uint32_t N, uint32_t K, int accumulate,
                      int32_t* err);
+/* The grouped form: A = a_big/a_small [a_rows][K] (packed rows of every
+ * group), W = w_big/w_small [groups * N][K]; M is each group's count from
+ * the device. */
+int tgkv_gemm_encode_grouped(TGGemmParams* p, const float* a_big, const float* a_small,
+                             uint32_t a_rows, const float* w_big, const float* w_small,
+                             uint32_t groups, uint32_t N, uint32_t K, float* out, uint64_t ldo,
+                             const uint32_t* group_count, const uint32_t* group_off,
+                             const uint32_t* out_rows, uint32_t max_rows, int32_t* err);
+/* The MoE prefill's operands.  pack: from the router's counts[ne] and
+ * lists[e * seq * na + i] (pairs t * na + k), the pairs of expert e become
+ * rows off[e] .. off[e] + counts[e] - 1 (off = the prefix sums, written to
+ * offs[ne]) of A (x's row t, split into tf32 part and remainder), and
+ * rows[r] = the pair of packed row r.  silu_split: h = silu(ab[r][j]) *
+ * ab[r][dff + j] for the first sum(counts) rows, split likewise. */
+int tgkv_moe_pack_split(const uint32_t* counts, const uint32_t* lists, const float* x, uint32_t d,
+                        uint32_t seq, uint32_t ne, uint32_t na, float* a_big, float* a_small,
+                        uint32_t* offs, uint32_t* rows, void* stream);
+int tgkv_moe_silu_split(const float* ab, const uint32_t* counts, uint32_t ne, uint32_t max_rows,
+                        uint32_t dff, float* h_big, float* h_small, void* stream);
 /* Output tile width the launch uses for an M x N product (64 or 128). */
 uint32_t tgkv_gemm_bn(uint32_t M, uint32_t N);
 int tgkv_gemm_launch(const TGGemmParams* p, void* stream);

@@ -120,8 +120,18 @@ __global__ void __launch_bounds__(128, 1) gemm_tf32x3_kernel(const __grid_consta
     const uint32_t tmem = *tmem_slot;
     // the inputs come from the kernels before this one on the stream
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // this CTA's rows: the whole A (plain), or its group's packed rows
+    uint32_t M = p.M, a_row0 = 0, w_row0 = 0;
+    if (p.group_count) {
+        M = p.group_count[blockIdx.z];
+        a_row0 = p.group_off[blockIdx.z];
+        w_row0 = blockIdx.z * p.N;
+    }
+    const bool active = m0 < M;               // CTA-uniform
 
-    if (warp == 0 && lane == 0) {
+    if (!active) {
+        // a tile past its group's rows: nothing to load, multiply or store
+    } else if (warp == 0 && lane == 0) {
         // ---------------- producer
         int issued = 0;
         for (int kb = 0; kb < total; ++kb) {
@@ -136,8 +146,9 @@ __global__ void __launch_bounds__(128, 1) gemm_tf32x3_kernel(const __grid_consta
             const int kx = (kb - seg * nkb) * kBK;
             unsigned char* st = smem + s * C::Stage;
             mbar_arrive_expect_tx(&full[s], (uint32_t)C::Stage);
-            tma_load_2d(st, seg == 0 ? &p.a_small : &p.a_big, kx, (int)m0, &full[s]);
-            tma_load_2d(st + kABytes, seg == 1 ? &p.w_small : &p.w_big, kx, (int)n0, &full[s]);
+            tma_load_2d(st, seg == 0 ? &p.a_small : &p.a_big, kx, (int)(a_row0 + m0), &full[s]);
+            tma_load_2d(st + kABytes, seg == 1 ? &p.w_small : &p.w_big, kx, (int)(w_row0 + n0),
+                        &full[s]);
             ++issued;
         }
         // the last stages' copies land before this thread may leave
@@ -170,20 +181,23 @@ __global__ void __launch_bounds__(128, 1) gemm_tf32x3_kernel(const __grid_consta
     __syncwarp();
 
     // ---------------- epilogue: warp w holds rows m0 + 32w .. + 31
-    const bool ok = mbar_wait(done, 0);
+    const bool ok = !active || mbar_wait(done, 0);
     if (!ok && lane == 0) atomicExch(p.err, kErrDone);
     tc_fence_after();
     // let the next kernel on the stream start its prologue
     if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const bool store = ok && !*reinterpret_cast<volatile int*>(abort_flag);
+    const bool store = active && ok && !*reinterpret_cast<volatile int*>(abort_flag);
     const uint32_t row = m0 + 32 * warp + lane;
-    float* orow = p.out + (uint64_t)row * p.ldo;
+    const uint32_t orow_i = !p.group_count ? row
+                            : p.out_rows ? (row < M ? p.out_rows[a_row0 + row] : 0u)
+                                         : a_row0 + row;
+    float* orow = p.out + (uint64_t)orow_i * p.ldo;
     const bool vec = (p.ldo % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0);
     const int n_acc = total < C::NAcc ? total : C::NAcc;   // accumulators written
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
         const uint32_t col0 = n0 + 32 * c;
-        if (col0 >= p.N) break;                        // warp-uniform
+        if (col0 >= p.N || !active) break;             // warp-uniform
         uint32_t r[32];
         const uint32_t t = tmem + ((uint32_t)(32 * warp) << 16) + 32 * c;
         tmem_ld32(t, r);
@@ -197,7 +211,7 @@ __global__ void __launch_bounds__(128, 1) gemm_tf32x3_kernel(const __grid_consta
             for (int j = 0; j < 32; ++j)
                 r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q[j]));
         }
-        if (!store || row >= p.M) continue;
+        if (!store || row >= M) continue;
         if (vec && col0 + 32 <= p.N) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
@@ -291,7 +305,9 @@ int launch(const TGGemmParams* p, void* stream) {
     }
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
-    cfg.gridDim = dim3((p->N + BN - 1) / BN, (p->M + kBM - 1) / kBM, 1);
+    cfg.gridDim = p->group_count
+                      ? dim3((p->N + BN - 1) / BN, (p->max_rows + kBM - 1) / kBM, p->groups)
+                      : dim3((p->N + BN - 1) / BN, (p->M + kBM - 1) / kBM, 1);
     cfg.blockDim = dim3(128, 1, 1);
     cfg.dynamicSmemBytes = C::Smem;
     cfg.stream = (cudaStream_t)stream;
@@ -333,9 +349,160 @@ extern "C" uint32_t tgkv_gemm_bn(uint32_t M, uint32_t N) {
     return tiles >= 74 ? 128u : 64u;
 }
 
+static uint32_t launch_bn(const TGGemmParams* p) {
+    return p->group_count ? tgkv_gemm_bn(p->max_rows * p->groups, p->N) : tgkv_gemm_bn(p->M, p->N);
+}
+
 extern "C" int tgkv_gemm_launch(const TGGemmParams* p, void* stream) {
-    return tgkv_gemm_bn(p->M, p->N) == 128 ? tgkv::gemm::launch<128>(p, stream)
-                                           : tgkv::gemm::launch<64>(p, stream);
+    return launch_bn(p) == 128 ? tgkv::gemm::launch<128>(p, stream)
+                               : tgkv::gemm::launch<64>(p, stream);
+}
+
+extern "C" int tgkv_gemm_encode_grouped(TGGemmParams* p, const float* a_big, const float* a_small,
+                                        uint32_t a_rows, const float* w_big, const float* w_small,
+                                        uint32_t groups, uint32_t N, uint32_t K, float* out,
+                                        uint64_t ldo, const uint32_t* group_count,
+                                        const uint32_t* group_off, const uint32_t* out_rows,
+                                        uint32_t max_rows, int32_t* err) {
+    using namespace tgkv::gemm;
+    memset(p, 0, sizeof(*p));
+    if (!a_rows || !groups || !N || !K || (K % 4) || ldo < N || !err || !group_count ||
+        !group_off || !max_rows || (uint64_t)groups * N > 0x7fffffffu)
+        return 0;
+    p->group_count = group_count;
+    p->group_off = group_off;
+    p->out_rows = out_rows;
+    p->groups = groups;
+    p->max_rows = max_rows;
+    p->N = N;
+    const uint32_t bn = launch_bn(p);
+    if (!encode(&p->a_big, a_big, K, a_rows, K, kBM) ||
+        !encode(&p->a_small, a_small, K, a_rows, K, kBM) ||
+        !encode(&p->w_big, w_big, K, groups * N, K, bn) ||
+        !encode(&p->w_small, w_small, K, groups * N, K, bn))
+        return 0;
+    p->out = out;
+    p->ldo = ldo;
+    p->M = max_rows;
+    p->K = K;
+    p->accumulate = 0;
+    p->err = err;
+    return 1;
+}
+
+namespace tgkv {
+namespace gemm {
+
+__device__ __forceinline__ void split1(float v, float& b, float& s) {
+    uint32_t u;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(u) : "f"(v));
+    b = __uint_as_float(u);
+    s = v - b;
+}
+
+// Packed row r: the expert e with off[e] <= r < off[e] + counts[e] (off the
+// prefix sums, each CTA computes them; at most 16 experts), slot i = r -
+// off[e], pair q = lists[e * seq * na + i], token q / na.  One CTA per 8
+// rows, a warp per row.
+__global__ void __launch_bounds__(256) moe_pack_kernel(const uint32_t* counts,
+                                                       const uint32_t* lists, const float* x,
+                                                       uint32_t d, uint32_t seq, uint32_t ne,
+                                                       uint32_t na, float* a_big, float* a_small,
+                                                       uint32_t* offs, uint32_t* rows) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    __shared__ uint32_t s_off[17];
+    if (threadIdx.x == 0) {
+        uint32_t o = 0;
+        for (uint32_t e = 0; e < ne; ++e) {
+            s_off[e] = o;
+            o += counts[e];
+        }
+        s_off[ne] = o;
+        if (blockIdx.x == 0)
+            for (uint32_t e = 0; e < ne; ++e) offs[e] = s_off[e];
+    }
+    __syncthreads();
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t r = blockIdx.x * 8 + warp;
+    if (r < s_off[ne]) {
+        uint32_t e = 0;
+        while (e + 1 < ne && s_off[e + 1] <= r) ++e;
+        const uint32_t q = lists[(uint64_t)e * seq * na + (r - s_off[e])];
+        if (lane == 0) rows[r] = q;
+        const float4* src = reinterpret_cast<const float4*>(x + (uint64_t)(q / na) * d);
+        float4* db = reinterpret_cast<float4*>(a_big + (uint64_t)r * d);
+        float4* ds = reinterpret_cast<float4*>(a_small + (uint64_t)r * d);
+        for (uint32_t i = lane; i < d / 4; i += 32) {
+            const float4 v = src[i];
+            float4 b, sm;
+            split1(v.x, b.x, sm.x);
+            split1(v.y, b.y, sm.y);
+            split1(v.z, b.z, sm.z);
+            split1(v.w, b.w, sm.w);
+            db[i] = b;
+            ds[i] = sm;
+        }
+    }
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(256) moe_silu_kernel(const float* ab, const uint32_t* counts,
+                                                       uint32_t ne, uint32_t dff, float* h_big,
+                                                       float* h_small) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    uint32_t n = 0;
+    for (uint32_t e = 0; e < ne; ++e) n += counts[e];
+    const uint64_t total = (uint64_t)n * dff;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total;
+         i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = i / dff, j = i % dff;
+        const float a = ab[r * 2 * dff + j], b = ab[r * 2 * dff + dff + j];
+        const float h = (a / (1.0f + expf(-a))) * b;        // the expert FFN's SiLU, no clamp
+        float hb, hs;
+        split1(h, hb, hs);
+        h_big[r * dff + j] = hb;
+        h_small[r * dff + j] = hs;
+    }
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+int launch_simple(const void* fn, dim3 grid, void** args, void* stream) {
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(256);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return (int)cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace gemm
+}  // namespace tgkv
+
+extern "C" int tgkv_moe_pack_split(const uint32_t* counts, const uint32_t* lists, const float* x,
+                                   uint32_t d, uint32_t seq, uint32_t ne, uint32_t na,
+                                   float* a_big, float* a_small, uint32_t* offs, uint32_t* rows,
+                                   void* stream) {
+    if (!ne || ne > 16 || d % 4 || !seq || !na) return (int)cudaErrorInvalidValue;
+    const uint32_t max_rows = seq * na;
+    void* args[] = {&counts, &lists, &x, &d, &seq, &ne, &na, &a_big, &a_small, &offs, &rows};
+    return tgkv::gemm::launch_simple((const void*)tgkv::gemm::moe_pack_kernel,
+                                     dim3((max_rows + 7) / 8), args, stream);
+}
+
+extern "C" int tgkv_moe_silu_split(const float* ab, const uint32_t* counts, uint32_t ne,
+                                   uint32_t max_rows, uint32_t dff, float* h_big, float* h_small,
+                                   void* stream) {
+    if (!ne || ne > 16 || !dff) return (int)cudaErrorInvalidValue;
+    uint64_t blocks = ((uint64_t)max_rows * dff + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    void* args[] = {&ab, &counts, &ne, &dff, &h_big, &h_small};
+    return tgkv::gemm::launch_simple((const void*)tgkv::gemm::moe_silu_kernel,
+                                     dim3((unsigned)blocks), args, stream);
 }
 
 extern "C" int tgkv_split_tf32(const float* x, uint64_t ldx, float* big, float* small,

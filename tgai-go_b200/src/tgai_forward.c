@@ -76,7 +76,7 @@ typedef struct {
     /* the prefill GEMMs' operands: each weight as its tf32-rounded part and
      * the exact remainder (tgkv_split_tf32), same shapes */
     float *wqkv_b, *wqkv_s, *wo_b, *wo_s, *router_b, *router_s;
-    float *w12_b, *w12_s, *w3_b, *w3_s;   /* dense FFN only */
+    float *w12_b, *w12_s, *w3_b, *w3_s;   /* the FFN's (a dense one, or every expert's) */
 } Layer;
 
 typedef struct Slot {
@@ -90,6 +90,7 @@ typedef struct Slot {
     uint32_t cap;            /* token rows the workspaces hold */
     float *x, *ln, *qkv, *q, *attn, *ab, *h, *router, *top_w, *y, *logits;
     float *abig, *asmall;    /* a prefill GEMM's input rows, split (tgkv_split_tf32) */
+    uint32_t *moe_off, *moe_rows;   /* MoE prefill: experts' first packed rows, row -> pair */
     int32_t *top_ids, *ids;
     uint32_t *counts, *lists;
     int32_t* h_ids;          /* page-locked */
@@ -314,6 +315,11 @@ static float* upload_cat(TGFwdModel* m, const float* const* parts, const uint64_
     return d;
 }
 
+static int moe_gemm_on(void) {
+    const char* e = getenv("TGKV_MOE_GEMM");
+    return !(e && e[0] == '0');
+}
+
 static int load_layer(TGFwdModel* m, uint32_t l, TGFwdWeightFn get, void* ctx) {
     const uint32_t d = m->c.d_model, dff = m->c.d_ff, ne = m->c.n_experts;
     Layer* L = &m->L[l];
@@ -385,6 +391,11 @@ static int load_layer(TGFwdModel* m, uint32_t l, TGFwdWeightFn get, void* ctx) {
         for (uint32_t e = 0; e < ne; e++) n12[e] = per;
         ok = (L->w3 = upload_cat(m, w3, n12, (int)ne)) != NULL;
     }
+    /* the experts' split form for the prefill's grouped GEMMs (twice the
+     * experts' bytes); TGKV_MOE_GEMM=0 keeps the CUDA-core expert kernels */
+    if (ok && moe_gemm_on())
+        ok = split_weight(m, L->w12, (uint64_t)ne * 2 * dff, d, &L->w12_b, &L->w12_s) &&
+             split_weight(m, L->w3, (uint64_t)ne * d, dff, &L->w3_b, &L->w3_s);
     free(w12);
     free(w3);
     free(n12);
@@ -518,8 +529,10 @@ static void slot_free_ws(Slot* s) {
     tg_cuda_kv_free(s->ids);
     tg_cuda_kv_free(s->counts);
     tg_cuda_kv_free(s->lists);
+    tg_cuda_kv_free(s->moe_off);
+    tg_cuda_kv_free(s->moe_rows);
     s->top_ids = s->ids = NULL;
-    s->counts = s->lists = NULL;
+    s->counts = s->lists = s->moe_off = s->moe_rows = NULL;
     tgkv_fwd_host_free(s->h_ids);
     s->h_ids = NULL;
     s->cap = 0;
@@ -570,8 +583,9 @@ static int slot_reserve(TGFwdModel* m, Slot* s, uint32_t need) {
     s->h_ids = (int32_t*)tgkv_fwd_host_alloc((uint64_t)cap * 4);
     uint64_t kmax = d > m->q_dim ? d : m->q_dim;
     if (dff > kmax) kmax = dff;
-    s->abig = (float*)tg_cuda_kv_malloc(cap * kmax * 4);
-    s->asmall = (float*)tg_cuda_kv_malloc(cap * kmax * 4);
+    /* split GEMM inputs: token rows, or the MoE's packed (token, expert) rows */
+    s->abig = (float*)tg_cuda_kv_malloc(pairs * kmax * 4);
+    s->asmall = (float*)tg_cuda_kv_malloc(pairs * kmax * 4);
     int ok = s->x && s->ln && s->qkv && s->q && s->attn && s->h && s->ids && s->h_ids &&
              s->abig && s->asmall;
     if (ne == 0) {
@@ -585,6 +599,12 @@ static int slot_reserve(TGFwdModel* m, Slot* s, uint32_t need) {
         s->counts = (uint32_t*)tg_cuda_kv_malloc(ne * 4);
         s->lists = (uint32_t*)tg_cuda_kv_malloc(ne * pairs * 4);
         ok = ok && s->router && s->top_w && s->top_ids && s->y && s->counts && s->lists;
+        if (m->L[0].w12_b) {              /* the grouped expert GEMMs' workspaces */
+            s->ab = (float*)tg_cuda_kv_malloc(pairs * 2 * dff * 4);
+            s->moe_off = (uint32_t*)tg_cuda_kv_malloc(16 * 4);
+            s->moe_rows = (uint32_t*)tg_cuda_kv_malloc(pairs * 4);
+            ok = ok && s->ab && s->moe_off && s->moe_rows;
+        }
     }
     if (!ok) {
         slot_free_ws(s);
@@ -848,10 +868,35 @@ static int run_layer(TGFwdModel* m, Slot* s, uint32_t l, uint32_t seq, uint32_t 
     }
     CHECK_LAUNCH(tgkv_fwd_route(s->router, L->qb, s->top_ids, s->top_w, s->counts, s->lists,
                                 seq, ne, na, st));
-    CHECK_LAUNCH(tgkv_fwd_expert_w12(L->w12, s->ln, s->h, s->counts, s->lists, seq, ne, na, d,
-                                     dff, st));
-    CHECK_LAUNCH(tgkv_fwd_expert_w3(L->w3, s->h, s->y, s->counts, s->lists, seq, ne, na, d, dff,
-                                    st));
+    if (L->w12_b) {
+        /* the experts on the tensor cores: the (token, expert) pairs packed by
+         * expert, one grouped GEMM for W1/W2, SiLU, one for W3 whose rows
+         * land at their pair's row of y */
+        const uint32_t pr = seq * na;
+        TGGemmParams gp;
+        CHECK_LAUNCH(tgkv_moe_pack_split(s->counts, s->lists, s->ln, d, seq, ne, na, s->abig,
+                                         s->asmall, s->moe_off, s->moe_rows, st));
+        if (!tgkv_gemm_encode_grouped(&gp, s->abig, s->asmall, pr, L->w12_b, L->w12_s, ne,
+                                      2 * dff, d, s->ab, 2 * dff, s->counts, s->moe_off, NULL,
+                                      seq, tgkv_bridge_err_word())) {
+            set_err("expert GEMM (W1/W2): tensor map encode failed");
+            return 0;
+        }
+        CHECK_LAUNCH(tgkv_gemm_launch(&gp, st));
+        CHECK_LAUNCH(tgkv_moe_silu_split(s->ab, s->counts, ne, pr, dff, s->abig, s->asmall, st));
+        if (!tgkv_gemm_encode_grouped(&gp, s->abig, s->asmall, pr, L->w3_b, L->w3_s, ne, d, dff,
+                                      s->y, d, s->counts, s->moe_off, s->moe_rows, seq,
+                                      tgkv_bridge_err_word())) {
+            set_err("expert GEMM (W3): tensor map encode failed");
+            return 0;
+        }
+        CHECK_LAUNCH(tgkv_gemm_launch(&gp, st));
+    } else {
+        CHECK_LAUNCH(tgkv_fwd_expert_w12(L->w12, s->ln, s->h, s->counts, s->lists, seq, ne, na,
+                                         d, dff, st));
+        CHECK_LAUNCH(tgkv_fwd_expert_w3(L->w3, s->h, s->y, s->counts, s->lists, seq, ne, na, d,
+                                        dff, st));
+    }
     CHECK_LAUNCH(tgkv_fwd_moe_combine(s->x, s->y, s->top_ids, s->top_w, seq, d, ne, na, st));
     return 1;
 }
