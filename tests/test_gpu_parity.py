@@ -449,6 +449,30 @@ def test_cfg5_long_context_131072(cuda, devbuf):
     lib.tg_kv_destroy(c)
 
 
+@pytest.mark.parametrize("merge2", ["1", "0"])
+def test_one_kv_head_of_131072_positions(cuda, devbuf, merge2, monkeypatch):
+    """configs[4] with its KV heads split over 8 GPUs: each GPU attends one KV
+    head (4 query heads) over 131072 positions, one segment of hundreds of
+    chunks.  Such segments merge in two levels (groups of 16 chunks, then the
+    groups); TGKV_MERGE2=0 merges in one CTA.  Both against the double oracle,
+    twice in a row (the counters reset themselves)."""
+    monkeypatch.setenv("TGKV_MERGE2", merge2)
+    lib = cuda
+    nh, nkv, hd, L = 4, 1, 128, 131072
+    q = O.normal(nh * hd, 707, 1).reshape(1, nh, hd)
+    k = O.normal(L * hd, 707, 2).reshape(L, hd)
+    v = O.normal(L * hd, 707, 3).reshape(L, hd)
+    c = make_cache(lib, devbuf, L, nkv, hd, 1, k, v)
+    del k, v
+    kvc = host_cache(lib, c, 1, L, hd)
+    f64 = O.attention_f64(q, kvc, nh, nkv, hd, 1, L - 1, L, L)
+    for _ in range(2):
+        got = attend(lib, devbuf, c, q, nh, 1)
+        assert rel_head_err(got, f64) < attn_tol(lib)
+    assert lib.tg_cuda_kv_device_error() == 0
+    lib.tg_kv_destroy(c)
+
+
 def token_kv(tok, pos, layer, kvd):
     """K/V of a token as a pure function of (token id, position, layer)."""
     k = O.normal(kvd, 31337, int(tok), int(pos), int(layer) * 2)

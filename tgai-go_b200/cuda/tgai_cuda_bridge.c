@@ -563,8 +563,21 @@ static int plan_attention(const TGCudaAttnCall* c, AttnPlan* pl) {
     return 1;
 }
 
+/* Two-level merge of long segments (more than 32 chunks: in groups of 16,
+ * then the groups); TGKV_MERGE2=0 merges every segment in one CTA. */
+static int merge2_on(void) {
+    const char* e = getenv("TGKV_MERGE2");
+    return !(e && e[0] == '0');
+}
+
+/* Partial slots of a launch: one per chunk, and with the two-level merge as
+ * many again for the group partials. */
+static uint64_t part_slots(const AttnPlan* pl) {
+    return pl->max_chunks * (merge2_on() ? 2u : 1u);
+}
+
 static uint64_t part_o_bytes(const AttnPlan* pl, uint32_t head_dim) {
-    return (pl->max_chunks * pl->gt * head_dim * 4 + 255) / 256 * 256;
+    return (part_slots(pl) * pl->gt * head_dim * 4 + 255) / 256 * 256;
 }
 
 /* Blocks of query rows over one bf16 head_dim-128 cache go to the tensor-core
@@ -621,16 +634,18 @@ uint64_t tg_cuda_kv_attn_scratch_bytes(const TGCudaAttnCall* c) {
     if (use_prefill(c)) return 256;
     AttnPlan pl;
     if (!plan_attention(c, &pl)) return 0;
-    return part_o_bytes(&pl, c->head_dim) + pl.max_chunks * pl.gt * 2 * 4;
+    return part_o_bytes(&pl, c->head_dim) + part_slots(&pl) * pl.gt * 2 * 4;
 }
 
 /* One arrival counter per segment; the tensor-core decode kernel also keeps
- * one tile queue per segment after them. */
+ * one tile queue per segment after them; the two-level merge one counter
+ * per chunk group after those. */
 uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c) {
     if (use_prefill(c)) return 1;
     AttnPlan pl;
     if (!plan_attention(c, &pl)) return 0;
-    return (uint64_t)c->n_items * c->n_kv_heads * pl.n_sub * (pl.tc ? 2u : 1u);
+    return (uint64_t)c->n_items * c->n_kv_heads * pl.n_sub * (pl.tc ? 2u : 1u) +
+           (merge2_on() ? pl.max_chunks : 0);
 }
 
 /* Segments of the call: (item, KV head, head subset) triples, each finished
@@ -737,6 +752,12 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         p.part_o = (float*)c->scratch;
         p.part_ml = (float*)((char*)c->scratch + po);
         p.counters = c->counters;
+        if (merge2_on()) {
+            p.two_level_min = 32;
+            p.l1_base = (uint32_t)pl.max_chunks;
+            p.gctr_base = (uint32_t)((uint64_t)c->n_items * c->n_kv_heads * pl.n_sub *
+                                     (pl.tc ? 2u : 1u));
+        }
         p.tile_ctr = (pl.tc && steal_on())
                          ? c->counters + (uint64_t)c->n_items * c->n_kv_heads * pl.n_sub
                          : NULL;

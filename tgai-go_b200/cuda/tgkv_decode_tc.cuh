@@ -515,28 +515,17 @@ attention_tc_kernel(const __grid_constant__ TGKvAttnParams p) {
         if (p.gather_world) gather_signal(p, tid);
         return;
     }
-    // ---- the last chunk of the segment to finish merges them all
-    __threadfence();
-    softmax_bar();
-    if (tid == 0) {
-        const uint32_t prev = atomicAdd(&p.counters[cidx], 1u);
-        flag[1] = (prev == ck.nch - 1) ? 1 : 0;
-    }
-    softmax_bar();
-    if (!flag[1]) return;
-    __threadfence();
+    // ---- the chunk that completes the segment merges it
     constexpr int kCap = (int)(OFF_ACC / (GT * 8));
-    if (!flag[0])                                    // the ring is idle unless a wait gave up
-        combine_segment<GT, HD, kCap>(p, ck.first, ck.nch, row, head0,
-                                      reinterpret_cast<float2*>(base + OFF_RING),
-                                      reinterpret_cast<float4*>(base + OFF_ACC),
-                                      reinterpret_cast<float*>(base + OFF_CRED), tid, lane, warp);
-    if (tid == 0) {
-        p.counters[cidx] = 0u;
+    if (merge_segment<GT, HD, kCap>(p, ck, u, cidx, row, head0,
+                                    reinterpret_cast<float2*>(base + OFF_RING),
+                                    reinterpret_cast<float4*>(base + OFF_ACC),
+                                    reinterpret_cast<float*>(base + OFF_CRED), flag, tid, lane,
+                                    warp) &&
+        steal && tid == 0)
         // every CTA of the segment has arrived, so every producer is past its
         // last take from the queue
-        if (steal) p.tile_ctr[cidx] = 0u;
-    }
+        p.tile_ctr[cidx] = 0u;
 }
 
 }  // namespace tgkv

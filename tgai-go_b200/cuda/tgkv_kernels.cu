@@ -204,11 +204,15 @@ __device__ __noinline__ void gather_signal(const TGKvAttnParams& p, int tid) {
 //    kB partials per step, so 128 * kB * 16 bytes are in flight per CTA.
 // Segments of more than CAP partials reload the pairs block by block.
 // Kept out of line so the streaming loop keeps its registers.
+// out_slot: ~0u writes the segment's outputs (and its gather); any other
+// value writes the merged, still unnormalised partial (O, and per head the
+// maximum and sum) to that partial slot, for the second level of a
+// two-level merge.
 template <int GT, int HD, int CAP>
 __device__ __noinline__ void combine_segment(const TGKvAttnParams& p, uint32_t first,
                                              uint32_t nparts, uint64_t row, uint32_t head0,
                                              float2* sm_ml, float4* sm_acc, float* sm_red,
-                                             int tid, int lane, int warp) {
+                                             int tid, int lane, int warp, uint32_t out_slot) {
     constexpr int NV = GT * HD / 4;            // float4 per partial output
     constexpr int G = 128 / NV;                // groups of threads over the partials
     constexpr int kB = 16;                     // partials per thread and step
@@ -306,17 +310,76 @@ __device__ __noinline__ void combine_segment(const TGKvAttnParams& p, uint32_t f
         float L = 0.f;
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; ++w) L += sm_red[(w * GT + h) * 2 + 1];
-        const bool any = L > 0.f;
-        const float o[4] = {any ? acc.x / L : 0.f, any ? acc.y / L : 0.f,
-                            any ? acc.z / L : 0.f, any ? acc.w / L : 0.f};
-        const uint64_t base = row + (uint64_t)(head0 + h) * HD + (v * 4) % HD;
+        if (out_slot != ~0u) {
+            reinterpret_cast<float4*>(p.part_o)[(uint64_t)out_slot * NV + v] = acc;
+            if ((v * 4) % HD == 0) {                // one thread per head: (M, L)
+                float M = -INFINITY;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            p.out[base + k] = o[k];
-            if (p.gather_world) gather_store(p, base + k, o[k]);
+                for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm_red[(w * GT + h) * 2]);
+                reinterpret_cast<float2*>(p.part_ml)[(uint64_t)out_slot * GT + h] =
+                    make_float2(M, L);
+            }
+        } else {
+            const bool any = L > 0.f;
+            const float o[4] = {any ? acc.x / L : 0.f, any ? acc.y / L : 0.f,
+                                any ? acc.z / L : 0.f, any ? acc.w / L : 0.f};
+            const uint64_t base = row + (uint64_t)(head0 + h) * HD + (v * 4) % HD;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                p.out[base + k] = o[k];
+                if (p.gather_world) gather_store(p, base + k, o[k]);
+            }
         }
     }
-    if (p.gather_world) gather_signal(p, tid);
+    if (out_slot == ~0u && p.gather_world) gather_signal(p, tid);
+}
+
+// After this CTA has written the partial of chunk u (segment ck, arrival
+// counter cidx): the CTA that completes the segment merges it.  Segments of
+// more than p.two_level_min chunks merge in two levels, so that no single
+// CTA walks hundreds of partials (one KV head of a 131072-position context
+// on a GPU is one segment of ~300 chunks): the last chunk of each group of
+// 16 to finish merges the group into a partial slot, and the last group to
+// finish merges those.  Called by the 128 threads of named barrier 1; flag
+// [0] is set when a wait gave up (the ring is then not idle and nothing is
+// merged), flag[1] is scratch.  Returns true on the CTA that finished the
+// segment (its counters are reset).
+template <int GT, int HD, int CAP>
+__device__ __forceinline__ bool merge_segment(const TGKvAttnParams& p, const Chunk& ck,
+                                              uint32_t u, uint64_t cidx, uint64_t row,
+                                              uint32_t head0, float2* sm_ml, float4* sm_acc,
+                                              float* sm_red, volatile int* flag, int tid,
+                                              int lane, int warp) {
+    constexpr uint32_t kGroup = 16;
+    __threadfence();
+    consumer_bar();
+    uint32_t parts = ck.nch, src = ck.first;
+    if (p.two_level_min && ck.nch > p.two_level_min) {
+        const uint32_t gi = (u - ck.first) / kGroup, g0 = gi * kGroup;
+        const uint32_t gsz = min(kGroup, ck.nch - g0);
+        const uint64_t gidx = (uint64_t)p.gctr_base + ck.first + gi;
+        if (tid == 0) flag[1] = atomicAdd(&p.counters[gidx], 1u) == gsz - 1 ? 1 : 0;
+        consumer_bar();
+        if (!flag[1]) return false;
+        __threadfence();
+        if (!flag[0])
+            combine_segment<GT, HD, CAP>(p, ck.first + g0, gsz, row, head0, sm_ml, sm_acc, sm_red,
+                                         tid, lane, warp, p.l1_base + ck.first + gi);
+        if (tid == 0) p.counters[gidx] = 0u;
+        __threadfence();
+        consumer_bar();
+        parts = (ck.nch + kGroup - 1) / kGroup;
+        src = p.l1_base + ck.first;
+    }
+    if (tid == 0) flag[1] = atomicAdd(&p.counters[cidx], 1u) == parts - 1 ? 1 : 0;
+    consumer_bar();
+    if (!flag[1]) return false;
+    __threadfence();
+    if (!flag[0])                                  // the ring is idle unless a wait gave up
+        combine_segment<GT, HD, CAP>(p, src, parts, row, head0, sm_ml, sm_acc, sm_red, tid, lane,
+                                     warp, ~0u);
+    if (tid == 0) p.counters[cidx] = 0u;
+    return true;
 }
 
 template <int DT, int HD, int GT>
@@ -583,23 +646,11 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
         return;
     }
 
-    // ---- the last chunk of the segment to finish merges them all
-    __threadfence();
-    consumer_bar();
+    // ---- the chunk that completes the segment merges it
     const uint64_t cidx = (uint64_t)(p.item_base + ck.item) * (p.n_sub * p.n_kv_heads) + ck.seg;
-    if (tid == 0) {
-        const uint32_t prev = atomicAdd(&p.counters[cidx], 1u);
-        sm_flag[1] = (prev == ck.nch - 1) ? 1 : 0;
-    }
-    consumer_bar();
-    if (!sm_flag[1]) return;
-    __threadfence();
-    if (!sm_flag[0])                              // the ring is idle unless a wait gave up
-        combine_segment<GT, HD, C::ML_CAP>(p, ck.first, ck.nch, row, head0,
-                                           reinterpret_cast<float2*>(smem),
-                                           reinterpret_cast<float4*>(smem + C::OFF_ACC), sm_red,
-                                           tid, lane, warp);
-    if (tid == 0) p.counters[cidx] = 0u;
+    merge_segment<GT, HD, C::ML_CAP>(p, ck, u, cidx, row, head0, reinterpret_cast<float2*>(smem),
+                                     reinterpret_cast<float4*>(smem + C::OFF_ACC), sm_red, sm_flag,
+                                     tid, lane, warp);
 }
 
 }  // namespace tgkv

@@ -77,6 +77,14 @@ typedef struct {
     /* Failure injection for tests: nonzero makes the producer issue no loads,
      * so every wait of the launch runs out and reports through err. */
     uint32_t  stall_loads;
+    /* Two-level merge for segments of more than two_level_min chunks (0:
+     * never): chunks merge in groups of 16 (the last of a group to finish
+     * merges it into partial slot l1_base + first + group, counting on
+     * counters[gctr_base + first + group]), then the last group to finish
+     * merges the group partials. */
+    uint32_t  two_level_min;
+    uint32_t  l1_base;
+    uint32_t  gctr_base;
     /* Used when cache0.tmap is 0 (the no-allocation entry): the cache's tensor
      * map travels in the parameter block itself. */
     CUtensorMap tmap0;
