@@ -269,6 +269,10 @@ def workload(args, name):
         wl["n_seq"] = args.seqs
     if args.layers:
         wl["layers"] = args.layers
+    if getattr(args, "kv_heads", 0):
+        wl["nkv"] = args.kv_heads
+    if getattr(args, "q_heads", 0):
+        wl["nh"] = args.q_heads
     return wl
 
 
@@ -1067,6 +1071,10 @@ def main():
                     help="sequences per GPU (default: the workload's); for small profiling cases")
     ap.add_argument("--layers", type=int, default=0,
                     help="layers (default: the workload's); for small profiling cases")
+    ap.add_argument("--kv-heads", type=int, default=0,
+                    help="KV heads (default: the workload's); with --q-heads, e.g. one rank's "
+                         "share of a KV-head split on one GPU")
+    ap.add_argument("--q-heads", type=int, default=0, help="query heads (default: the workload's)")
     ap.add_argument("--weak", action="store_true",
                     help="cfg4 at N > 1: every GPU its own set of sequences (weak scaling) as "
                          "the headline, instead of the one set split over the GPUs (strong)")
