@@ -43,6 +43,9 @@ int   tg_cuda_kv_h2d(void* dst, const void* src, size_t bytes, void* stream);
  * legacy default stream), where tg_cuda_kv_h2d copies synchronously.  A
  * pageable source may be reused as soon as this returns. */
 int   tg_cuda_kv_h2d_async(void* dst, const void* src, size_t bytes, void* stream);
+/* Device to host on `stream`, asynchronous also when stream is NULL (for a
+ * page-locked destination; a pageable one is copied before the call returns). */
+int   tg_cuda_kv_d2h_async(void* dst, const void* src, size_t bytes, void* stream);
 /* dst (device) = a | b | c, read by one small kernel from page-locked host
  * memory (a, b, c: device pointers of such memory, tg_cuda_kv_host_device_ptr;
  * sizes and addresses multiples of 16 bytes).  Queued as a programmatic

@@ -74,6 +74,45 @@ def test_single_rank_gather_equals_plain_decode(cuda, devbuf, monkeypatch, kerne
         lib.tg_kv_destroy(c)
 
 
+@pytest.mark.parametrize("pinned", [True, False])
+def test_single_rank_gather_from_host_buffers(cuda, devbuf, pinned):
+    """tg_kv_batch_decode_gather_host on one rank: inputs from page-locked
+    memory go up through the staging kernel, from pageable memory through
+    copies; the gathered rows come back to out_host; five calls in a row on
+    one gather object, each against the oracle."""
+    import torch
+    lib = cuda
+    n_seq, L, nkv, hd, nh = 2, 1800, 4, 128, 16
+    caches, b, rows = _plan(lib, devbuf, n_seq, L, nkv, hd, nh, 6300)
+    elems = n_seq * nh * hd
+    g = lib.tg_kv_gather_create(1, 0, elems)
+    tgkv.check(g, lib)
+    alloc = (lambda *s: torch.empty(*s).pin_memory()) if pinned else (lambda *s: torch.empty(*s))
+    qh, kh, vh = alloc(n_seq, nh, hd), alloc(n_seq, nkv * hd), alloc(n_seq, nkv * hd)
+    oh = alloc(elems)
+    for step in range(5):
+        q = O.normal(n_seq * nh * hd, 6400 + step, 1).reshape(n_seq, nh, hd)
+        kn = O.normal(n_seq * nkv * hd, 6400 + step, 2).reshape(n_seq, nkv * hd)
+        vn = O.normal(n_seq * nkv * hd, 6400 + step, 3).reshape(n_seq, nkv * hd)
+        qh.numpy()[:] = q
+        kh.numpy()[:] = kn
+        vh.numpy()[:] = vn
+        tgkv.check(lib.tg_kv_batch_decode_gather_host(b, qh.data_ptr(), kh.data_ptr(),
+                                                      vh.data_ptr(), oh.data_ptr(), g, None), lib)
+        assert lib.tg_cuda_kv_sync(None)
+        got = oh.numpy().reshape(n_seq, nh, hd).copy()
+        for i, c in enumerate(caches):
+            Lc = lib.tg_kv_len(c)
+            kvc = host_cache(lib, c, 1, L + 8, nkv * hd)
+            eng = O.attention_engine(q[i:i + 1], kvc, nh, nkv, hd, 1, Lc - 1, Lc, L + 8)
+            assert rel_head_err(got[i], eng[0]) < 1e-5, (step, i)
+    assert lib.tg_cuda_kv_device_error() == 0
+    lib.tg_kv_gather_destroy(g)
+    lib.tg_kv_batch_destroy(b)
+    for c in caches:
+        lib.tg_kv_destroy(c)
+
+
 def test_gather_rejects_mismatched_shape(cuda, devbuf):
     lib = cuda
     caches, b, rows = _plan(lib, devbuf, 2, 300, 2, 64, 8, 6200)

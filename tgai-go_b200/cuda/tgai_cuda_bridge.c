@@ -336,6 +336,12 @@ int tg_cuda_kv_h2d_async(void* dst, const void* src, size_t bytes, void* stream)
                    "h2d async");
 }
 
+int tg_cuda_kv_d2h_async(void* dst, const void* src, size_t bytes, void* stream) {
+    if (!bytes) return 1;
+    return cuda_ok(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, (cudaStream_t)stream),
+                   "d2h async");
+}
+
 int tg_cuda_kv_stage_host(void* dst, const void* a, size_t na, const void* b, size_t nb,
                           const void* c, size_t nc, void* stream) {
     if ((na | nb | nc) % 16 || (((uintptr_t)dst | (uintptr_t)a | (uintptr_t)b | (uintptr_t)c) & 15)) {

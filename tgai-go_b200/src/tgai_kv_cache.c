@@ -674,7 +674,7 @@ static int batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_h
     const uint64_t qb = (uint64_t)b->n * b->n_heads * b->head_dim * 4;
     const uint64_t kb = (uint64_t)b->n * b->kv_dim * 4;
     const uint64_t need = 2 * qb + 2 * kb + 64;
-    if (!g && qb + 2 * kb <= TGKV_SMALL_UPLOAD && !(qb % 16) && !(kb % 16)) {
+    if (qb + 2 * kb <= TGKV_SMALL_UPLOAD && !(qb % 16) && !(kb % 16)) {
         void* dq = tg_cuda_kv_host_device_ptr(q_host);
         void* dk = tg_cuda_kv_host_device_ptr(k_host);
         void* dv = tg_cuda_kv_host_device_ptr(v_host);
@@ -696,10 +696,14 @@ static int batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_h
                 set_err("%s", tg_cuda_kv_last_error());
                 return 0;
             }
-            float* direct = (float*)tg_cuda_kv_host_device_ptr(out_host);
-            if (!batch_decode(b, q, k, v, direct ? direct : o, NULL, stream)) return 0;
+            /* the kernel stores a page-locked out_host's rows itself; with a
+             * gather, the whole gathered buffer comes back after the wait */
+            float* direct = g ? NULL : (float*)tg_cuda_kv_host_device_ptr(out_host);
+            if (!batch_decode(b, q, k, v, direct ? direct : o, g, stream)) return 0;
             b->last_launches++;
-            if (!direct && !tg_cuda_kv_d2h(out_host, o, qb, stream)) {
+            const void* src = g ? (const void*)tg_kv_gather_buffer(g) : (const void*)o;
+            const uint64_t ob = g ? (uint64_t)g->world * g->elems * 4 : qb;
+            if (!direct && !tg_cuda_kv_d2h_async(out_host, src, ob, stream)) {
                 set_err("%s", tg_cuda_kv_last_error());
                 return 0;
             }
@@ -739,7 +743,7 @@ static int batch_decode_host(TGKvBatch* b, const float* q_host, const float* k_h
     if (!batch_decode(b, q, k, v, direct ? direct : o, g, stream)) return 0;
     const void* src = g ? (const void*)tg_kv_gather_buffer(g) : (const void*)o;
     const uint64_t ob = g ? (uint64_t)g->world * g->elems * 4 : qb;
-    if ((!direct && !tg_cuda_kv_d2h(out_host, src, ob, stream)) ||
+    if ((!direct && !tg_cuda_kv_d2h_async(out_host, src, ob, stream)) ||
         !tg_cuda_kv_event_record(b->slot_free[s], stream)) {
         set_err("%s", tg_cuda_kv_last_error());
         return 0;

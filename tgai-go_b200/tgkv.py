@@ -145,6 +145,7 @@ PROTOS = {
     "tg_cuda_kv_free": (None, [vp]),
     "tg_cuda_kv_h2d": (i32, [vp, vp, C.c_size_t, vp]),
     "tg_cuda_kv_h2d_async": (i32, [vp, vp, C.c_size_t, vp]),
+    "tg_cuda_kv_d2h_async": (i32, [vp, vp, C.c_size_t, vp]),
     "tg_cuda_kv_stage_host": (i32, [vp, vp, C.c_size_t, vp, C.c_size_t, vp, C.c_size_t, vp]),
     "tg_cuda_kv_d2h": (i32, [vp, vp, C.c_size_t, vp]),
     "tg_cuda_kv_memset": (i32, [vp, i32, C.c_size_t, vp]),
