@@ -26,7 +26,7 @@ def decode_kernel(request, monkeypatch):
     """Every test three times: with the library's own choice of decode
     kernel; with every bf16 head_dim-128 call forced onto the tensor-core
     decode kernel (which the library otherwise keeps for launches of at
-    least 262144 position x head rows); and the same with its opt-in tile
+    least 131072 position x head rows); and the same with its opt-in tile
     stealing.  Both
     split-sequence kernels and both tensor-core schedules meet every case."""
     if request.param.startswith("tc"):

@@ -515,7 +515,7 @@ __attribute__((visibility("hidden"))) uint32_t tgkv_pick_chunk_tiled(const uint3
 
 /* Decode calls over bf16 head_dim-128 caches with a swizzled tensor map (a
  * batch's caches all have one when they are bf16 / 128) run on the
- * tensor-core decode kernel when the launch streams at least 262144
+ * tensor-core decode kernel when the launch streams at least 131072
  * (position, KV head, head subset) rows -- about one wave of 16-tile CTAs.
  * That kernel keeps one CTA per SM and pays more per CTA (TMEM, the q terms,
  * the pipeline fill) but streams HBM at full speed; small launches are
@@ -534,7 +534,10 @@ static int use_decode_tc(const TGCudaAttnCall* c, uint32_t gt) {
     uint64_t rows = 0;
     for (uint32_t i = 0; i < c->n_items; i++) rows += c->n_pos[i];
     rows *= (uint64_t)c->n_heads / gt;                 /* KV heads x head subsets */
-    return rows >= 262144;
+    /* one KV head of a 131072-position context (a GPU's share of configs[4]
+     * split over 8): 1337 tok/s here against 1234 on the CUDA-core kernel;
+     * one 4096-position sequence of 4 KV heads (16384 rows) stays there */
+    return rows >= 131072;
 }
 
 static int plan_attention(const TGCudaAttnCall* c, AttnPlan* pl) {
@@ -569,11 +572,16 @@ static int plan_attention(const TGCudaAttnCall* c, AttnPlan* pl) {
     return 1;
 }
 
-/* Two-level merge of long segments (more than 32 chunks: in groups of 16,
- * then the groups); TGKV_MERGE2=0 merges every segment in one CTA. */
+/* Two-level merge of long segments (in groups of 16 chunks, then the
+ * groups) above merge2_min() chunks; TGKV_MERGE2=0 merges every segment in
+ * one CTA. */
 static int merge2_on(void) {
     const char* e = getenv("TGKV_MERGE2");
     return !(e && e[0] == '0');
+}
+static uint32_t merge2_min(void) {
+    const char* e = getenv("TGKV_MERGE2_MIN");
+    return e && atoi(e) > 0 ? (uint32_t)atoi(e) : 96u;
 }
 
 /* Partial slots of a launch: one per chunk, and with the two-level merge as
@@ -759,7 +767,7 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         p.part_ml = (float*)((char*)c->scratch + po);
         p.counters = c->counters;
         if (merge2_on()) {
-            p.two_level_min = 32;
+            p.two_level_min = merge2_min();
             p.l1_base = (uint32_t)pl.max_chunks;
             p.gctr_base = (uint32_t)((uint64_t)c->n_items * c->n_kv_heads * pl.n_sub *
                                      (pl.tc ? 2u : 1u));
