@@ -45,6 +45,15 @@ constexpr int kErrFullTimeout = 1;
 constexpr int kErrEmptyTimeout = 2;
 constexpr int kErrGatherTimeout = 4;
 
+// Kernels launch as programmatic dependents unless TGKV_PDL=0.
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("TGKV_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 }  // namespace tgkv
 
 namespace tgkv {
@@ -873,37 +882,47 @@ extern "C" int tgkv_launch_append(const TGKvAppendParams* p, int dtype, void* st
 }
 
 namespace tgkv {
+// Launched as a programmatic dependent of the attention: it starts spinning
+// once the attention's CTAs have streamed their tiles (every rank's arrivals
+// come from the attention's last, merging CTAs), so its launch overlaps the
+// merges; it waits for the attention itself only at its end, so the next
+// kernel, which waits for this one, also follows the attention.
 __global__ void gather_wait_kernel(const uint32_t* flag, uint32_t target, int32_t* err) {
-    if (threadIdx.x != 0) return;
-    const unsigned long long t0 = global_ns();
-    for (;;) {
-        uint32_t v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-        if ((int32_t)(v - target) >= 0) break;
-        if (global_ns() - t0 > kWaitLimitNs) {
-            atomicExch(err, kErrGatherTimeout);
-            break;
+    if (threadIdx.x == 0) {
+        const unsigned long long t0 = global_ns();
+        for (;;) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+            if ((int32_t)(v - target) >= 0) break;
+            if (global_ns() - t0 > kWaitLimitNs) {
+                atomicExch(err, kErrGatherTimeout);
+                break;
+            }
+            __nanosleep(64);
         }
-        __nanosleep(64);
     }
+    __syncwarp();
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 }  // namespace tgkv
 
 extern "C" int tgkv_launch_gather_wait(const uint32_t* flag, uint32_t target, int32_t* err,
                                        void* stream) {
-    tgkv::gather_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flag, target, err);
-    return (int)cudaGetLastError();
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = tgkv::pdl_enabled() ? 1 : 0;
+    return (int)cudaLaunchKernelEx(&cfg, tgkv::gather_wait_kernel, flag, target, err);
 }
 
 namespace tgkv {
-bool pdl_enabled() {
-    static const bool on = [] {
-        const char* e = getenv("TGKV_PDL");
-        return !(e && e[0] == '0');
-    }();
-    return on;
-}
-
 // Up to three page-locked host arrays (device-mapped pointers) copied into
 // one device buffer back to back.  Every thread issues all its loads before
 // any store, so the PCIe round trip is paid once.  Launched as a programmatic
