@@ -7,10 +7,11 @@
 // epilogue (2.5-3 us), which is most of a layer's time on a 3B MoE.  Here a
 // layer is five phases of one resident grid:
 //   P1  RMSNorm(x) . Wqkv in row pairs, bias, RoPE, K/V row appended at pos;
-//   P2  split attention over the cache: warp tasks of (KV head, position
-//       range) for all query heads of the group, online softmax, partials;
-//   P3  every CTA merges the partials of all heads into shared memory (one
-//       warp per head), then the out projection + residual;
+//   P2  split attention over the cache: warp tasks of (query head, position
+//       range), online softmax, partials; the task that finishes a head last
+//       merges its partials;
+//   P3  the merged heads into shared memory, then the out projection +
+//       residual;
 //   P4  RMSNorm(x), router + top-k (every CTA, same arithmetic as the
 //       engine's), routed experts' W1/W2 rows + SiLU (or the dense FFN's);
 //   P5  routed experts' W3 rows, k-ordered sum + residual (or dense W3).
@@ -150,54 +151,25 @@ __device__ __forceinline__ void dots(const float* const (&w)[NW], const float* c
     for (int n = 0; n < NW; ++n) acc[n] = warp_sum(acc[n]);
 }
 
-// Bulk prefetch of `bytes` (multiple of 16, 16-byte aligned) into L2: one
-// instruction, no registers held, nothing waits for it.
-__device__ __forceinline__ void prefetch_l2(const void* ptr, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(bytes) : "memory");
-}
-
-// The rows this warp will read in a coming phase, into L2: rows
-// first + k * step (< limit) of `base` (row stride `stride` floats, `bytes`
-// per row), one per lane and pass.  `skip` leading rows are left out (a
-// phase's first row, which its own loads start at once).
-__device__ __forceinline__ void prefetch_rows(const float* base, uint64_t stride, uint32_t bytes,
-                                              uint32_t first, uint32_t step, uint32_t limit,
-                                              uint32_t skip = 0) {
-    const uint32_t lane = threadIdx.x & 31;
-    for (uint32_t k = skip + lane;; k += 32) {
-        const uint64_t r = (uint64_t)first + (uint64_t)k * step;
-        if (r >= limit) break;
-        prefetch_l2(base + r * stride, bytes);
-    }
-}
-
 }  // namespace tgkvs
 
 using namespace tgkvs;
 
-// P2 for one KV head's position range [p_begin, p_end): the G query heads of
-// the group against K/V rows of the fp32 cache, lane l owning dimensions
-// [4l, 4l + 4) (lanes past head_dim / 4 idle).  Online softmax in the natural
-// exponent; the partial goes to part as [m, l, 0, 0, o[head_dim]] (running
-// max, sum, unnormalised output; stride head_dim + 4 keeps o 16-byte aligned).
-template <int G>
-__device__ __forceinline__ void attn_task(const TGFwdStepParams& p, const float* kvc, uint32_t kvh,
-                                          uint32_t task, uint32_t p_begin, uint32_t p_end) {
+// P2 for query head h's position range [p_begin, p_end) against the K/V rows
+// of its KV head kvh in the fp32 cache, lane l owning dimensions [4l, 4l + 4)
+// (lanes past head_dim / 4 idle); kSub positions' rows in flight at a time.
+// Online softmax in the natural exponent; the partial goes to part as
+// [m, l, 0, 0, o[head_dim]] (running max, sum, unnormalised output; stride
+// head_dim + 4 keeps o 16-byte aligned), slot h * kTgStepMaxTasks + task.
+__device__ __forceinline__ void attn_task(const TGFwdStepParams& p, const float* kvc, uint32_t h,
+                                          uint32_t kvh, uint32_t task, uint32_t p_begin,
+                                          uint32_t p_end) {
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t hd = p.head_dim, kv_dim = p.n_kv_heads * hd;
     const bool on = lane * 4 < hd;
-    float4 qv[G];
-#pragma unroll
-    for (int t = 0; t < G; ++t)
-        qv[t] = on ? ldcg4(p.q + (uint64_t)(kvh * G + t) * hd + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-    float m[G], l[G];
-    float4 o[G];
-#pragma unroll
-    for (int t = 0; t < G; ++t) {
-        m[t] = -INFINITY;
-        l[t] = 0.f;
-        o[t] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    const float4 qv = on ? ldcg4(p.q + (uint64_t)h * hd + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float m = -INFINITY, l = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
     const float* K = kvc + (uint64_t)kvh * hd + lane * 4;
     const float* V = kvc + (uint64_t)p.max_seq * kv_dim + (uint64_t)kvh * hd + lane * 4;
     for (uint32_t p0 = p_begin; p0 < p_end; p0 += kSub) {
@@ -208,91 +180,94 @@ __device__ __forceinline__ void attn_task(const TGFwdStepParams& p, const float*
             kr[u] = in ? ldcg4(K + (uint64_t)(p0 + u) * kv_dim) : make_float4(0.f, 0.f, 0.f, 0.f);
             vr[u] = in ? ldcg4(V + (uint64_t)(p0 + u) * kv_dim) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+        float sc[kSub];
+        float mx = m;
 #pragma unroll
-        for (int t = 0; t < G; ++t) {
-            float s[kSub];
-            float mx = m[t];
-#pragma unroll
-            for (int u = 0; u < kSub; ++u) {
-                s[u] = warp_sum(dot4(qv[t], kr[u], 0.f)) * p.scale;
-                if (p0 + u >= p_end) s[u] = -INFINITY;
-                mx = fmaxf(mx, s[u]);
-            }
-            const float corr = m[t] == -INFINITY ? 0.f : expf(m[t] - mx);
-            float4 acc = make_float4(o[t].x * corr, o[t].y * corr, o[t].z * corr, o[t].w * corr);
-            float ls = l[t] * corr;
-#pragma unroll
-            for (int u = 0; u < kSub; ++u) {
-                const float e = s[u] == -INFINITY ? 0.f : expf(s[u] - mx);
-                ls += e;
-                acc.x = fmaf(e, vr[u].x, acc.x);
-                acc.y = fmaf(e, vr[u].y, acc.y);
-                acc.z = fmaf(e, vr[u].z, acc.z);
-                acc.w = fmaf(e, vr[u].w, acc.w);
-            }
-            m[t] = mx;
-            l[t] = ls;
-            o[t] = acc;
+        for (int u = 0; u < kSub; ++u) {
+            sc[u] = warp_sum(dot4(qv, kr[u], 0.f)) * p.scale;
+            if (p0 + u >= p_end) sc[u] = -INFINITY;
+            mx = fmaxf(mx, sc[u]);
         }
-    }
-    const uint32_t stride = hd + 4;
+        const float corr = m == -INFINITY ? 0.f : expf(m - mx);
+        float4 acc = make_float4(o.x * corr, o.y * corr, o.z * corr, o.w * corr);
+        float ls = l * corr;
 #pragma unroll
-    for (int t = 0; t < G; ++t) {
-        float* dst = p.part + ((uint64_t)(kvh * kTgStepMaxTasks + task) * G + t) * stride;
-        if (lane == 0) {
-            dst[0] = m[t];
-            dst[1] = l[t];
+        for (int u = 0; u < kSub; ++u) {
+            const float e = sc[u] == -INFINITY ? 0.f : expf(sc[u] - mx);
+            ls += e;
+            acc.x = fmaf(e, vr[u].x, acc.x);
+            acc.y = fmaf(e, vr[u].y, acc.y);
+            acc.z = fmaf(e, vr[u].z, acc.z);
+            acc.w = fmaf(e, vr[u].w, acc.w);
         }
-        if (on) *reinterpret_cast<float4*>(dst + 4 + lane * 4) = o[t];
+        m = mx;
+        l = ls;
+        o = acc;
     }
+    float* dst = p.part + ((uint64_t)h * kTgStepMaxTasks + task) * (hd + 4);
+    if (lane == 0) {
+        dst[0] = m;
+        dst[1] = l;
+    }
+    if (on) *reinterpret_cast<float4*>(dst + 4 + lane * 4) = o;
 }
 
-// Head h's attention output from its n_tasks partials, by one warp, into
-// dst [head_dim] (shared memory): an online merge over batches of 16
-// partials (all their loads in flight), each rescaled to the running maximum.
-template <int G>
-__device__ __forceinline__ void attn_merge_head(const TGFwdStepParams& p, uint32_t h,
-                                                uint32_t n_tasks, float* dst) {
+// Head h's attention output from its n_tasks partials, by the one warp that
+// finished the head's last task, into attn (global, [q_dim]): the maximum M
+// of the partials' maxima, L = sum exp(m_i - M) l_i (lane i % 32 holding
+// partial i's m and l), O = sum exp(m_i - M) o_i / L with lane l owning
+// dimensions [4l, 4l + 4), sixteen partials' rows in flight at a time.
+__device__ __forceinline__ void attn_merge(const TGFwdStepParams& p, uint32_t h, uint32_t n_tasks) {
     const uint32_t lane = threadIdx.x & 31;
-    const uint32_t hd = p.head_dim, stride = hd + 4, kvh = h / G, t = h % G;
+    const uint32_t hd = p.head_dim, stride = hd + 4;
     const bool on = lane * 4 < hd;
-    const float* base = p.part + ((uint64_t)kvh * kTgStepMaxTasks * G + t) * stride;
-    float M = -INFINITY, L = 0.f;
+    const float* base = p.part + (uint64_t)h * kTgStepMaxTasks * stride;
+    constexpr int kPer = kTgStepMaxTasks / 32;
+    float w[kPer], li[kPer];
+    float M = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+        const uint32_t i = lane + 32 * u;
+        w[u] = i < n_tasks ? __ldcg(base + (uint64_t)i * stride) : -INFINITY;
+        li[u] = i < n_tasks ? __ldcg(base + (uint64_t)i * stride + 1) : 0.f;
+        M = fmaxf(M, w[u]);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float L = 0.f;
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+        w[u] = w[u] == -INFINITY ? 0.f : expf(w[u] - M);     // the weight of partial i
+        L = fmaf(w[u], li[u], L);
+    }
+    L = warp_sum(L);
     float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (uint32_t c0 = 0; c0 < n_tasks; c0 += 16) {
-        float mc[16], lc[16];
+#pragma unroll 1
+    for (uint32_t i0 = 0; i0 < n_tasks; i0 += 16) {
         float4 oc[16];
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-            const bool in = c0 + u < n_tasks;
-            const float* pc = base + (uint64_t)(c0 + u) * G * stride;
-            mc[u] = in ? __ldcg(pc) : -INFINITY;
-            lc[u] = in ? __ldcg(pc + 1) : 0.f;
-            oc[u] = in && on ? ldcg4(pc + 4 + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        float nm = M;
-#pragma unroll
-        for (int u = 0; u < 16; ++u) nm = fmaxf(nm, mc[u]);
-        const float corr = M == -INFINITY ? 0.f : expf(M - nm);
-        L *= corr;
-        O.x *= corr;
-        O.y *= corr;
-        O.z *= corr;
-        O.w *= corr;
+        for (int u = 0; u < 16; ++u)
+            oc[u] = on && i0 + u < n_tasks ? ldcg4(base + (uint64_t)(i0 + u) * stride + 4 + lane * 4)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
-            const float f = mc[u] == -INFINITY ? 0.f : expf(mc[u] - nm);
-            L = fmaf(f, lc[u], L);
+            const uint32_t i = i0 + u;
+            float f = 0.f;
+#pragma unroll
+            for (int v = 0; v < kPer; ++v) {
+                const float fv = __shfl_sync(0xffffffffu, w[v], i & 31);
+                if (i >> 5 == (uint32_t)v) f = fv;
+            }
+            if (i >= n_tasks) f = 0.f;
             O.x = fmaf(f, oc[u].x, O.x);
             O.y = fmaf(f, oc[u].y, O.y);
             O.z = fmaf(f, oc[u].z, O.z);
             O.w = fmaf(f, oc[u].w, O.w);
         }
-        M = nm;
     }
     if (on) {
         const float inv = 1.0f / L;
-        *reinterpret_cast<float4*>(dst + lane * 4) =
+        *reinterpret_cast<float4*>(p.attn + (uint64_t)h * hd + lane * 4) =
             make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
     }
 }
@@ -355,6 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
     float* sh = smem + p.sx_floats;       // [na or 1][dff]
     uint32_t* bar = p.state;
     int* err = reinterpret_cast<int*>(p.state + 1);
+    uint32_t* head_ctr = p.state + 2;     // finished attention tasks per query head
     uint32_t target = 0;
     // attention split: at most kTgStepMaxTasks position ranges per KV head,
     // each a multiple of kSub positions, about 16 positions where L allows
@@ -365,28 +341,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
     n_tasks = (L + ch - 1) / ch;
     const uint32_t half = hd >> 1;
     const uint32_t npair = (q_dim + 2 * kv_dim) / 2;
-    // With p.prefetch, each phase's weight rows go to L2 one phase ahead (the
-    // routed experts' as soon as the router has chosen), so HBM keeps
-    // streaming while the grid waits at a barrier; every warp prefetches
-    // exactly the rows it will read itself.  Off by default: it measured
-    // slower, the early streams queueing ahead of the current phase's loads.
-    if (p.prefetch) prefetch_rows(p.layers[0].wqkv, 2 * (uint64_t)d, 8 * d, gw, tw, npair);
 
     for (uint32_t l = 0; l < p.n_layers; ++l) {
         const TGFwdStepLayer W = p.layers[l];
         float* kvc = p.kvc[l];
-        if (p.prefetch) {
-            // P3's out-projection rows and P2's K/V ranges
-            prefetch_rows(W.wo, q_dim, 4 * q_dim, gw, tw, d);
-            for (uint32_t t = gw; t < nkv * n_tasks; t += tw) {
-                const uint32_t kvh = t / n_tasks, pb = (t % n_tasks) * ch;
-                const uint32_t pe = pb + ch < L ? pb + ch : L;
-                for (uint32_t j = pb + lane; j < pe; j += 32) {
-                    prefetch_l2(kvc + (uint64_t)j * kv_dim + kvh * hd, 4 * hd);
-                    prefetch_l2(kvc + ((uint64_t)p.max_seq + j) * kv_dim + kvh * hd, 4 * hd);
-                }
-            }
-        }
         // ---- P1: norm, Q/K/V row pairs, bias, RoPE at pos, K/V append
         stage(sx, p.x, W.ln1, d, red);
         for (uint32_t mp = gw; mp < npair; mp += tw) {
@@ -416,20 +374,29 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
             }
         }
         if (!grid_sync(bar, target, err, &s_ok)) return;
-        // ---- P2: split attention, partials per (KV head, position range)
-        for (uint32_t t = gw; t < nkv * n_tasks; t += tw) {
-            const uint32_t kvh = t / n_tasks, task = t % n_tasks;
+        // ---- P2: split attention, partials per (query head, position
+        // range), one task per CTA before any CTA takes a second; the task
+        // that finishes a head last merges it into attn
+        for (uint32_t t = blockIdx.x + gridDim.x * warp; t < nkv * G * n_tasks; t += tw) {
+            const uint32_t h = t / n_tasks, task = t % n_tasks;
             const uint32_t pb = task * ch, pe = pb + ch < L ? pb + ch : L;
-            attn_task<G>(p, kvc, kvh, task, pb, pe);
+            attn_task(p, kvc, h, h / G, task, pb, pe);
+            __syncwarp();
+            uint32_t prev = 0;
+            if (lane == 0) {
+                __threadfence();                     // this task's partial, then the count
+                prev = atomicAdd(head_ctr + h, 1u);
+            }
+            prev = __shfl_sync(0xffffffffu, prev, 0);
+            if (prev == n_tasks - 1) {
+                __threadfence();                     // every task's partial before the merge
+                attn_merge(p, h, n_tasks);
+                if (lane == 0) head_ctr[h] = 0;      // counted again only a layer later
+            }
         }
         if (!grid_sync(bar, target, err, &s_ok)) return;
-        // ---- P3: every CTA merges all heads into sx, then out projection + residual
-        if (p.prefetch && !ne) {          // the dense FFN's W1 and W2 rows of P4
-            prefetch_rows(W.w12, d, 4 * d, gw, tw, dff);
-            prefetch_rows(W.w12 + (uint64_t)dff * d, d, 4 * d, gw, tw, dff);
-        }
-        for (uint32_t h = warp; h < nkv * G; h += kWarps) attn_merge_head<G>(p, h, n_tasks, sx + h * hd);
-        __syncthreads();
+        // ---- P3: the merged heads into sx, then out projection + residual
+        stage(sx, p.attn, nullptr, q_dim, red);
         for (uint32_t n = gw; n < d; n += tw) {
             float a[1];
             dots<1, 12>({W.wo + (uint64_t)n * q_dim}, {sx}, q_dim, a);
@@ -447,24 +414,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
             __syncthreads();
             if (warp == 0) top_k_warp(slog, ne, na, s_ids, s_w);
             __syncthreads();
-            if (p.prefetch) {
-                // this warp's later W1/W2 rows of the routed experts, then
-                // their W3 rows of P5
-                for (uint32_t k = 0; k < na; ++k) {
-                    const int e = s_ids[k];
-                    if (e < 0 || (uint32_t)e >= ne) continue;
-                    const float* w1 = W.w12 + (uint64_t)e * 2 * dff * d;
-                    // task t = k * dff + j: the first of this warp's tasks is skipped
-                    const uint32_t t0 = gw, lo = k * dff, hi = lo + dff;
-                    uint32_t first = t0 >= lo ? t0 : t0 + ((lo - t0 + tw - 1) / tw) * tw;
-                    if (first == t0) first += tw;
-                    if (first < hi) {
-                        prefetch_rows(w1, d, 4 * d, first - lo, tw, dff);
-                        prefetch_rows(w1 + (uint64_t)dff * d, d, 4 * d, first - lo, tw, dff);
-                    }
-                    prefetch_rows(W.w3 + (uint64_t)e * d * dff, dff, 4 * dff, gw, tw, d);
-                }
-            }
             for (uint32_t t = gw; t < na * dff; t += tw) {
                 const uint32_t k = t / dff, j = t % dff;
                 const int e = s_ids[k];
@@ -478,7 +427,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
                 if (lane == 0) p.h[(uint64_t)k * dff + j] = hv;
             }
         } else {
-            if (p.prefetch) prefetch_rows(W.w3, dff, 4 * dff, gw, tw, d);
             for (uint32_t j = gw; j < dff; j += tw) {
                 float a[2];
                 dots<2, 12>({W.w12 + (uint64_t)j * d, W.w12 + (uint64_t)(dff + j) * d}, {sx, sx}, d, a);
@@ -487,8 +435,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
         }
         if (!grid_sync(bar, target, err, &s_ok)) return;
         // ---- P5: W3 rows, k-ordered weighted sum (or dense W3) + residual
-        if (p.prefetch && l + 1 < p.n_layers)
-            prefetch_rows(p.layers[l + 1].wqkv, 2 * (uint64_t)d, 8 * d, gw, tw, npair);
         stage(sh, p.h, nullptr, (ne ? na : 1) * dff, red);
         for (uint32_t i = gw; i < d; i += tw) {
             float ot = 0.f;
@@ -589,6 +535,7 @@ extern "C" int tgkv_fwd_step_supported(uint32_t d, uint32_t n_heads, uint32_t n_
     if (g != 1 && g != 2 && g != 3 && g != 4 && g != 8) return 0;
     if (head_dim != 32 && head_dim != 64 && head_dim != 128) return 0;
     if (d % 4 || dff % 4 || ne > 16 || na > 8 || (ne && (na == 0 || na > ne))) return 0;
+    if (n_heads > kTgStepStateWords - 2) return 0;
     return tgkv_fwd_step_smem(d, n_heads * head_dim, dff, ne, na) <= 160 * 1024;
 }
 

@@ -100,9 +100,11 @@ int tgkv_fwd_dec_w3_combine(const float* w3, const float* h, const int32_t* top_
  * RoPE + append, split attention, out projection, router + experts W1/W2 or
  * the dense W1/W2, W3 + combine) separated by bounded grid barriers.  x [d]
  * holds the embedded token on entry and the last layer's output on return;
- * the caller zeroes state [2] (barrier count, error word) before each launch
- * and reads state[1] (0, or 6 when a barrier timed out) after it. */
+ * the caller zeroes state [kTgStepStateWords] (barrier count, error word,
+ * attention tasks finished per head) before each launch and reads state[1]
+ * after it (0, or 6 when a barrier timed out). */
 enum { kTgStepMaxTasks = 128 };     /* attention partials per KV head */
+enum { kTgStepStateWords = 2 + 128 };/* barrier count, error word, a task count per head */
 typedef struct {
     const float *ln1, *ln2, *wqkv, *bqkv, *wo, *w12, *w3, *router, *qb;
 } TGFwdStepLayer;
@@ -115,7 +117,6 @@ typedef struct {
     uint32_t n_layers, d, n_heads, n_kv_heads, head_dim, dff, ne, na, pos, max_seq;
     uint32_t sx_floats;             /* max(d, q_dim) */
     float scale;                    /* score scale: 1/sqrt(head_dim) times the YaRN mscale */
-    uint32_t prefetch;              /* 1: each phase's weight rows go to L2 a phase ahead */
 } TGFwdStepParams;
 int tgkv_fwd_step_supported(uint32_t d, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
                             uint32_t dff, uint32_t ne, uint32_t na);

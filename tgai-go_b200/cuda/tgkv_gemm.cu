@@ -9,20 +9,21 @@
 // The product is A_big.W_big + A_big.W_small + A_small.W_big; the dropped
 // A_small.W_small term is below 2^-22 of |a||w|, and the tf32 rounding the
 // tensor core applies to `small` costs about as much, so every product is
-// good to about 2^-21.  The three products are one K-concatenated pipeline:
-// k-block kb of segment 0, 1, 2 loads (A_small, W_big), (A_big, W_small),
-// (A_big, W_big).  The tensor core's fp32 accumulation truncates at every
-// step, relative to the accumulator's magnitude, so the two small terms go
-// first (while the accumulator is ~2^-11 of its final size) and the k-blocks
-// are dealt round-robin over all of TMEM (512 / BN accumulators), which the
-// epilogue adds in IEEE fp32: every accumulator sees a fraction of the steps
-// at a fraction of the magnitude.
+// good to about 2^-21.  One pipeline stage holds all four tiles of a k-block
+// (A_big, A_small, W_big, W_small), each loaded once, and the MMA thread
+// issues the three products from it.  The tensor core's fp32 accumulation
+// truncates at every step, relative to the accumulator's magnitude, so the
+// two small cross terms go to an accumulator of their own (about 2^-11 of
+// the result) and the big products are dealt round-robin over the rest of
+// TMEM (512 / BN - 1 accumulators); the epilogue adds them in IEEE fp32, so
+// every accumulator sees a fraction of the steps at a fraction of the
+// magnitude.
 //
 // One CTA (128 threads) per 128 x BN output tile.  Lane 0 of warp 0 moves
 // 128x32 (A) and BNx32 (W) fp32 tiles with 128-byte-swizzled tiled TMA into
 // a ring of stages (mbarrier completion); lane 0 of warp 1 issues
-// tcgen05.mma kind::tf32 (M = 128, N = BN, K = 8; four per k-block) into a
-// TMEM accumulator and releases each stage with tcgen05.commit; then all
+// tcgen05.mma kind::tf32 (M = 128, N = BN, K = 8; twelve per k-block) into
+// TMEM accumulators and releases each stage with tcgen05.commit; then all
 // four warps read their 32 TMEM lanes (rows) and store or accumulate the
 // output rows.  Rows past M and columns past N arrive as zeros (TMA bounds)
 // and are not stored.  Every wait is bounded (about 2 s): on expiry the
@@ -48,11 +49,14 @@ constexpr int kABytes = kBM * kBK * 4;        // 16 KB
 template <int BN>
 struct Cfg {
     static constexpr int BBytes = BN * kBK * 4;
-    static constexpr int Stage = kABytes + BBytes;
+    // a stage: A_big, A_small, W_big, W_small of one k-block
+    static constexpr int OffAs = kABytes, OffWb = 2 * kABytes, OffWs = 2 * kABytes + BBytes;
+    static constexpr int Stage = 2 * kABytes + 2 * BBytes;
     static constexpr int NStage = (196608 / Stage) > 8 ? 8 : (196608 / Stage);
     static constexpr int OffBar = NStage * Stage;
     static constexpr int Smem = OffBar + (2 * NStage + 2) * 8 + 16 + 1024;   // + alignment slack
-    static constexpr int NAcc = 512 / BN;              // accumulators: all 512 TMEM columns
+    static constexpr int NAcc = 512 / BN;              // accumulators: all 512 TMEM columns,
+    static constexpr int NBig = NAcc - 1;              //   the first for the cross terms
     static constexpr uint32_t TmemCols = 512;
 };
 
@@ -97,7 +101,7 @@ __global__ void __launch_bounds__(128, 1) gemm_tf32x3_kernel(const __grid_consta
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
     const int nkb = (int)((p.K + kBK - 1) / kBK);
-    const int total = 3 * nkb;
+    const int total = nkb;
 
     if (tid == 0) {
         for (int s = 0; s < C::NStage; ++s) {
@@ -142,13 +146,13 @@ __global__ void __launch_bounds__(128, 1) gemm_tf32x3_kernel(const __grid_consta
                 break;
             }
             if (*reinterpret_cast<volatile int*>(abort_flag)) break;
-            const int seg = kb / nkb;
-            const int kx = (kb - seg * nkb) * kBK;
+            const int kx = kb * kBK;
             unsigned char* st = smem + s * C::Stage;
             mbar_arrive_expect_tx(&full[s], (uint32_t)C::Stage);
-            tma_load_2d(st, seg == 0 ? &p.a_small : &p.a_big, kx, (int)(a_row0 + m0), &full[s]);
-            tma_load_2d(st + kABytes, seg == 1 ? &p.w_small : &p.w_big, kx, (int)(w_row0 + n0),
-                        &full[s]);
+            tma_load_2d(st, &p.a_big, kx, (int)(a_row0 + m0), &full[s]);
+            tma_load_2d(st + C::OffAs, &p.a_small, kx, (int)(a_row0 + m0), &full[s]);
+            tma_load_2d(st + C::OffWb, &p.w_big, kx, (int)(w_row0 + n0), &full[s]);
+            tma_load_2d(st + C::OffWs, &p.w_small, kx, (int)(w_row0 + n0), &full[s]);
             ++issued;
         }
         // the last stages' copies land before this thread may leave
@@ -166,14 +170,18 @@ __global__ void __launch_bounds__(128, 1) gemm_tf32x3_kernel(const __grid_consta
                 break;
             }
             tc_fence_after();
-            const uint32_t a = smem_addr(smem + s * C::Stage);
-            const uint32_t b = a + kABytes;
-            const uint32_t acc = tmem + (uint32_t)((kb % C::NAcc) * BN);
+            const uint32_t ab = smem_addr(smem + s * C::Stage);
+            const uint32_t as = ab + C::OffAs, wb = ab + C::OffWb, ws = ab + C::OffWs;
+            const uint32_t big = tmem + (uint32_t)((1 + kb % C::NBig) * BN);
 #pragma unroll
-            for (int k = 0; k < kBK / 8; ++k)          // K = 8 tf32 = 32 bytes per MMA
-                umma_tf32(acc, umma_desc_sw128(a + 32 * k, 16, 1024),
-                          umma_desc_sw128(b + 32 * k, 16, 1024), idesc,
-                          (kb >= C::NAcc) || (k > 0));
+            for (int k = 0; k < kBK / 8; ++k) {        // K = 8 tf32 = 32 bytes per MMA
+                const uint64_t dab = umma_desc_sw128(ab + 32 * k, 16, 1024);
+                const uint64_t dwb = umma_desc_sw128(wb + 32 * k, 16, 1024);
+                umma_tf32(tmem, umma_desc_sw128(as + 32 * k, 16, 1024), dwb, idesc,
+                          (kb > 0) || (k > 0));
+                umma_tf32(tmem, dab, umma_desc_sw128(ws + 32 * k, 16, 1024), idesc, 1u);
+                umma_tf32(big, dab, dwb, idesc, (kb >= C::NBig) || (k > 0));
+            }
             umma_commit(&empty[s]);                    // the stage is free once these are done
         }
         umma_commit(done);                             // every MMA issued so far is done
@@ -193,7 +201,7 @@ __global__ void __launch_bounds__(128, 1) gemm_tf32x3_kernel(const __grid_consta
                                          : a_row0 + row;
     float* orow = p.out + (uint64_t)orow_i * p.ldo;
     const bool vec = (p.ldo % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.out) & 15) == 0);
-    const int n_acc = total < C::NAcc ? total : C::NAcc;   // accumulators written
+    const int n_acc = 1 + (total < C::NBig ? total : C::NBig);   // accumulators written
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
         const uint32_t col0 = n0 + 32 * c;

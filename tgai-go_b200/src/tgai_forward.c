@@ -916,7 +916,7 @@ static int step_on(void) {
 static int run_step(TGFwdModel* m, Slot* s, uint32_t pos) {
     const TGFwdConfig* c = &m->c;
     void* st = s->stream;
-    const uint32_t state_n = 2;
+    const uint32_t state_n = kTgStepStateWords;
     if (!s->step_kvc) {
         float** h = (float**)malloc(c->n_layers * sizeof(float*));
         if (!h) { set_err("host allocation failed"); return 0; }
@@ -970,13 +970,6 @@ static int run_step(TGFwdModel* m, Slot* s, uint32_t pos) {
     p.max_seq = c->max_seq_len;
     p.sx_floats = c->d_model > m->q_dim ? c->d_model : m->q_dim;
     p.scale = 1.0f / sqrtf((float)m->hd);
-    {   /* L2 prefetch of the next phase's weights: TGKV_STEP_PREFETCH=1 (off by
-         * default: 612 tok/s with it against 655 without on the V2.7-shaped model;
-         * the phases are bound by their dependent round trips and the barriers,
-         * and the early streams only queue ahead of the current phase's loads) */
-        const char* pe = getenv("TGKV_STEP_PREFETCH");
-        p.prefetch = pe && pe[0] == '1';
-    }
     const int e = tgkv_fwd_decode_step(&p, st);
     if (e < 0) {
         __atomic_store_n(&m->step_refused, 1, __ATOMIC_RELAXED);
