@@ -15,6 +15,9 @@
 //   P4  RMSNorm(x), router + top-k (every CTA, same arithmetic as the
 //       engine's), routed experts' W1/W2 rows + SiLU (or the dense FFN's);
 //   P5  routed experts' W3 rows, k-ordered sum + residual (or dense W3).
+// Before each barrier a warp loads the first column block of its first rows
+// of the next phase into registers where they are known (all but the routed
+// experts' W1/W2), so those loads stream while the grid waits.
 // Every barrier is bounded: a CTA that waits more than ~1 s sets the error
 // word and the grid leaves at the next barrier, so a broken run returns a
 // status instead of hanging the GPU.  Data written inside the launch (x, q,
@@ -121,24 +124,32 @@ __device__ __forceinline__ void stage(float* dst, const float* src, const float*
     __syncthreads();
 }
 
-// acc[n] = W_n . x_n over K columns (x_n in shared memory), NW rows of one
-// warp; the 16-byte loads of kU column blocks of every row are issued before
-// any product.  All lanes hold the sums.
+// The column block [i0, i0 + kU * 128) of NW rows into registers: lane l
+// loads float4 l, l + 32, ... of it (zeros past K).
 template <int NW, int kU>
-__device__ __forceinline__ void dots(const float* const (&w)[NW], const float* const (&x)[NW],
-                                     uint32_t K, float (&acc)[NW]) {
+__device__ __forceinline__ void load_block(float4 (&a4)[NW][kU], const float* const (&w)[NW],
+                                           uint32_t K, uint32_t i0) {
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+#pragma unroll
+        for (int n = 0; n < NW; ++n)
+            a4[n][u] = i0 + u * 128 < K ? __ldg(reinterpret_cast<const float4*>(w[n] + i0 + u * 128))
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// acc[n] = W_n . x_n over K columns (x_n in shared memory), NW rows of one
+// warp, with the rows' first column block already in a4 (load_block at
+// lane * 4, issued earlier -- before a grid barrier, so that it streams
+// while the grid waits); each later block's loads are all issued before its
+// products.  All lanes hold the sums.
+template <int NW, int kU>
+__device__ __forceinline__ void dots_from(float4 (&a4)[NW][kU], const float* const (&w)[NW],
+                                          const float* const (&x)[NW], uint32_t K,
+                                          float (&acc)[NW]) {
     const uint32_t lane = threadIdx.x & 31;
 #pragma unroll
     for (int n = 0; n < NW; ++n) acc[n] = 0.f;
-    for (uint32_t i0 = lane * 4; i0 < K; i0 += kU * 128) {
-        float4 a4[NW][kU];
-#pragma unroll
-        for (int u = 0; u < kU; ++u)
-#pragma unroll
-            for (int n = 0; n < NW; ++n)
-                a4[n][u] = i0 + u * 128 < K
-                               ? __ldg(reinterpret_cast<const float4*>(w[n] + i0 + u * 128))
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t i0 = lane * 4; i0 < K;) {
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
             if (i0 + u * 128 >= K) break;
@@ -146,6 +157,8 @@ __device__ __forceinline__ void dots(const float* const (&w)[NW], const float* c
             for (int n = 0; n < NW; ++n)
                 acc[n] = dot4(a4[n][u], *reinterpret_cast<const float4*>(x[n] + i0 + u * 128), acc[n]);
         }
+        i0 += kU * 128;
+        if (i0 < K) load_block<NW, kU>(a4, w, K, i0);
     }
 #pragma unroll
     for (int n = 0; n < NW; ++n) acc[n] = warp_sum(acc[n]);
@@ -341,6 +354,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
     n_tasks = (L + ch - 1) / ch;
     const uint32_t half = hd >> 1;
     const uint32_t npair = (q_dim + 2 * kv_dim) / 2;
+    // The first column block of the warp's first rows of the next phase,
+    // loaded before the grid barrier that precedes it (pf_for: which phase
+    // it is for; 0: none): Q/K/V pair, out-projection row, router row, W3
+    // rows of the first two experts (or the dense W3 row).
+    enum { kPfNone = 0, kPfQkv, kPfWo, kPfRouter, kPfW3 };
+    // Every task loads its rows through pf too, and every prefetch point
+    // writes it (zeros where the warp has no such row), so that it is the
+    // one block of row registers of the kernel and dead during the attention.
+    float4 pf[2][12];
+    float4 (&pf1)[1][12] = reinterpret_cast<float4 (&)[1][12]>(pf);
+    int pf_for;
+    const uint32_t lane4 = lane * 4;
+    {
+        const float* r0 = p.layers[0].wqkv + (uint64_t)(2 * (gw < npair ? gw : 0)) * d;
+        load_block<2, 12>(pf, {r0, r0 + d}, gw < npair ? d : 0, lane4);
+        pf_for = gw < npair ? kPfQkv : kPfNone;
+    }
 
     for (uint32_t l = 0; l < p.n_layers; ++l) {
         const TGFwdStepLayer W = p.layers[l];
@@ -349,8 +379,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
         stage(sx, p.x, W.ln1, d, red);
         for (uint32_t mp = gw; mp < npair; mp += tw) {
             const uint32_t n0 = 2 * mp;
+            const float* r0 = W.wqkv + (uint64_t)n0 * d;
             float a[2];
-            dots<2, 12>({W.wqkv + (uint64_t)n0 * d, W.wqkv + (uint64_t)(n0 + 1) * d}, {sx, sx}, d, a);
+            if (!(mp == gw && pf_for == kPfQkv)) load_block<2, 12>(pf, {r0, r0 + d}, d, lane4);
+            dots_from<2, 12>(pf, {r0, r0 + d}, {sx, sx}, d, a);
             if (lane == 0) {
                 float v0 = a[0], v1 = a[1];
                 if (W.bqkv) {
@@ -394,21 +426,33 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
                 if (lane == 0) head_ctr[h] = 0;      // counted again only a layer later
             }
         }
+        load_block<1, 12>(pf1, {W.wo + (uint64_t)(gw < d ? gw : 0) * q_dim}, gw < d ? q_dim : 0,
+                          lane4);
+        pf_for = gw < d ? kPfWo : kPfNone;
         if (!grid_sync(bar, target, err, &s_ok)) return;
         // ---- P3: the merged heads into sx, then out projection + residual
         stage(sx, p.attn, nullptr, q_dim, red);
         for (uint32_t n = gw; n < d; n += tw) {
+            const float* r = W.wo + (uint64_t)n * q_dim;
             float a[1];
-            dots<1, 12>({W.wo + (uint64_t)n * q_dim}, {sx}, q_dim, a);
+            if (!(n == gw && pf_for == kPfWo)) load_block<1, 12>(pf1, {r}, q_dim, lane4);
+            dots_from<1, 12>(pf1, {r}, {sx}, q_dim, a);
             if (lane == 0) p.x[n] = __ldcg(p.x + n) + a[0];
+        }
+        {
+            const bool r = ne && warp < ne;
+            load_block<1, 12>(pf1, {W.router + (uint64_t)(r ? warp : 0) * d}, r ? d : 0, lane4);
+            pf_for = r ? kPfRouter : kPfNone;
         }
         if (!grid_sync(bar, target, err, &s_ok)) return;
         // ---- P4: norm, router + top-k (every CTA), expert W1/W2 rows + SiLU
         stage(sx, p.x, W.ln2, d, red);
         if (ne) {
             for (uint32_t e = warp; e < ne; e += kWarps) {
+                const float* r = W.router + (uint64_t)e * d;
                 float a[1];
-                dots<1, 12>({W.router + (uint64_t)e * d}, {sx}, d, a);
+                if (!(e == warp && pf_for == kPfRouter)) load_block<1, 12>(pf1, {r}, d, lane4);
+                dots_from<1, 12>(pf1, {r}, {sx}, d, a);
                 if (lane == 0) slog[e] = W.qb ? a[0] + W.qb[e] : a[0];
             }
             __syncthreads();
@@ -421,17 +465,34 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
                 if (e >= 0 && (uint32_t)e < ne) {
                     const float* wa = W.w12 + ((uint64_t)e * 2 * dff + j) * d;
                     float a[2];
-                    dots<2, 12>({wa, wa + (uint64_t)dff * d}, {sx, sx}, d, a);
+                    load_block<2, 12>(pf, {wa, wa + (uint64_t)dff * d}, d, lane4);
+                    dots_from<2, 12>(pf, {wa, wa + (uint64_t)dff * d}, {sx, sx}, d, a);
                     hv = silu_mul(a[0], a[1]);
                 }
                 if (lane == 0) p.h[(uint64_t)k * dff + j] = hv;
             }
         } else {
             for (uint32_t j = gw; j < dff; j += tw) {
+                const float* r0 = W.w12 + (uint64_t)j * d;
+                const float* r1 = W.w12 + (uint64_t)(dff + j) * d;
                 float a[2];
-                dots<2, 12>({W.w12 + (uint64_t)j * d, W.w12 + (uint64_t)(dff + j) * d}, {sx, sx}, d, a);
+                load_block<2, 12>(pf, {r0, r1}, d, lane4);
+                dots_from<2, 12>(pf, {r0, r1}, {sx, sx}, d, a);
                 if (lane == 0) p.h[j] = silu_mul(fminf(fmaxf(a[0], -88.0f), 88.0f), a[1]);
             }
+        }
+        {
+            // dense: the W3 row of output gw; experts: the rows of output gw
+            // of the first two experts when both are routed
+            const bool two = ne && na > 1 && s_ids[0] >= 0 && (uint32_t)s_ids[0] < ne &&
+                             s_ids[1] >= 0 && (uint32_t)s_ids[1] < ne;
+            const bool on = gw < d && (!ne || two);
+            const uint32_t i = on ? gw : 0;
+            const float* r0 = ne ? W.w3 + ((uint64_t)(two ? s_ids[0] : 0) * d + i) * dff
+                                 : W.w3 + (uint64_t)i * dff;
+            const float* r1 = ne ? W.w3 + ((uint64_t)(two ? s_ids[1] : 0) * d + i) * dff : r0;
+            load_block<2, 12>(pf, {r0, ne ? r1 : r0}, on ? dff : 0, lane4);
+            pf_for = on ? kPfW3 : kPfNone;
         }
         if (!grid_sync(bar, target, err, &s_ok)) return;
         // ---- P5: W3 rows, k-ordered weighted sum (or dense W3) + residual
@@ -446,25 +507,37 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
                     const float* w0 = W.w3 + ((uint64_t)(v0 ? e0 : 0) * d + i) * dff;
                     float a0 = 0.f, a1 = 0.f;
                     if (v1) {
+                        const float* w1 = W.w3 + ((uint64_t)e1 * d + i) * dff;
                         float a[2];
-                        dots<2, 12>({w0, W.w3 + ((uint64_t)e1 * d + i) * dff},
-                                    {sh + (uint64_t)k * dff, sh + (uint64_t)(k + 1) * dff}, dff, a);
+                        if (!(k == 0 && i == gw && pf_for == kPfW3))
+                            load_block<2, 12>(pf, {w0, w1}, dff, lane4);
+                        dots_from<2, 12>(pf, {w0, w1},
+                                         {sh + (uint64_t)k * dff, sh + (uint64_t)(k + 1) * dff}, dff, a);
                         a0 = a[0];
                         a1 = a[1];
                     } else if (v0) {
                         float a[1];
-                        dots<1, 12>({w0}, {sh + (uint64_t)k * dff}, dff, a);
+                        load_block<1, 12>(pf1, {w0}, dff, lane4);
+                        dots_from<1, 12>(pf1, {w0}, {sh + (uint64_t)k * dff}, dff, a);
                         a0 = a[0];
                     }
                     if (v0) ot = fmaf(s_w[k], a0, ot);
                     if (v1) ot = fmaf(s_w[k + 1], a1, ot);
                 }
             } else {
+                const float* r = W.w3 + (uint64_t)i * dff;
                 float a[1];
-                dots<1, 12>({W.w3 + (uint64_t)i * dff}, {sh}, dff, a);
+                if (!(i == gw && pf_for == kPfW3)) load_block<1, 12>(pf1, {r}, dff, lane4);
+                dots_from<1, 12>(pf1, {r}, {sh}, dff, a);
                 ot = a[0];
             }
             if (lane == 0) p.x[i] = __ldcg(p.x + i) + ot;
+        }
+        {
+            const bool on = l + 1 < p.n_layers && gw < npair;
+            const float* r0 = p.layers[on ? l + 1 : l].wqkv + (uint64_t)(2 * (on ? gw : 0)) * d;
+            load_block<2, 12>(pf, {r0, r0 + d}, on ? d : 0, lane4);
+            pf_for = on ? kPfQkv : kPfNone;
         }
         if (!grid_sync(bar, target, err, &s_ok)) return;
     }
