@@ -124,16 +124,33 @@ __device__ __forceinline__ void stage(float* dst, const float* src, const float*
     __syncthreads();
 }
 
+// A weight load: read-only path, not kept in L1, and marked first to leave
+// L2 (every weight is read once per token, 3.4 GB on the V2.7-shaped model,
+// while the K/V rows, activations and partials should stay there).
+__device__ __forceinline__ float4 ld_weight(const float* p, uint64_t policy) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p), "l"(policy));
+    return v;
+}
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
 // The column block [i0, i0 + kU * 128) of NW rows into registers: lane l
 // loads float4 l, l + 32, ... of it (zeros past K).
 template <int NW, int kU>
 __device__ __forceinline__ void load_block(float4 (&a4)[NW][kU], const float* const (&w)[NW],
                                            uint32_t K, uint32_t i0) {
+    const uint64_t pol = evict_first_policy();
 #pragma unroll
     for (int u = 0; u < kU; ++u)
 #pragma unroll
         for (int n = 0; n < NW; ++n)
-            a4[n][u] = i0 + u * 128 < K ? __ldg(reinterpret_cast<const float4*>(w[n] + i0 + u * 128))
+            a4[n][u] = i0 + u * 128 < K ? ld_weight(w[n] + i0 + u * 128, pol)
                                         : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
@@ -338,7 +355,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
     const uint32_t d = p.d, hd = p.head_dim, nkv = p.n_kv_heads;
     const uint32_t q_dim = nkv * G * hd, kv_dim = nkv * hd, dff = p.dff, ne = p.ne, na = p.na;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t gw = blockIdx.x * kWarps + warp, tw = gridDim.x * kWarps;
+    // warp tasks go round the CTAs first (task t to CTA t % grid), so that
+    // a phase with fewer tasks than warps still keeps every SM loading
+    const uint32_t gw = blockIdx.x + gridDim.x * warp, tw = gridDim.x * kWarps;
     float* sx = smem;                     // [max(d, q_dim)]
     float* sh = smem + p.sx_floats;       // [na or 1][dff]
     uint32_t* bar = p.state;
@@ -409,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const TGFwdSte
         // ---- P2: split attention, partials per (query head, position
         // range), one task per CTA before any CTA takes a second; the task
         // that finishes a head last merges it into attn
-        for (uint32_t t = blockIdx.x + gridDim.x * warp; t < nkv * G * n_tasks; t += tw) {
+        for (uint32_t t = gw; t < nkv * G * n_tasks; t += tw) {
             const uint32_t h = t / n_tasks, task = t % n_tasks;
             const uint32_t pb = task * ch, pe = pb + ch < L ? pb + ch : L;
             attn_task(p, kvc, h, h / G, task, pb, pe);
