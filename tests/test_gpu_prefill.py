@@ -88,14 +88,17 @@ def test_prefill_with_temperature(cuda, devbuf):
     (1, 128, 12, 4, 64),     # group of 3
 ])
 def test_ineligible_calls_stay_on_split_kernel(cuda, devbuf, dtype, hd, nh, nkv, nq):
-    """Not for the suffix kernel: the split-sequence kernel takes them (these
-    launches are far below the tensor-core decode kernel's size threshold)."""
+    """Not for the suffix kernel: a split-sequence kernel takes them -- the
+    CUDA-core one, or for the group of 3 (64 rows x ~270 positions x 12 head
+    subsets, about 206K streamed rows, above the 131072-row threshold) the
+    tensor-core decode kernel."""
     lib = cuda
     L = 300
     q, k, v = synth_qkv(99 + nh + hd, L, nh, nkv, hd)
     c = make_cache(lib, devbuf, L, nkv, hd, dtype, k, v)
     got = attend(lib, devbuf, c, q[-nq:], nh, nq)
-    assert lib.tg_cuda_kv_attn_last_kernel() == SPLIT
+    want = DECODE_TC if (dtype, hd, nh // nkv) == (1, 128, 3) else SPLIT
+    assert lib.tg_cuda_kv_attn_last_kernel() == want
     kvc = host_cache(lib, c, dtype, L, nkv * hd)
     eng = O.attention_engine(q[-nq:], kvc, nh, nkv, hd, nq, L - nq, L, L)
     assert rel_head_err(got, eng) < 1e-5

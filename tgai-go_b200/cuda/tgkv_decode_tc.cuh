@@ -183,7 +183,11 @@ attention_tc_kernel(const __grid_constant__ TGKvAttnParams p) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
-    // Programmatic dependent launch: nothing above reads global memory.
+    // A one-cache launch's tensor map was written when the cache was made:
+    // its descriptor is fetched while the previous kernel finishes.
+    if (!p.caches && warp == kTmaWarp && lane == 0 && p.cache0.tmap_sw) prefetch_tmap(p.cache0.tmap_sw);
+    // Programmatic dependent launch: nothing above reads global memory
+    // written by the previous kernels.
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (warp == kTmaWarp) {

@@ -224,7 +224,9 @@ __device__ __noinline__ void combine_segment(const TGKvAttnParams& p, uint32_t f
                                              int tid, int lane, int warp, uint32_t out_slot) {
     constexpr int NV = GT * HD / 4;            // float4 per partial output
     constexpr int G = 128 / NV;                // groups of threads over the partials
-    constexpr int kB = 16;                     // partials per thread and step
+    constexpr int kB = HD > 128 ? 16 : 24;     // partials per thread and step (24: a
+                                               // segment of up to 24 chunks merges in one
+                                               // round trip of loads)
     constexpr int kMl = 8;                     // (m, l) pairs per thread and step
     static_assert(NV <= 128 && 128 % NV == 0, "partial vectors");
     const int v = tid % NV, g = tid / NV;
@@ -420,8 +422,14 @@ attention_kernel(const __grid_constant__ TGKvAttnParams p) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
+    // A one-cache launch's tensor map was written when the cache was made (or
+    // sits in the parameters): its descriptor is fetched while the previous
+    // kernel finishes.
+    if (!p.caches && warp == kConsumerWarps && lane == 0)
+        prefetch_tmap(p.cache0.tmap ? p.cache0.tmap : reinterpret_cast<uint64_t>(&p.tmap0));
     // Programmatic dependent launch: everything above overlaps the previous
-    // kernel on the stream; nothing below reads global memory before it is done.
+    // kernel on the stream; nothing below reads global memory written by the
+    // previous kernels before they are done.
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (warp == kConsumerWarps) {
