@@ -171,7 +171,8 @@ uint32_t tg_cuda_kv_attn_last_launches(void);
  * 0 none, 1 split-sequence on CUDA cores (tgkv_kernels.cu), 2 tensor-core
  * suffix (tgkv_prefill.cu), 3 tensor-core split-sequence decode
  * (tgkv_decode_tc.cuh; bf16 head_dim-128 caches, TGKV_DECODE_TC=0 turns it
- * off). */
+ * off), 4 causal block of query rows over an fp32 cache on CUDA cores
+ * (tgkv_prefill_f32.cu; TGKV_PREFILL=0 turns it off). */
 int tg_cuda_kv_attn_last_kernel(void);
 /* CTAs per row block (KV split) of the last tensor-core suffix launch. */
 uint32_t tg_cuda_kv_attn_last_split(void);

@@ -19,7 +19,7 @@ from test_gpu_parity import attend, host_cache, make_cache, synth_qkv
 
 pytestmark = pytest.mark.gpu
 
-SPLIT, TENSOR, DECODE_TC = 1, 2, 3    # tg_cuda_kv_attn_last_kernel() families
+SPLIT, TENSOR, DECODE_TC, BLOCK32 = 1, 2, 3, 4   # tg_cuda_kv_attn_last_kernel() families
 BF16_TOL = 1e-2            # the bf16-cache tolerance of the path
 # TC_TOL: emulating the hi + lo split exactly on the CPU gives 6.5e-6 on the
 # cfg3 shape; the tensor cores' fp32 accumulation adds about as much again.
@@ -91,13 +91,15 @@ def test_ineligible_calls_stay_on_split_kernel(cuda, devbuf, dtype, hd, nh, nkv,
     """Not for the suffix kernel: a split-sequence kernel takes them -- the
     CUDA-core one, or for the group of 3 (64 rows x ~270 positions x 12 head
     subsets, about 206K streamed rows, above the 131072-row threshold) the
-    tensor-core decode kernel."""
+    tensor-core decode kernel -- except the fp32 cache, whose block of rows
+    goes to the fp32 block kernel (tgkv_prefill_f32.cu)."""
     lib = cuda
     L = 300
     q, k, v = synth_qkv(99 + nh + hd, L, nh, nkv, hd)
     c = make_cache(lib, devbuf, L, nkv, hd, dtype, k, v)
     got = attend(lib, devbuf, c, q[-nq:], nh, nq)
-    want = DECODE_TC if (dtype, hd, nh // nkv) == (1, 128, 3) else SPLIT
+    want = (BLOCK32 if dtype == 0 else
+            DECODE_TC if (dtype, hd, nh // nkv) == (1, 128, 3) else SPLIT)
     assert lib.tg_cuda_kv_attn_last_kernel() == want
     kvc = host_cache(lib, c, dtype, L, nkv * hd)
     eng = O.attention_engine(q[-nq:], kvc, nh, nkv, hd, nq, L - nq, L, L)

@@ -642,10 +642,36 @@ static uint32_t prefill_split(const TGCudaAttnCall* c, uint32_t pos0) {
 
 int tg_cuda_kv_attn_fuses_suffix(const TGCudaAttnCall* c) { return use_prefill(c); }
 
+/* Blocks of query rows over one fp32 cache (the forward's prefill: its caches
+ * are fp32 like the engine's) go to the CUDA-core block kernel
+ * (tgkv_prefill_f32.cu) when there are at least 32 (row, head) pairs:
+ * consecutive positions, head_dim 32/64/128, group 1/2/3/4/8, no fused
+ * append, no gather, q and out 16-byte aligned.  The split-sequence kernel
+ * would run one query row per item: a 512-token prefill of the V2.7-shaped
+ * model took 150 us a layer there.  TGKV_PREFILL=0 keeps them on it. */
+static int use_prefill_f32(const TGCudaAttnCall* c) {
+    const char* e = getenv("TGKV_PREFILL");
+    if (e && e[0] == '0') return 0;
+    if (!c || !c->n_kv_heads || !c->n_heads || c->n_heads % c->n_kv_heads || !c->n_pos ||
+        !c->n_items || c->n_pos[0] == 0)
+        return 0;
+    if (c->dtype != 0 || c->table_dev || !c->cache.base || c->k_new || c->v_new ||
+        c->gather_world)
+        return 0;
+    const uint32_t g = c->n_heads / c->n_kv_heads;
+    if (!tgkv_prefill_f32_supported(c->head_dim, g)) return 0;
+    if ((uint64_t)c->n_items * g < 32) return 0;
+    if (((uintptr_t)c->q | (uintptr_t)c->out) & 15u) return 0;
+    if ((uint64_t)c->n_pos[0] - 1 + c->n_items > c->cache.max_seq) return 0;
+    for (uint32_t i = 1; i < c->n_items; i++)
+        if (c->n_pos[i] != c->n_pos[0] + i) return 0;
+    return 1;
+}
+
 /* Calls that go to the tensor-core kernel need no split scratch: one token
  * byte and one counter keep the caller's sizing logic uniform. */
 uint64_t tg_cuda_kv_attn_scratch_bytes(const TGCudaAttnCall* c) {
-    if (use_prefill(c)) return 256;
+    if (use_prefill(c) || use_prefill_f32(c)) return 256;
     AttnPlan pl;
     if (!plan_attention(c, &pl)) return 0;
     return part_o_bytes(&pl, c->head_dim) + part_slots(&pl) * pl.gt * 2 * 4;
@@ -655,7 +681,7 @@ uint64_t tg_cuda_kv_attn_scratch_bytes(const TGCudaAttnCall* c) {
  * one tile queue per segment after them; the two-level merge one counter
  * per chunk group after those. */
 uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c) {
-    if (use_prefill(c)) return 1;
+    if (use_prefill(c) || use_prefill_f32(c)) return 1;
     AttnPlan pl;
     if (!plan_attention(c, &pl)) return 0;
     return (uint64_t)c->n_items * c->n_kv_heads * pl.n_sub * (pl.tc ? 2u : 1u) +
@@ -665,7 +691,7 @@ uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c) {
 /* Segments of the call: (item, KV head, head subset) triples, each finished
  * (and, with a gather, signalled) once. */
 uint64_t tg_cuda_kv_attn_segments(const TGCudaAttnCall* c) {
-    if (use_prefill(c)) return 0;
+    if (use_prefill(c) || use_prefill_f32(c)) return 0;
     AttnPlan pl;
     if (!plan_attention(c, &pl)) return 0;
     return (uint64_t)c->n_items * c->n_kv_heads * pl.n_sub;
@@ -690,10 +716,12 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
     t_last_kernel = 0;
     t_last_split = 0;
     if (!g_ready && !tg_cuda_kv_init()) return 0;
-    /* the tensor-core route needs none of the split planning */
+    /* the tensor-core suffix and the fp32 block routes need none of the
+     * split planning */
     const int prefill = use_prefill(c);
+    const int block32 = !prefill && use_prefill_f32(c);
     AttnPlan pl;
-    if (!prefill && !plan_attention(c, &pl)) return 0;
+    if (!prefill && !block32 && !plan_attention(c, &pl)) return 0;
     if (c->n_items == 0) return 1;
     if (!c->q || !c->out || (!c->table_dev && (!c->cache.base || !c->cache.tmap))) {
         set_err("attention: NULL pointer");
@@ -743,6 +771,24 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         if (!launch_rc(tgkv_launch_prefill(&pp, stream), "prefill kernel")) return 0;
         t_last_launches = 1;
         t_last_kernel = 2;
+        return 1;
+    }
+    if (block32) {
+        TGKvPrefillF32Params pp;
+        memset(&pp, 0, sizeof(pp));
+        pp.q = c->q;
+        pp.out = c->out;
+        pp.kv = (const float*)(uintptr_t)c->cache.base;
+        pp.n_q = c->n_items;
+        pp.n_heads = c->n_heads;
+        pp.n_kv_heads = c->n_kv_heads;
+        pp.head_dim = c->head_dim;
+        pp.max_seq = c->cache.max_seq;
+        pp.pos0 = c->n_pos[0] - 1;
+        pp.qscale = c->scale * 1.4426950408889634f;
+        if (!launch_rc(tgkv_launch_prefill_f32(&pp, stream), "fp32 block kernel")) return 0;
+        t_last_launches = 1;
+        t_last_kernel = 4;
         return 1;
     }
     if (!c->scratch || !c->counters) {

@@ -147,8 +147,23 @@ typedef struct {
     uint32_t     max_seq;
 } TGKvPrefillParams;
 
-/* Launchers (tgkv_kernels.cu, tgkv_prefill.cu).  Return 0 on success, else a
- * cudaError_t. */
+/* Causal attention of n_q consecutive query rows over one fp32 cache on the
+ * CUDA cores (tgkv_prefill_f32.cu): row r at position pos0 + r attends
+ * positions [0, pos0 + r] of kv ([2][max_seq][n_kv_heads * head_dim]).  q and
+ * out: [n_q][n_heads][head_dim], 16-byte aligned.  head_dim 32/64/128, group
+ * n_heads / n_kv_heads 1, 2, 3, 4 or 8. */
+typedef struct {
+    const float* q;
+    float*       out;
+    const float* kv;
+    uint32_t n_q, n_heads, n_kv_heads, head_dim, max_seq, pos0;
+    float    qscale;             /* softmax scale * log2(e) */
+} TGKvPrefillF32Params;
+
+/* Launchers (tgkv_kernels.cu, tgkv_prefill.cu, tgkv_prefill_f32.cu).  Return 0
+ * on success, else a cudaError_t. */
+int tgkv_launch_prefill_f32(const TGKvPrefillF32Params* p, void* stream);
+int tgkv_prefill_f32_supported(uint32_t head_dim, uint32_t group);
 int tgkv_launch_prefill(const TGKvPrefillParams* p, void* stream);
 /* Clusters of n_split prefill CTAs resident at once on the current device. */
 uint32_t tgkv_prefill_max_clusters(uint32_t n_split);
