@@ -2,13 +2,14 @@
 
 Blocks of at least 32 (query row, head) pairs over one fp32 cache -- the
 whole-model forward's prefill, whose caches are fp32 like the engine's -- run
-on a CUDA-core kernel that stages 32 query vectors per CTA and walks the K/V
-tiles up to the block's causal limit.  Checked against the engine-order
+on a CUDA-core kernel that stages a row block of up to 64 query vectors and
+deals its K/V tiles (up to the block's causal limit) to splits that one CTA
+each streams, the last split to finish merging them.  Checked against the engine-order
 oracle (src/tgai_engine.c:3943-4011 semantics) at the split-sequence kernel's
 fp32 bar, for every group size and head_dim the kernel takes, row counts that
-are not multiples of a CTA's rows, a fresh prefill from position 0, a
-continuation far into the context, stale rows past the length, and against
-the split-sequence kernel (TGKV_PREFILL=0) on the same call.
+are not multiples of a block's rows, one split and many, a fresh prefill from
+position 0, a continuation far into the context, stale rows past the length,
+and against the split-sequence kernel (TGKV_PREFILL=0) on the same call.
 """
 import numpy as np
 import pytest
@@ -31,6 +32,7 @@ F32_TOL = 1e-5                 # the fp32 split-sequence kernel's bar
     (64, 8, 8, 100, 37),        # G = 1, rows not a multiple of the CTA's 32
     (32, 16, 2, 1000, 40),      # G = 8: 4 rows a CTA
     (128, 8, 4, 2048, 33),      # G = 2, far into the context, a last block of one row
+    (32, 16, 2, 40, 40),        # two tiles in all: one split, rows written directly
 ])
 def test_block_matches_oracle(cuda, devbuf, hd, nh, nkv, L, nq):
     lib = cuda

@@ -668,10 +668,31 @@ static int use_prefill_f32(const TGCudaAttnCall* c) {
     return 1;
 }
 
-/* Calls that go to the tensor-core kernel need no split scratch: one token
- * byte and one counter keep the caller's sizing logic uniform. */
+/* The fp32 block kernel's plan: row blocks, tiles per split, splits of the
+ * longest block; its partials (floats) and counters. */
+typedef struct {
+    uint32_t n_blocks, tps, n_split;
+    uint64_t part_floats, ctrs;
+} Block32Plan;
+static Block32Plan plan_block32(const TGCudaAttnCall* c) {
+    Block32Plan b;
+    tgkv_prefill_f32_plan(c->n_items, c->n_pos[0] - 1, c->n_heads / c->n_kv_heads,
+                          c->n_kv_heads, (uint32_t)(g_sm_count ? g_sm_count : 148), &b.n_blocks,
+                          &b.tps, &b.n_split);
+    b.ctrs = (uint64_t)c->n_kv_heads * b.n_blocks;
+    b.part_floats = b.n_split > 1 ? b.ctrs * b.n_split * 64u * (c->head_dim + 4u) : 0;
+    return b;
+}
+
+/* Calls that go to the tensor-core suffix kernel need no split scratch: one
+ * token byte and one counter keep the caller's sizing logic uniform; the fp32
+ * block kernel needs its split partials and a counter per row block. */
 uint64_t tg_cuda_kv_attn_scratch_bytes(const TGCudaAttnCall* c) {
-    if (use_prefill(c) || use_prefill_f32(c)) return 256;
+    if (use_prefill(c)) return 256;
+    if (use_prefill_f32(c)) {
+        const Block32Plan b = plan_block32(c);
+        return b.part_floats ? b.part_floats * 4 : 256;
+    }
     AttnPlan pl;
     if (!plan_attention(c, &pl)) return 0;
     return part_o_bytes(&pl, c->head_dim) + part_slots(&pl) * pl.gt * 2 * 4;
@@ -681,7 +702,8 @@ uint64_t tg_cuda_kv_attn_scratch_bytes(const TGCudaAttnCall* c) {
  * one tile queue per segment after them; the two-level merge one counter
  * per chunk group after those. */
 uint64_t tg_cuda_kv_attn_counters(const TGCudaAttnCall* c) {
-    if (use_prefill(c) || use_prefill_f32(c)) return 1;
+    if (use_prefill(c)) return 1;
+    if (use_prefill_f32(c)) return plan_block32(c).ctrs;
     AttnPlan pl;
     if (!plan_attention(c, &pl)) return 0;
     return (uint64_t)c->n_items * c->n_kv_heads * pl.n_sub * (pl.tc ? 2u : 1u) +
@@ -774,8 +796,18 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         return 1;
     }
     if (block32) {
+        const Block32Plan bp = plan_block32(c);
+        if (bp.n_split > 1 && (!c->scratch || !c->counters)) {
+            set_err("attention: fp32 block scratch not provided");
+            return 0;
+        }
         TGKvPrefillF32Params pp;
         memset(&pp, 0, sizeof(pp));
+        pp.part = (float*)c->scratch;
+        pp.ctr = c->counters;
+        pp.n_blocks = bp.n_blocks;
+        pp.tps = bp.tps;
+        pp.n_split = bp.n_split;
         pp.q = c->q;
         pp.out = c->out;
         pp.kv = (const float*)(uintptr_t)c->cache.base;
@@ -789,6 +821,7 @@ int tg_cuda_kv_attention(const TGCudaAttnCall* c, void* stream) {
         if (!launch_rc(tgkv_launch_prefill_f32(&pp, stream), "fp32 block kernel")) return 0;
         t_last_launches = 1;
         t_last_kernel = 4;
+        t_last_split = bp.n_split;
         return 1;
     }
     if (!c->scratch || !c->counters) {

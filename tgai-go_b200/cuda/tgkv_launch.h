@@ -151,14 +151,24 @@ typedef struct {
  * CUDA cores (tgkv_prefill_f32.cu): row r at position pos0 + r attends
  * positions [0, pos0 + r] of kv ([2][max_seq][n_kv_heads * head_dim]).  q and
  * out: [n_q][n_heads][head_dim], 16-byte aligned.  head_dim 32/64/128, group
- * n_heads / n_kv_heads 1, 2, 3, 4 or 8. */
+ * n_heads / n_kv_heads 1, 2, 3, 4 or 8.  Row blocks of 64 / group rows; a
+ * block's K/V tiles are dealt to splits of tps tiles (tgkv_prefill_f32_plan);
+ * with more than one split, part holds n_kv_heads * n_blocks * n_split
+ * partials of 64 vectors x (head_dim + 4) floats and ctr one zeroed counter
+ * per (KV head, block), returned to zero by the kernel. */
 typedef struct {
     const float* q;
     float*       out;
     const float* kv;
+    float*       part;
+    uint32_t*    ctr;
     uint32_t n_q, n_heads, n_kv_heads, head_dim, max_seq, pos0;
     float    qscale;             /* softmax scale * log2(e) */
+    uint32_t n_blocks, tps, n_split;
 } TGKvPrefillF32Params;
+void tgkv_prefill_f32_plan(uint32_t n_q, uint32_t pos0, uint32_t group, uint32_t n_kv_heads,
+                           uint32_t sm_count, uint32_t* n_blocks, uint32_t* tps,
+                           uint32_t* n_split);
 
 /* Launchers (tgkv_kernels.cu, tgkv_prefill.cu, tgkv_prefill_f32.cu).  Return 0
  * on success, else a cudaError_t. */
