@@ -1,8 +1,9 @@
 """Generate the golden vectors in tests/golden/ from the reference's own code.
 
-Runs only where the reference checkout exists (REF, default /root/reference)
-and oracle/_ref/ has been built (`make -C oracle ref`); the GPU box never runs
-this, it only reads the committed .npz files.
+Runs only where the reference checkout exists (the REF environment variable
+names it; the default is the build container's checkout) and oracle/_ref/ has
+been built (`make -C oracle ref`); the GPU box never runs this, it only reads
+the committed .npz files.
 
   engine_pins.npz    tg_dot / softmax / rope of src/tgai_engine.c on seeded
                      random inputs (outputs of the reference build).
