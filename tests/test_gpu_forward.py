@@ -136,6 +136,28 @@ def run_against_oracle(cuda, cfg, w, steps):
 STEPS = ((0, 6), (6, 1), (7, 1), (8, 3), (11, 4))
 
 
+def test_v27_shape_against_oracle(cuda, decode_path):
+    """The bench model's attention shape -- 12 query / 4 KV heads of 128 (a
+    group of 3), 4 experts top-2, cut to 2 layers: the 100-token prefill on
+    the fp32 block attention and the GEMMs, one-token steps on the
+    one-launch step (or the per-layer launches), 3-token steps and a second
+    prefill chunk on the per-layer kernels, against the float64 oracle."""
+    cfg = dict(FM.CONFIGS["moe"], n_layers=2, d_model=1536, n_heads=12, n_kv_heads=4,
+               d_ff=512, n_experts=4, n_activated=2)
+    w = FM.weights(cfg, 2718)
+    f = tgkv.Forward(cuda, fwd_config(cfg), w)
+    o = fwd_oracle.Forward(cfg, w)
+    rng = np.random.default_rng(27)
+    ids = rng.integers(0, cfg["vocab"], 200).astype(np.int32)
+    try:
+        for pos, n in ((0, 100), (100, 1), (101, 1), (102, 3), (105, 40), (145, 1)):
+            e = rel(f.forward("s", ids[pos:pos + n], pos), o.forward("s", ids[pos:pos + n], pos))
+            assert e < FWD_TOL, (pos, n, e)
+    finally:
+        f.close()
+    assert cuda.tg_cuda_kv_device_error() == 0
+
+
 def test_router_ties_follow_the_engine(cuda, decode_path):
     """Equal router logits: the engine's top-k takes the lowest expert index
     among equals, never one already chosen (strict greater from -1e30,
