@@ -191,6 +191,22 @@ __device__ __forceinline__ Chunk decode_chunk(const TGKvAttnParams& p, uint32_t 
 __device__ __forceinline__ void gather_store(const TGKvAttnParams& p, uint64_t idx, float v) {
     for (uint32_t r = 0; r < p.gather_world; ++r) p.gather_out[r][p.gather_base + idx] = v;
 }
+// Four consecutive finished elements (idx a multiple of 4) to every rank's
+// buffer: one 16-byte store per rank where the destination is 16-byte
+// aligned, so that a warp's stores cross NVLink as whole 128-byte lines.
+__device__ __forceinline__ void gather_store4(const TGKvAttnParams& p, uint64_t idx, float4 v) {
+    for (uint32_t r = 0; r < p.gather_world; ++r) {
+        float* d = p.gather_out[r] + p.gather_base + idx;
+        if ((reinterpret_cast<uintptr_t>(d) & 15) == 0) {
+            *reinterpret_cast<float4*>(d) = v;
+        } else {
+            d[0] = v.x;
+            d[1] = v.y;
+            d[2] = v.z;
+            d[3] = v.w;
+        }
+    }
+}
 
 // After the CTA's 128 consumer threads stored a segment's outputs to every
 // rank: system fence per thread, then one arrival per rank.
@@ -336,10 +352,8 @@ __device__ __noinline__ void combine_segment(const TGKvAttnParams& p, uint32_t f
                                 any ? acc.z / L : 0.f, any ? acc.w / L : 0.f};
             const uint64_t base = row + (uint64_t)(head0 + h) * HD + (v * 4) % HD;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                p.out[base + k] = o[k];
-                if (p.gather_world) gather_store(p, base + k, o[k]);
-            }
+            for (int k = 0; k < 4; ++k) p.out[base + k] = o[k];
+            if (p.gather_world) gather_store4(p, base, make_float4(o[0], o[1], o[2], o[3]));
         }
     }
     if (out_slot == ~0u && p.gather_world) gather_signal(p, tid);
